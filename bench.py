@@ -1,0 +1,469 @@
+"""Benchmark of the B200 hot path; prints ONE JSON line (rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload NAME]
+    (N > 1: launched as `python -m torch.distributed.run --nproc-per-node N ... bench.py --gpus N ...`)
+
+Default workload (BASELINE config 3 at T = 8192, the headline "qk-norm+RoPE+KV-write GB/s at T=8192"): the fused
+q/k RMSNorm + RoPE + paged KV write at the Qwen3-8B attention shape (32 q / 8 kv heads, head_dim 128, qkv bf16
+[T, 6144] ~ N(0,1), cache [1024, 256, 8, 128], positions in [0, 32768), theta 1e6, 5 % of slots -1).
+Multi-GPU: sharded by KV head as nano-vllm's tensor parallelism lays it out (rank r owns kv heads
+[r*8/N, (r+1)*8/N) and the q heads sharing them, and that slice of the cache); no collective on the data path.
+Weak scaling: the batch is 8192 * N tokens, so each rank moves the same bytes as the one-GPU run.
+
+A step is one kernel launch over one batch. Between steps an L2 flush (a 256 MiB write) runs outside the timed
+events; `value` = all ranks' algorithmic bytes / max over ranks of the summed CUDA-event kernel times.
+`e2e` = the same metric through the public Python API (nanovllm_b200.kernels.qk_norm_rope_kv) with the step's
+inputs (qkv, positions, slots) copied from pinned host memory and q_out copied back inside the timed region.
+`cpu_baseline` / `--impl reference`: the reference's torch implementation restated in oracle/ (bitwise equal to
+it, tests/test_oracle.py), run on the host cores in bf16.
+
+Other workloads (not the driver's headline): fused06b (config 1 shape at T = 8192), norm (config 2: rms_norm,
+add_rms_norm, silu_and_mul at T = 8192), matmul (config 4, bf16 M = K = N = 4096).
+"""
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "nano-vllm-triton-kernels_b200"))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+
+L2_FLUSH_BYTES = 256 << 20
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+METRIC_FUSED = "qk-norm+RoPE+KV-write GB/s (% HBM peak) at T=8192"
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", default="fused8b", choices=["fused8b", "fused06b", "norm", "matmul"])
+    ap.add_argument("--tokens", type=int, default=8192, help="tokens per step at N = 1")
+    ap.add_argument("--scaling", choices=["weak", "strong"], default="weak")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            return json.load(f), "measured"
+    return FALLBACK_PEAKS, "fallback"
+
+
+def load_traffic(key):
+    """ncu DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) recorded under profiles/."""
+    path = os.path.join(ROOT, "profiles", "ncu_traffic.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            return json.load(f).get(key)
+    return None
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# Distributed plumbing (one process per GPU, NCCL, 127.0.0.1 rendezvous).
+
+def setup_dist(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if args.gpus > 1 and world == 1:
+        # Not launched by torchrun: relaunch ourselves under it.
+        cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={args.gpus}",
+               "--master-addr", "127.0.0.1", "--master-port", os.environ.get("MASTER_PORT", "29531"),
+               *sys.argv]
+        sys.exit(subprocess.call(cmd))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        torch.cuda.set_device(local)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    torch.distributed.all_reduce(t)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# Clocks during the timed region.
+
+class ClockSampler:
+    """nvidia-smi samples (every 20 ms) of the SM clock and throttle reasons; summary() keeps those taken between
+    mark_start() and mark_end(), i.e. during the timed region."""
+    QUERY = ("timestamp,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+        self.t0 = self.t1 = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
+                                          "--format=csv,noheader,nounits", "-lms", "20"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            time.sleep(0.3)
+        except OSError:
+            self.proc = None
+        return self
+
+    def mark_start(self):
+        self.t0 = datetime.datetime.now()
+
+    def mark_end(self):
+        self.t1 = datetime.datetime.now()
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.1)
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self):
+        rows = []
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                ts = datetime.datetime.strptime(f[0], "%Y/%m/%d %H:%M:%S.%f")
+                rows.append((ts, float(f[1]), float(f[2]), f[5:9]))
+            except ValueError:
+                continue
+        inside = [r for r in rows if self.t0 and self.t1 and self.t0 <= r[0] <= self.t1]
+        use = inside or rows
+        if not use:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        reasons = sorted({n for r in use for n, v in zip(names, r[3]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(r[1] for r in use), "sm_max_mhz": max(r[2] for r in use),
+                "reasons": reasons, "samples": len(use), "samples_in_timed_region": len(inside)}
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# Workloads: each returns a dict with `launch()` (one step on device-resident inputs, on the current stream),
+# `units` (algorithmic bytes or flops per step on this rank), `e2e()` (one step through the public API from pinned
+# host buffers, returns (h2d_bytes, d2h_bytes)), `cpu()` (one step of the oracle on CPU) and metadata.
+
+def fused_workload(args, rank, world, dev, hq_total, hkv_total, max_pos, num_blocks, label):
+    from nanovllm_b200 import workloads
+    from nanovllm_b200.kernels.qk_norm_rope_kv import qk_norm_rope_kv
+
+    T = args.tokens * (world if args.scaling == "weak" else 1)
+    assert hkv_total % world == 0, "kv heads must divide across the GPUs"
+    hq, hkv, d = hq_total // world, hkv_total // world, 128
+    # Each rank generates only its shard: its qkv_proj output [T, (hq + 2 hkv) * d] and cache slice.
+    blocks = max(num_blocks, (T + 255) // 256 + 1)
+    x = workloads.fused_inputs(T, hq, hkv, d, max_pos=max_pos, theta=1e6, num_blocks=blocks, seed=1234,
+                               device=dev)
+    # positions and slots are replicated across ranks: regenerate them from a rank-independent seed.
+    g = torch.Generator(device=dev).manual_seed(99)
+    x["positions"] = torch.randint(0, max_pos, (T,), device=dev, generator=g)
+    slots = torch.randperm(blocks * 256, device=dev, generator=g)[:T].to(torch.int32)
+    slots[torch.randperm(T, device=dev, generator=g)[:round(0.05 * T)]] = -1
+    x["slots"] = slots
+    bytes_per_step = T * ((hq + 2 * hkv) * d * 2 * 2 + 8 + 4 + d * 4) + 2 * d * 2
+
+    def launch():
+        qk_norm_rope_kv(x["q"], x["k"], x["v"], x["positions"], x["q_w"], x["k_w"], x["eps"], x["cos_sin"],
+                        x["k_cache"], x["v_cache"], x["slots"], False)
+
+    host = {}
+
+    def e2e():
+        if not host:  # pinned host copies of the step's inputs, and the device buffers they are copied into
+            host.update(qkv=x["qkv"].cpu().pin_memory(), positions=x["positions"].cpu().pin_memory(),
+                        slots=x["slots"].cpu().pin_memory(),
+                        q_out=torch.empty(T, hq, d, dtype=torch.bfloat16).pin_memory(),
+                        dqkv=torch.empty_like(x["qkv"]), dpos=torch.empty_like(x["positions"]),
+                        dslots=torch.empty_like(x["slots"]))
+        dqkv, dpos, dslots = host["dqkv"], host["dpos"], host["dslots"]
+        dqkv.copy_(host["qkv"], non_blocking=True)
+        dpos.copy_(host["positions"], non_blocking=True)
+        dslots.copy_(host["slots"], non_blocking=True)
+        q, k, v = dqkv.split([hq * d, hkv * d, hkv * d], dim=-1)
+        q_out, _ = qk_norm_rope_kv(q.view(T, hq, d), k.view(T, hkv, d), v.view(T, hkv, d), dpos, x["q_w"],
+                                   x["k_w"], x["eps"], x["cos_sin"], x["k_cache"], x["v_cache"], dslots, False)
+        host["q_out"].copy_(q_out, non_blocking=True)
+        h2d = host["qkv"].numel() * 2 + host["positions"].numel() * 8 + host["slots"].numel() * 4
+        return h2d, host["q_out"].numel() * 2
+
+    cpu_state = {}
+
+    def cpu(tokens=T):
+        """The oracle on the host over the first `tokens` tokens of the batch."""
+        from oracle import reference_math as om
+        if not cpu_state:
+            cpu_state.update({k: (v.cpu() if torch.is_tensor(v) else v) for k, v in x.items()})
+            c = cpu_state
+            q, k, v = c["qkv"].split([hq * d, hkv * d, hkv * d], dim=-1)
+            c["q"], c["k"], c["v"] = q.view(T, hq, d), k.view(T, hkv, d), v.view(T, hkv, d)
+        c = cpu_state
+        om.qk_norm_rope_kv(c["q"][:tokens], c["k"][:tokens], c["v"][:tokens], c["positions"][:tokens], c["q_w"],
+                           c["k_w"], c["eps"], c["cos_sin"], c["k_cache"], c["v_cache"], c["slots"][:tokens], False)
+        return tokens * ((hq + 2 * hkv) * d * 2 * 2 + 8 + 4 + d * 4) + 2 * d * 2
+
+    return dict(launch=launch, units=bytes_per_step, e2e=e2e, cpu=cpu, unit="GB/s", scale=1e9, bound="hbm",
+                metric=METRIC_FUSED, dtype="bf16", launches_per_step=1,
+                traffic_key=label,
+                config={"workload": label, "tokens_per_step": T, "tokens_per_gpu_step_at_n1": args.tokens,
+                        "q_heads": hq_total, "kv_heads": hkv_total, "head_dim": d,
+                        "kv_heads_per_gpu": hkv, "cache_blocks": blocks, "block_size": 256,
+                        "max_position": max_pos, "skip_fraction": 0.05, "write_k": False,
+                        "parallelism": f"tp{world} (KV-head sharding, no collective)",
+                        "l2": "flushed between timed steps (256 MiB write outside the events)",
+                        "bytes_formula": "T*((Hq+2Hkv)*D*2 read + 8 + 4 + D*4 + (Hq+2Hkv)*D*2 written) + 2*D*2"})
+
+
+def norm_workload(args, rank, world, dev):
+    from nanovllm_b200 import workloads
+    from nanovllm_b200.kernels.rms_norm import fused_add_rms_norm, rms_norm
+    from nanovllm_b200.kernels.swiglu import silu_and_mul
+    T = args.tokens * (world if args.scaling == "weak" else 1)
+    n, inter = 1024, 3072
+    x = workloads.norm_inputs(T, n, seed=5, device=dev)
+    gu = workloads.silu_inputs(T, inter, seed=6, device=dev)["x"]
+    units = (2 * T * n + n) * 2 + (4 * T * n + n) * 2 + 3 * T * inter * 2
+
+    def launch():
+        rms_norm(x["x"], x["w"], x["eps"])
+        fused_add_rms_norm(x["x"], x["residual"], x["w"], x["eps"])
+        silu_and_mul(gu)
+
+    xc = {}
+
+    def cpu(tokens=T):
+        from oracle import reference_math as om
+        if not xc:
+            xc.update({k: (v.cpu() if torch.is_tensor(v) else v) for k, v in x.items()}, gu=gu.cpu())
+        om.rms_forward(xc["x"][:tokens], xc["w"], xc["eps"])
+        om.add_rms_forward(xc["x"][:tokens], xc["residual"][:tokens], xc["w"], xc["eps"])
+        om.silu_and_mul(xc["gu"][:tokens])
+        return (2 * tokens * n + n) * 2 + (4 * tokens * n + n) * 2 + 3 * tokens * inter * 2
+
+    return dict(launch=launch, units=units, e2e=None, cpu=cpu, unit="GB/s", scale=1e9, bound="hbm",
+                metric="rms_norm + add_rms_norm + silu_and_mul GB/s at T=8192", dtype="bf16", launches_per_step=3,
+                traffic_key="norm", config={"workload": "norm", "tokens_per_step": T, "hidden": n,
+                                            "intermediate": inter, "parallelism": f"replicas x{world}",
+                                            "l2": "flushed between timed steps"})
+
+
+def matmul_workload(args, rank, world, dev):
+    from nanovllm_b200 import workloads
+    from nanovllm_b200.kernels.matmul import matmul
+    M = K = N = 4096
+    n_local = N // world if args.scaling == "strong" else N
+    x = workloads.matmul_inputs(M, n_local, K, dtype=torch.bfloat16, seed=7, device=dev)
+    units = 2 * M * n_local * K
+
+    def launch():
+        matmul(x["a"], x["b"])
+
+    xc = {}
+
+    def cpu(tokens=M):
+        if not xc:
+            xc.update(a=x["a"].cpu(), b=x["b"].cpu())
+        xc["a"][:tokens] @ xc["b"]  # torch CPU bf16 matmul (fp32 accumulation) over the first `tokens` rows
+        return 2 * tokens * n_local * K
+
+    return dict(launch=launch, units=units, e2e=None, cpu=cpu, unit="TFLOP/s", scale=1e12, bound="tensor",
+                metric="matmul bf16 TFLOP/s at M=K=N=4096", dtype="bf16", launches_per_step=1, traffic_key="matmul",
+                config={"workload": "matmul", "M": M, "N": n_local, "K": K, "b_layout": "weight.t() (K-major)",
+                        "parallelism": f"column-parallel x{world}", "l2": "flushed between timed steps"})
+
+
+def make_workload(args, rank, world, dev):
+    if args.workload == "fused8b":
+        return fused_workload(args, rank, world, dev, 32, 8, 32768, 1024, "fused8b")
+    if args.workload == "fused06b":
+        return fused_workload(args, rank, world, dev, 16, 8, 4096, 64, "fused06b")
+    if args.workload == "norm":
+        return norm_workload(args, rank, world, dev)
+    return matmul_workload(args, rank, world, dev)
+
+
+# ---------------------------------------------------------------------------------------------------------------
+
+def time_cpu(fn, budget_s=10.0, max_reps=30):
+    """Median seconds of fn() on the host cores after one warm-up, repeated until ~budget_s."""
+    fn()
+    times = []
+    start = time.perf_counter()
+    while len(times) < max_reps and (len(times) < 3 or time.perf_counter() - start < budget_s):
+        t0 = time.perf_counter()
+        fn()
+        times.append(time.perf_counter() - t0)
+    return statistics.median(times), len(times)
+
+
+def run_reference_arm(args, rank, world):
+    """`--impl reference`: the reference's CPU implementation (the oracle port) on the host cores. Each step runs on
+    a prefix of the one-GPU batch sized so that warm-up + steps take about two minutes."""
+    if rank != 0:
+        return
+    torch.set_num_threads(os.cpu_count() or 1)
+    wargs = argparse.Namespace(**vars(args))
+    wargs.scaling = "strong"  # one host: the one-GPU job
+    dev = torch.device("cuda") if torch.cuda.is_available() else torch.device("cpu")
+    wl = make_workload(wargs, 0, 1, dev)
+    full = wl["config"].get("tokens_per_step", wl["config"].get("M"))
+    with torch.inference_mode():
+        t0 = time.perf_counter()
+        wl["cpu"]()
+        t_full = time.perf_counter() - t0
+        per_step = 120.0 / (args.steps + args.warmup)
+        tokens = max(1, min(full, int(full * per_step / max(t_full, 1e-9))))
+        for _ in range(args.warmup):
+            wl["cpu"](tokens)
+        total, units = 0.0, 0
+        for _ in range(args.steps):
+            t0 = time.perf_counter()
+            units += wl["cpu"](tokens)
+            total += time.perf_counter() - t0
+    value = units / total / wl["scale"]
+    sample = (f"first {tokens} of the {full} rows/tokens of the one-GPU step ({wl['config']['workload']}) per step, "
+              f"torch CPU bf16 eager restatement of the reference")
+    line = {"metric": wl["metric"], "value": value, "unit": wl["unit"], "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1e3 * total / args.steps, "higher_is_better": True,
+            "scaling": args.scaling, "vs_baseline": None, "dtype": wl["dtype"], "data": "synthetic",
+            "config": wl["config"], "impl": "reference",
+            "cpu_baseline": {"value": value, "unit": wl["unit"], "cores": torch.get_num_threads(), "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": value, "unit": wl["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse_args()
+    rank, world, local = setup_dist(args)
+    if args.impl == "reference":
+        run_reference_arm(args, rank, world)
+        if world > 1:
+            torch.distributed.destroy_process_group()
+        return
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py needs a CUDA device (the kernels have no CPU path)")
+    dev = torch.device("cuda", local)
+    torch.backends.cuda.matmul.allow_tf32 = False
+    peaks, peak_kind = load_peaks()
+    wl = make_workload(args, rank, world, dev)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    with torch.inference_mode():
+        for _ in range(args.warmup):
+            flush.zero_()
+            wl["launch"]()
+        torch.cuda.synchronize()
+        starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        barrier(world)
+        with ClockSampler(local) as clocks:
+            clocks.mark_start()
+            for i in range(args.steps):
+                flush.zero_()
+                starts[i].record(stream)
+                wl["launch"]()
+                ends[i].record(stream)
+            barrier(world)
+            clocks.mark_end()
+        per_step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+        local_s = sum(per_step_ms) / 1e3
+        total_s = max_over_ranks(local_s, world)
+        all_units = sum_over_ranks(float(wl["units"]) * args.steps, world)
+        value = all_units / total_s / wl["scale"]
+        achieved = wl["units"] / (local_s / args.steps) / wl["scale"]  # this rank's kernel, per launch
+
+        e2e = None
+        if wl["e2e"] is not None and not args.no_e2e:
+            for _ in range(max(2, args.warmup // 2)):
+                wl["e2e"]()
+            torch.cuda.synchronize()
+            barrier(world)
+            e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e_start.record(stream)
+            for _ in range(args.steps):
+                h2d, d2h = wl["e2e"]()
+            e_end.record(stream)
+            torch.cuda.synchronize()
+            e_s = max_over_ranks(e_start.elapsed_time(e_end) / 1e3, world)
+            e2e = {"value": all_units / e_s / wl["scale"], "unit": wl["unit"], "h2d_bytes_per_step": h2d,
+                   "d2h_bytes_per_step": d2h,
+                   "path": "nanovllm_b200.kernels.qk_norm_rope_kv (public API) with pinned host inputs/outputs"}
+
+    if wl["bound"] == "hbm":
+        peak = peaks["hbm_gbs"]
+        roof_unit = "GB/s"
+    else:
+        peak = peaks["bf16_tflops"]
+        roof_unit = "TFLOP/s"
+    traffic = load_traffic(wl["traffic_key"])
+    line = {"metric": wl["metric"], "value": value, "unit": wl["unit"], "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1e3 * total_s / args.steps, "higher_is_better": True,
+            "scaling": args.scaling, "vs_baseline": None, "dtype": wl["dtype"],
+            "data": "synthetic (seeded, BASELINE config shapes and distributions)", "config": wl["config"],
+            "roofline": {"bound": wl["bound"], "achieved": achieved, "peak": peak, "unit": roof_unit,
+                         "frac": achieved / peak, "peak_source": f"{peak_kind} (MEASURED_PEAKS.json)"
+                         if peak_kind == "measured" else "fallback", "traffic": traffic,
+                         "frac_of_nominal_8tbs": achieved / 8000.0 if wl["bound"] == "hbm" else None},
+            "clocks": clocks.summary(), "gpu_launches": args.steps * wl["launches_per_step"],
+            "gpu_launches_scope": "rank 0, timed region"}
+    if e2e is not None:
+        line["e2e"] = e2e
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        torch.set_num_threads(os.cpu_count() or 1)
+        with torch.inference_mode():
+            secs, reps = time_cpu(wl["cpu"])
+        line["cpu_baseline"] = {"value": wl["units"] / secs / wl["scale"], "unit": wl["unit"],
+                                "cores": torch.get_num_threads(), "kind": "port",
+                                "sample": f"the full step on the host (torch CPU bf16 restatement of the reference), "
+                                          f"median of {reps} runs"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,132 @@
+/* nvb200.h — C ABI of the B200 (sm_100a) kernels behind nanovllm_b200.
+ *
+ * Every entry point takes plain device pointers, element strides and sizes, launches on the given CUDA
+ * stream, never synchronises, never allocates and never reads device data on the host, so each call can be
+ * captured in a CUDA graph. The return value is NVB200_OK or an NVB200_ERR_* code; no C++ exception crosses
+ * this boundary. Strides are in ELEMENTS (as torch's Tensor.stride()), sizes in elements.
+ *
+ * The Python functions that mirror the reference's nanovllm/kernels API (nanovllm_b200.kernels.*) validate
+ * their torch arguments exactly as the reference's wrappers do, allocate the outputs with torch, and then call
+ * these functions through ctypes. A C, C++ or Python/ctypes caller can call them directly.
+ */
+#ifndef NVB200_H
+#define NVB200_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define NVB200_API __attribute__((visibility("default")))
+#else
+#define NVB200_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same type as cudaStream_t; NULL is the legacy default stream. */
+typedef struct CUstream_st *nvb200_stream_t;
+
+enum {
+  NVB200_OK = 0,
+  NVB200_ERR_ARG = 1,         /* a size, stride, pointer or dtype that the op does not accept */
+  NVB200_ERR_UNSUPPORTED = 2, /* a valid request that this build has no kernel for (e.g. head_dim > 512) */
+  NVB200_ERR_CUDA = 3,        /* a CUDA runtime call or the launch itself failed (cudaGetLastError) */
+  NVB200_ERR_NO_DEVICE = 4    /* the current device is not sm_100 */
+};
+
+/* Element types. */
+enum { NVB200_BF16 = 0, NVB200_F16 = 1, NVB200_F32 = 2 };
+
+/* Bits an entry point may OR into its optional device status word (int32, zero it to clear). The kernels
+ * never trap: an index they cannot honour is skipped and reported here. */
+enum {
+  NVB200_STATUS_BAD_POSITION = 1, /* positions[t] outside [0, num_positions): cos/sin row 0 used instead  */
+  NVB200_STATUS_BAD_SLOT = 2,     /* slot_mapping[t] outside [-1, num_slots): the k/v rows are not stored */
+  NVB200_STATUS_WAIT_TIMEOUT = 4  /* an mbarrier wait ran past its bound; the CTA stopped early            */
+};
+
+/* Human-readable name of an NVB200_* return code. */
+NVB200_API const char *nvb200_status_string(int code);
+
+/* Fused per-head q/k RMSNorm + neox RoPE + paged KV-cache write.
+ * Replaces: nanovllm/kernels/qk_norm_rope_kv.py:92-125 (qk_norm_rope_kv) and its Triton kernel :45-82.
+ *
+ *   q [T, Hq, D], k, v [T, Hkv, D] bf16, each head contiguous (stride(2) == 1, stride(1) == D), any token stride.
+ *   positions [T] int64; cos_sin fp32 rows of D (cos | sin), row r at cos_sin + r * cos_sin_stride.
+ *   q_weight, k_weight [D] bf16.
+ *   k_cache, v_cache: contiguous [num_slots, Hkv, D] bf16 (a [blocks, block_size, Hkv, D] cache), or both NULL:
+ *     then nothing is stored and slot_mapping may be NULL. slot_mapping [T] int32, -1 = do not store.
+ *   q_out [T, Hq, D] contiguous bf16 (written), k_out [T, Hkv, D] contiguous bf16 or NULL (normed+rotated k).
+ *   status: optional int32 device word for NVB200_STATUS_* bits, may be NULL.
+ * Numerics: n = bf16(bf16(x * rsqrt(mean(x^2) + eps)) * w) per head in fp32; y1 = n1*cos - n2*sin,
+ * y2 = n2*cos + n1*sin with separately rounded fp32 products (no FMA), rounded to bf16. v is stored raw. */
+typedef struct nvb200_qk_norm_rope_kv_args {
+  void *q_out;
+  void *k_out;
+  const void *q;
+  const void *k;
+  const void *v;
+  int64_t q_token_stride;
+  int64_t k_token_stride;
+  int64_t v_token_stride;
+  const int64_t *positions;
+  const int32_t *slot_mapping;
+  const void *q_weight;
+  const void *k_weight;
+  const float *cos_sin;
+  int64_t cos_sin_stride;
+  int64_t num_positions;
+  void *k_cache;
+  void *v_cache;
+  int64_t num_slots;
+  int64_t num_tokens;
+  int32_t num_q_heads;
+  int32_t num_kv_heads;
+  int32_t head_dim;
+  float eps;
+  int32_t *status;
+} nvb200_qk_norm_rope_kv_args;
+
+NVB200_API int nvb200_qk_norm_rope_kv(const nvb200_qk_norm_rope_kv_args *args, nvb200_stream_t stream);
+
+/* RMSNorm over the last dim, y contiguous [groups * rows_per_group, n].
+ * Replaces: nanovllm/kernels/rms_norm.py:83-98 (rms_norm) and _rms_norm_kernel :34-54.
+ * Row g * rows_per_group + r of x starts at x + g * group_stride + r * row_stride (a 2-D [rows, n] view is
+ * groups = rows, rows_per_group = 1; a 3-D [T, H, n] view is groups = T, rows_per_group = H). Unit last stride.
+ * y = (x.float() * rsqrt(mean(x.float()^2) + eps)).to(dtype) * w, the product in dtype. */
+NVB200_API int nvb200_rms_norm(void *y, const void *x, const void *w, int64_t groups, int64_t rows_per_group,
+                    int64_t group_stride, int64_t row_stride, int64_t n, float eps, int dtype,
+                    nvb200_stream_t stream);
+
+/* s = x + residual in fp32; residual_out = s.to(dtype); y = RMSNorm of the unrounded s. y, residual_out
+ * contiguous [rows, n]; x and residual have unit last stride and any row stride.
+ * Replaces: nanovllm/kernels/rms_norm.py:101-111 (fused_add_rms_norm) and _fused_add_rms_norm_kernel :57-80. */
+NVB200_API int nvb200_fused_add_rms_norm(void *y, void *residual_out, const void *x, const void *residual, const void *w,
+                              int64_t rows, int64_t n, int64_t x_row_stride, int64_t residual_row_stride,
+                              float eps, int dtype, nvb200_stream_t stream);
+
+/* out[r, :] = silu(x[r, :n].float()).to(dtype) * x[r, n:2n]; out contiguous [rows, n]; x unit last stride.
+ * Replaces: nanovllm/kernels/swiglu.py:34-43 (silu_and_mul) and _silu_and_mul_kernel :19-31. */
+NVB200_API int nvb200_silu_and_mul(void *out, const void *x, int64_t rows, int64_t n, int64_t x_row_stride, int dtype,
+                        nvb200_stream_t stream);
+
+/* C[M, N] = A[M, K] @ B[K, N] with fp32 accumulation, C in the inputs' dtype (bf16 or fp32).
+ * Replaces: nanovllm/kernels/matmul.py:84-99 (matmul) and _matmul_kernel :33-81.
+ * Any strides for A and B (B is typically weight.t(), strides (1, K)); C any strides.
+ * dtype: NVB200_BF16 (tcgen05 kind::f16) or NVB200_F32 with tf32 = 1 (tcgen05 kind::tf32, inputs rounded to
+ * tf32) or tf32 = 0 ("ieee": fp32 FMA on the CUDA cores).
+ * workspace: device scratch of workspace_bytes (16-byte aligned) used when an operand's layout cannot be read
+ * by TMA and must be packed first; nvb200_matmul_workspace_size() tells how much a call needs (0 for the
+ * usual layouts), and a call given less returns NVB200_ERR_ARG. */
+NVB200_API int64_t nvb200_matmul_workspace_size(int64_t M, int64_t N, int64_t K, int64_t sam, int64_t sak, int64_t sbk,
+                                     int64_t sbn, int dtype);
+NVB200_API int nvb200_matmul(void *c, const void *a, const void *b, int64_t M, int64_t N, int64_t K, int64_t sam,
+                  int64_t sak, int64_t sbk, int64_t sbn, int64_t scm, int64_t scn, int dtype, int tf32,
+                  void *workspace, int64_t workspace_bytes, int32_t *status, nvb200_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NVB200_H */

@@ -1,0 +1,197 @@
+// Shared device helpers for the sm_100a kernels: bf16 rounding, packed 16-byte vectors, mbarriers with bounded
+// waits, and the 1-D bulk-copy (cp.async.bulk) engine that moves token tiles between HBM and shared memory.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "nvb200.h"
+
+#define NVB200_DEVICE __device__ __forceinline__
+
+namespace nvb200 {
+
+// ---------------------------------------------------------------------------------------------------------------
+// Numeric helpers. All rounding is round-to-nearest-even, as torch's .to(bfloat16) / .to(float16).
+
+template <typename T> struct Elem;
+template <> struct Elem<__nv_bfloat16> {
+  static NVB200_DEVICE float to_f(__nv_bfloat16 x) { return __bfloat162float(x); }
+  static NVB200_DEVICE __nv_bfloat16 from_f(float x) { return __float2bfloat16_rn(x); }
+};
+template <> struct Elem<__half> {
+  static NVB200_DEVICE float to_f(__half x) { return __half2float(x); }
+  static NVB200_DEVICE __half from_f(float x) { return __float2half_rn(x); }
+};
+template <> struct Elem<float> {
+  static NVB200_DEVICE float to_f(float x) { return x; }
+  static NVB200_DEVICE float from_f(float x) { return x; }
+};
+
+// Round an fp32 value to T and back (the value torch holds after .to(T)).
+template <typename T> NVB200_DEVICE float round_to(float x) { return Elem<T>::to_f(Elem<T>::from_f(x)); }
+
+// 16 bytes as 8 bf16, for vectorised global and shared-memory access. Element 2i is the low half of word i.
+union Pack8 {
+  uint4 u;
+  __nv_bfloat162 h2[4];
+  __nv_bfloat16 h[8];
+};
+
+// Two bf16 in one 32-bit word -> fp32 (exact: a bf16 is the top half of an fp32).
+NVB200_DEVICE float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
+NVB200_DEVICE float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+
+// Rounds lo and hi to bf16 (round to nearest even) and packs them, lo in the low half.
+NVB200_DEVICE uint32_t pack_bf16x2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+NVB200_DEVICE void unpack8(const uint4 &u, float (&f)[8]) {
+  f[0] = bf16_lo(u.x), f[1] = bf16_hi(u.x), f[2] = bf16_lo(u.y), f[3] = bf16_hi(u.y);
+  f[4] = bf16_lo(u.z), f[5] = bf16_hi(u.z), f[6] = bf16_lo(u.w), f[7] = bf16_hi(u.w);
+}
+
+NVB200_DEVICE uint4 pack8(const float (&f)[8]) {
+  return make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]), pack_bf16x2(f[4], f[5]),
+                    pack_bf16x2(f[6], f[7]));
+}
+
+// Product of two bf16x2 words, each lane rounded once to bf16 (the exact product of two bf16 fits fp32, so this
+// equals torch's bf16 multiply: fp32 product rounded to bf16).
+NVB200_DEVICE uint32_t bf16x2_mul(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Shared-memory addresses and vector access.
+
+NVB200_DEVICE uint32_t smem_addr(const void *p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+
+NVB200_DEVICE uint4 ld_shared_v4(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+  return v;
+}
+
+NVB200_DEVICE float4 ld_shared_f4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));
+  return v;
+}
+
+NVB200_DEVICE void st_shared_v4(uint32_t addr, const uint4 &v) {
+  asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// mbarrier (shared-memory transaction barrier).
+
+NVB200_DEVICE void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+// Makes the initialised barriers visible to the async proxy (the bulk-copy engine) before first use.
+NVB200_DEVICE void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+
+NVB200_DEVICE void mbar_arrive(uint32_t bar) {
+  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(bar) : "memory");
+}
+
+NVB200_DEVICE void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(bar),
+               "r"(bytes)
+               : "memory");
+}
+
+NVB200_DEVICE bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+NVB200_DEVICE uint64_t global_timer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Upper bound of any single wait in these kernels. A healthy wait lasts microseconds; one second means the
+// awaited copy or arrival will never come, and the kernel gives up instead of hanging the GPU.
+constexpr uint64_t kWaitLimitNs = 1000000000ull;
+
+// Waits for the phase of `bar` with the given parity to complete. Returns false if it has not after
+// kWaitLimitNs: the caller then records NVB200_STATUS_WAIT_TIMEOUT and winds its CTA down.
+NVB200_DEVICE bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t start = global_timer_ns();
+  for (uint32_t spin = 1;; ++spin) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((spin & 255u) == 0 && global_timer_ns() - start > kWaitLimitNs) return false;
+  }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// 1-D bulk copies (cp.async.bulk). Both addresses 16-byte aligned, size a multiple of 16 bytes.
+
+// Global -> shared, completion counted on `bar` as transaction bytes.
+NVB200_DEVICE void bulk_g2s(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+      "l"(src), "r"(bytes), "r"(bar)
+      : "memory");
+}
+
+// Shared -> global, tracked in the issuing thread's bulk group.
+NVB200_DEVICE void bulk_s2g(void *dst, uint32_t src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(src), "r"(bytes)
+               : "memory");
+}
+
+NVB200_DEVICE void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+
+// Waits until all but the N most recent bulk groups of this thread have finished READING shared memory.
+template <int N> NVB200_DEVICE void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+
+// Waits until all but the N most recent bulk groups of this thread are complete (writes visible).
+template <int N> NVB200_DEVICE void bulk_wait() { asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory"); }
+
+// Orders this thread's generic-proxy shared-memory writes before later async-proxy (bulk copy) reads.
+NVB200_DEVICE void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+NVB200_DEVICE void set_status(int32_t *status, int32_t bits) {
+  if (status != nullptr) atomicOr(status, bits);
+}
+
+}  // namespace nvb200
+
+// ---------------------------------------------------------------------------------------------------------------
+// Host helpers shared by the entry points.
+
+namespace nvb200 {
+
+// Streaming multiprocessors of the current device (cached per device; 148 on B200).
+int sm_count();
+
+// Returns NVB200_OK if the current device is sm_100 (B200/GB200), else NVB200_ERR_NO_DEVICE.
+int check_device();
+
+inline int launch_status() { return cudaGetLastError() == cudaSuccess ? NVB200_OK : NVB200_ERR_CUDA; }
+
+inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace nvb200

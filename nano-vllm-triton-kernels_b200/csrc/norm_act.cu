@@ -1,0 +1,301 @@
+// RMSNorm, Add+RMSNorm and SiLU x Mul on strided row views, for sm_100a.
+//
+// Behaviour follows nanovllm/kernels/rms_norm.py:34-80 and nanovllm/kernels/swiglu.py:19-31, whose numerics are the
+// torch code of nanovllm/layers/layernorm.py:20-44 and nanovllm/layers/activation.py:15-18:
+//   rms_norm      y = T(T(x.float() * rsqrt(mean(x.float()^2) + eps)) * w)
+//   add_rms_norm  s = x.float() + r.float(); residual_out = T(s); y = rms_norm of the unrounded s
+//   silu_and_mul  out = T(T(silu(gate.float())) * up)
+// where T(.) rounds to the tensor dtype (bf16, fp16 or fp32) and the product of two bf16/fp16 values is exact in
+// fp32, so T(a * b) equals torch's dtype multiply.
+//
+// These ops are HBM-bound (bytes per row: rms 2n, add_rms 4n, silu 3n elements). Rows of up to 2048 bf16 elements
+// (1024 fp32) live in registers: a group of L lanes (L a power of two <= 32) owns a row, each lane moves 16-byte
+// vectors, so a warp keeps 4-8 independent 16-byte loads in flight per lane and the sum of squares takes log2(L)
+// shuffles. Longer rows use one CTA per row with a second pass over the row (served from L2).
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace nvb200 {
+namespace {
+
+constexpr int kRowThreads = 256;
+constexpr int kMaxVecPerLane = 8;
+
+// VEC consecutive elements of type T as fp32.
+template <typename T, int VEC> struct VecIO;
+template <> struct VecIO<__nv_bfloat16, 8> {
+  static NVB200_DEVICE void load(const __nv_bfloat16 *p, float (&f)[8]) {
+    unpack8(*reinterpret_cast<const uint4 *>(p), f);
+  }
+  static NVB200_DEVICE void store(__nv_bfloat16 *p, const float (&f)[8]) { *reinterpret_cast<uint4 *>(p) = pack8(f); }
+};
+template <> struct VecIO<__half, 8> {
+  static NVB200_DEVICE void load(const __half *p, float (&f)[8]) {
+    union { uint4 u; __half2 h[4]; } v;
+    v.u = *reinterpret_cast<const uint4 *>(p);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 t = __half22float2(v.h[i]);
+      f[2 * i] = t.x;
+      f[2 * i + 1] = t.y;
+    }
+  }
+  static NVB200_DEVICE void store(__half *p, const float (&f)[8]) {
+    union { uint4 u; __half2 h[4]; } v;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v.h[i] = __floats2half2_rn(f[2 * i], f[2 * i + 1]);
+    *reinterpret_cast<uint4 *>(p) = v.u;
+  }
+};
+template <> struct VecIO<float, 4> {
+  static NVB200_DEVICE void load(const float *p, float (&f)[4]) {
+    const float4 v = *reinterpret_cast<const float4 *>(p);
+    f[0] = v.x, f[1] = v.y, f[2] = v.z, f[3] = v.w;
+  }
+  static NVB200_DEVICE void store(float *p, const float (&f)[4]) {
+    *reinterpret_cast<float4 *>(p) = make_float4(f[0], f[1], f[2], f[3]);
+  }
+};
+template <typename T> struct VecIO<T, 1> {
+  static NVB200_DEVICE void load(const T *p, float (&f)[1]) { f[0] = Elem<T>::to_f(*p); }
+  static NVB200_DEVICE void store(T *p, const float (&f)[1]) { *p = Elem<T>::from_f(f[0]); }
+};
+
+struct RowArgs {
+  void *y;
+  void *res_out;
+  const void *x;
+  const void *r;
+  const void *w;
+  int64_t rows;
+  int64_t rows_per_group;  // rms_norm 3-D views; 1 otherwise
+  int64_t x_group_stride, x_row_stride, r_row_stride;
+  int n;
+  int lanes;  // L: lanes per row (register kernel)
+  float eps;
+};
+
+// y = T(T(v * rstd) * w): v * rstd rounded to fp32 then to T, times w in fp32 (exact for 16-bit T), rounded.
+template <typename T> NVB200_DEVICE float norm_out(float v, float rstd, float w) {
+  return __fmul_rn(round_to<T>(__fmul_rn(v, rstd)), w);
+}
+
+template <typename T, int VEC, bool ADD>
+__global__ void __launch_bounds__(kRowThreads) row_norm_kernel(const __grid_constant__ RowArgs a) {
+  const int L = a.lanes;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * (kRowThreads / L) + threadIdx.x / L;
+  const int li = threadIdx.x % L;
+  const bool live = row < a.rows;
+  const T *x = static_cast<const T *>(a.x);
+  const T *r = static_cast<const T *>(a.r);
+  const T *w = static_cast<const T *>(a.w);
+  int64_t xoff = 0, roff = 0;
+  if (live) {
+    xoff = (row / a.rows_per_group) * a.x_group_stride + (row % a.rows_per_group) * a.x_row_stride;
+    roff = row * a.r_row_stride;
+  }
+  float v[kMaxVecPerLane][VEC];
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < kMaxVecPerLane; ++k) {
+    const int col = (k * L + li) * VEC;
+    if (live && col < a.n) {
+      VecIO<T, VEC>::load(x + xoff + col, v[k]);
+      if (ADD) {
+        float rv[VEC];
+        VecIO<T, VEC>::load(r + roff + col, rv);
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) v[k][e] = __fadd_rn(v[k][e], rv[e]);
+      }
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) ss = fmaf(v[k][e], v[k][e], ss);
+    }
+  }
+  for (int o = L / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if (!live) return;
+  const float rstd = rsqrtf(ss / static_cast<float>(a.n) + a.eps);
+  T *y = static_cast<T *>(a.y) + row * a.n;
+  T *so = ADD ? static_cast<T *>(a.res_out) + row * a.n : nullptr;
+#pragma unroll
+  for (int k = 0; k < kMaxVecPerLane; ++k) {
+    const int col = (k * L + li) * VEC;
+    if (col < a.n) {
+      float wv[VEC], out[VEC];
+      VecIO<T, VEC>::load(w + col, wv);
+      if (ADD) VecIO<T, VEC>::store(so + col, v[k]);
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) out[e] = norm_out<T>(v[k][e], rstd, wv[e]);
+      VecIO<T, VEC>::store(y + col, out);
+    }
+  }
+}
+
+// Rows longer than the register kernel holds: one CTA per row, sum of squares first, then a second pass.
+template <typename T, bool ADD>
+__global__ void __launch_bounds__(kRowThreads) long_row_norm_kernel(const __grid_constant__ RowArgs a) {
+  __shared__ float partial[kRowThreads / 32];
+  const int64_t row = blockIdx.x;
+  const T *x = static_cast<const T *>(a.x) + (row / a.rows_per_group) * a.x_group_stride +
+               (row % a.rows_per_group) * a.x_row_stride;
+  const T *r = ADD ? static_cast<const T *>(a.r) + row * a.r_row_stride : nullptr;
+  const T *w = static_cast<const T *>(a.w);
+  T *y = static_cast<T *>(a.y) + row * a.n;
+  T *so = ADD ? static_cast<T *>(a.res_out) + row * a.n : nullptr;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < a.n; i += kRowThreads) {
+    float s = Elem<T>::to_f(x[i]);
+    if (ADD) {
+      s = __fadd_rn(s, Elem<T>::to_f(r[i]));
+      so[i] = Elem<T>::from_f(s);
+    }
+    ss = fmaf(s, s, ss);
+  }
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((threadIdx.x & 31) == 0) partial[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int i = 0; i < kRowThreads / 32; ++i) tot += partial[i];
+  const float rstd = rsqrtf(tot / static_cast<float>(a.n) + a.eps);
+  for (int i = threadIdx.x; i < a.n; i += kRowThreads) {
+    float s = Elem<T>::to_f(x[i]);
+    if (ADD) s = __fadd_rn(s, Elem<T>::to_f(r[i]));
+    y[i] = Elem<T>::from_f(norm_out<T>(s, rstd, Elem<T>::to_f(w[i])));
+  }
+}
+
+template <typename T, bool ADD> int launch_norm(RowArgs &a, bool vec_ok, cudaStream_t stream) {
+  constexpr int VEC = sizeof(T) == 4 ? 4 : 8;
+  const int vec = vec_ok && a.n % VEC == 0 ? VEC : 1;
+  const int nvec = a.n / vec;
+  if (nvec > 32 * kMaxVecPerLane) {
+    if (a.rows > 0x7fffffffLL) return NVB200_ERR_UNSUPPORTED;
+    long_row_norm_kernel<T, ADD><<<static_cast<unsigned>(a.rows), kRowThreads, 0, stream>>>(a);
+    return launch_status();
+  }
+  int L = 1;
+  while (L < 32 && (L * 4 < nvec || L * kMaxVecPerLane < nvec)) L *= 2;
+  a.lanes = L;
+  const int64_t rows_per_block = kRowThreads / L;
+  const int64_t blocks = (a.rows + rows_per_block - 1) / rows_per_block;
+  if (blocks > 0x7fffffffLL) return NVB200_ERR_UNSUPPORTED;
+  if (vec == VEC)
+    row_norm_kernel<T, VEC, ADD><<<static_cast<unsigned>(blocks), kRowThreads, 0, stream>>>(a);
+  else
+    row_norm_kernel<T, 1, ADD><<<static_cast<unsigned>(blocks), kRowThreads, 0, stream>>>(a);
+  return launch_status();
+}
+
+template <bool ADD> int dispatch_norm(RowArgs &a, bool vec_ok, int dtype, cudaStream_t stream) {
+  switch (dtype) {
+    case NVB200_BF16: return launch_norm<__nv_bfloat16, ADD>(a, vec_ok, stream);
+    case NVB200_F16: return launch_norm<__half, ADD>(a, vec_ok, stream);
+    case NVB200_F32: return launch_norm<float, ADD>(a, vec_ok, stream);
+    default: return NVB200_ERR_ARG;
+  }
+}
+
+int elem_size(int dtype) { return dtype == NVB200_F32 ? 4 : 2; }
+
+// ---------------------------------------------------------------------------------------------------------------
+// SiLU x Mul: one thread per VEC outputs, grid-stride over rows * n / VEC.
+
+template <typename T> NVB200_DEVICE float silu_mul(float g, float u) {
+  // torch's silu: x / (1 + exp(-x)) in fp32, rounded to T; then T(silu * up) (exact product for 16-bit T).
+  const float sl = g / (1.0f + expf(-g));
+  return __fmul_rn(round_to<T>(sl), u);
+}
+
+template <typename T, int VEC>
+__global__ void __launch_bounds__(256) silu_and_mul_kernel(T *out, const T *x, int64_t rows, int n,
+                                                            int64_t x_row_stride) {
+  const int nv = n / VEC;
+  const int64_t total = rows * nv;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t row = i / nv;
+    const int col = static_cast<int>(i - row * nv) * VEC;
+    float g[VEC], u[VEC], o[VEC];
+    VecIO<T, VEC>::load(x + row * x_row_stride + col, g);
+    VecIO<T, VEC>::load(x + row * x_row_stride + n + col, u);
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) o[e] = silu_mul<T>(g[e], u[e]);
+    VecIO<T, VEC>::store(out + row * n + col, o);
+  }
+}
+
+template <typename T> int launch_silu(void *out, const void *x, int64_t rows, int64_t n, int64_t stride,
+                                      bool vec_ok, cudaStream_t stream) {
+  constexpr int VEC = sizeof(T) == 4 ? 4 : 8;
+  const bool vec = vec_ok && n % VEC == 0;
+  const int64_t items = rows * (vec ? n / VEC : n);
+  const int64_t want = (items + 255) / 256;
+  const int64_t cap = static_cast<int64_t>(sm_count()) * 8;  // 8 CTAs of 256 threads per SM, grid-stride beyond
+  const unsigned blocks = static_cast<unsigned>(std::max<int64_t>(1, std::min(want, cap)));
+  if (vec)
+    silu_and_mul_kernel<T, VEC><<<blocks, 256, 0, stream>>>(static_cast<T *>(out), static_cast<const T *>(x), rows,
+                                                            static_cast<int>(n), stride);
+  else
+    silu_and_mul_kernel<T, 1><<<blocks, 256, 0, stream>>>(static_cast<T *>(out), static_cast<const T *>(x), rows,
+                                                          static_cast<int>(n), stride);
+  return launch_status();
+}
+
+}  // namespace
+}  // namespace nvb200
+
+using namespace nvb200;
+
+extern "C" int nvb200_rms_norm(void *y, const void *x, const void *w, int64_t groups, int64_t rows_per_group,
+                               int64_t group_stride, int64_t row_stride, int64_t n, float eps, int dtype,
+                               nvb200_stream_t stream) {
+  if (groups < 0 || rows_per_group <= 0 || n <= 0 || n > 0x7fffffffLL) return NVB200_ERR_ARG;
+  if (dtype != NVB200_BF16 && dtype != NVB200_F16 && dtype != NVB200_F32) return NVB200_ERR_ARG;
+  const int64_t rows = groups * rows_per_group;
+  if (rows == 0) return NVB200_OK;
+  if (!y || !x || !w) return NVB200_ERR_ARG;
+  if (int rc = check_device()) return rc;
+  const int es = elem_size(dtype);
+  RowArgs a{};
+  a.y = y, a.x = x, a.w = w, a.rows = rows, a.rows_per_group = rows_per_group;
+  a.x_group_stride = group_stride, a.x_row_stride = row_stride, a.n = static_cast<int>(n), a.eps = eps;
+  const bool vec_ok = aligned16(y) && aligned16(x) && aligned16(w) && (group_stride * es) % 16 == 0 &&
+                      (row_stride * es) % 16 == 0;
+  return dispatch_norm<false>(a, vec_ok, dtype, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int nvb200_fused_add_rms_norm(void *y, void *residual_out, const void *x, const void *residual,
+                                         const void *w, int64_t rows, int64_t n, int64_t x_row_stride,
+                                         int64_t residual_row_stride, float eps, int dtype, nvb200_stream_t stream) {
+  if (rows < 0 || n <= 0 || n > 0x7fffffffLL) return NVB200_ERR_ARG;
+  if (dtype != NVB200_BF16 && dtype != NVB200_F16 && dtype != NVB200_F32) return NVB200_ERR_ARG;
+  if (rows == 0) return NVB200_OK;
+  if (!y || !residual_out || !x || !residual || !w) return NVB200_ERR_ARG;
+  if (int rc = check_device()) return rc;
+  const int es = elem_size(dtype);
+  RowArgs a{};
+  a.y = y, a.res_out = residual_out, a.x = x, a.r = residual, a.w = w, a.rows = rows, a.rows_per_group = 1;
+  a.x_group_stride = x_row_stride, a.x_row_stride = 0, a.r_row_stride = residual_row_stride;
+  a.n = static_cast<int>(n), a.eps = eps;
+  const bool vec_ok = aligned16(y) && aligned16(residual_out) && aligned16(x) && aligned16(residual) &&
+                      aligned16(w) && (x_row_stride * es) % 16 == 0 && (residual_row_stride * es) % 16 == 0;
+  return dispatch_norm<true>(a, vec_ok, dtype, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int nvb200_silu_and_mul(void *out, const void *x, int64_t rows, int64_t n, int64_t x_row_stride,
+                                   int dtype, nvb200_stream_t stream) {
+  if (rows < 0 || n <= 0 || n > 0x3fffffffLL) return NVB200_ERR_ARG;
+  if (rows == 0) return NVB200_OK;
+  if (!out || !x) return NVB200_ERR_ARG;
+  if (int rc = check_device()) return rc;
+  const int es = elem_size(dtype);
+  const bool vec_ok = aligned16(out) && aligned16(x) && (x_row_stride * es) % 16 == 0 && (n * es) % 16 == 0;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case NVB200_BF16: return launch_silu<__nv_bfloat16>(out, x, rows, n, x_row_stride, vec_ok, s);
+    case NVB200_F16: return launch_silu<__half>(out, x, rows, n, x_row_stride, vec_ok, s);
+    case NVB200_F32: return launch_silu<float>(out, x, rows, n, x_row_stride, vec_ok, s);
+    default: return NVB200_ERR_ARG;
+  }
+}

@@ -1,0 +1,450 @@
+// Fused per-head q/k RMSNorm + neox RoPE + paged KV-cache write for sm_100a.
+//
+// Behaviour follows nanovllm/kernels/qk_norm_rope_kv.py:45-82 (the Triton kernel) and the torch code it replaces:
+// layers/layernorm.py:20-30 (RMSNorm.rms_forward), layers/rotary_embedding.py:6-14,37-48 (apply_rotary_emb,
+// RotaryEmbedding.forward) and layers/attention.py:11-31 (store_kvcache_kernel: slot -1 is skipped).
+//
+// Design (bulk path, used whenever every row is 16-byte aligned, i.e. always for qkv_proj views):
+//   * Work unit = one token x a group of G kv heads and the G*R q heads that share them (GQA, R = Hq/Hkv).
+//     Large batches use G = Hkv (one unit per token); small batches split heads so that every SM gets work.
+//   * One persistent CTA per SM owns a contiguous range of units. Warp 0 is the producer: it prefetches 32
+//     positions/slots at a time with one coalesced load and moves each unit's q rows, k rows, v rows (only when
+//     the slot is kept) and cos/sin row from HBM into a shared-memory stage with 1-D bulk copies
+//     (cp.async.bulk, completion counted on an mbarrier). Up to 16 stages are in flight per SM.
+//   * Consumer warps (8) take units round robin. A warp normalises and rotates 32/LPH heads per step in place in
+//     shared memory, each lane holding 8 elements of the first half and the matching 8 of the second half
+//     (LPH = D/16 lanes per head), so RoPE pairs are lane-local and the sum of squares needs log2(LPH) shuffles.
+//   * The finished q rows go to q_out, the k rows to k_out and/or k_cache[slot], and the v rows straight from the
+//     stage to v_cache[slot] with bulk stores (cp.async.bulk shared->global): v never enters registers.
+// Numerics: torch's two roundings (bf16 after the normalisation, bf16 product with the weight, which equals the
+// exact product rounded once) and RoPE with separately rounded fp32 products (no FMA contraction).
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace nvb200 {
+namespace {
+
+constexpr int kConsumerWarps = 8;
+constexpr int kThreads = 32 * (1 + kConsumerWarps);
+constexpr int kMaxStages = 16;
+constexpr int kSmemBudget = 200 * 1024;  // stage bytes per CTA (1 CTA per SM)
+constexpr int kHeaderBytes = 512;        // mbarriers and per-stage slot numbers
+
+struct QknrParams {
+  __nv_bfloat16 *q_out;
+  __nv_bfloat16 *k_out;
+  const __nv_bfloat16 *q;
+  const __nv_bfloat16 *k;
+  const __nv_bfloat16 *v;
+  int64_t q_stride, k_stride, v_stride;
+  const int64_t *positions;
+  const int32_t *slots;
+  const __nv_bfloat16 *q_w;
+  const __nv_bfloat16 *k_w;
+  const float *cos_sin;
+  int64_t cs_stride, num_positions;
+  __nv_bfloat16 *k_cache;
+  __nv_bfloat16 *v_cache;
+  int64_t num_slots;
+  int64_t num_tokens;
+  int hq, hkv;
+  int splits;       // units per token (S)
+  int g;            // kv heads per unit (G = Hkv / S)
+  int r;            // q heads per kv head (R)
+  int64_t units;    // T * S
+  int64_t chunk;    // units per CTA
+  int stages;       // pipeline depth
+  int stage_bytes;  // bytes per stage (multiple of 128)
+  float eps;
+  int32_t *status;
+};
+
+// ---------------------------------------------------------------------------------------------------------------
+// Per-head math of the bulk kernel. x1/x2: the 8 + 8 elements this lane holds of the two halves (fp32 values of
+// bf16 inputs). rstd: 1/rms of the head. w1/w2: the matching weights as bf16x2 words. c/s: cos/sin of the lane's
+// 8 RoPE pairs. y1/y2: the rotated outputs in fp32 (rounded to bf16 by the caller's pack).
+
+NVB200_DEVICE void norm_rope8(const float (&x1)[8], const float (&x2)[8], float rstd, const uint32_t (&w1)[4],
+                              const uint32_t (&w2)[4], const float (&c)[8], const float (&s)[8], float (&y1)[8],
+                              float (&y2)[8]) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    // torch: x.mul_(rsqrt(var + eps)) in fp32, .to(bf16), .mul_(weight) in bf16 (exact product, one rounding).
+    const uint32_t n1 = bf16x2_mul(pack_bf16x2(__fmul_rn(x1[2 * i], rstd), __fmul_rn(x1[2 * i + 1], rstd)), w1[i]);
+    const uint32_t n2 = bf16x2_mul(pack_bf16x2(__fmul_rn(x2[2 * i], rstd), __fmul_rn(x2[2 * i + 1], rstd)), w2[i]);
+    const float a0 = bf16_lo(n1), a1 = bf16_hi(n1), b0 = bf16_lo(n2), b1 = bf16_hi(n2);
+    // apply_rotary_emb: y1 = x1*cos - x2*sin, y2 = x2*cos + x1*sin, each product rounded separately.
+    y1[2 * i] = __fsub_rn(__fmul_rn(a0, c[2 * i]), __fmul_rn(b0, s[2 * i]));
+    y1[2 * i + 1] = __fsub_rn(__fmul_rn(a1, c[2 * i + 1]), __fmul_rn(b1, s[2 * i + 1]));
+    y2[2 * i] = __fadd_rn(__fmul_rn(b0, c[2 * i]), __fmul_rn(a0, s[2 * i]));
+    y2[2 * i + 1] = __fadd_rn(__fmul_rn(b1, c[2 * i + 1]), __fmul_rn(a1, s[2 * i + 1]));
+  }
+}
+
+NVB200_DEVICE void load_w8(const __nv_bfloat16 *p, uint32_t (&w)[4]) {
+  const uint4 v = __ldg(reinterpret_cast<const uint4 *>(p));
+  w[0] = v.x, w[1] = v.y, w[2] = v.z, w[3] = v.w;
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Bulk-copy pipeline kernel. D in {64, 128, 256}.
+
+template <int D>
+__global__ void __launch_bounds__(kThreads, 1) qknr_bulk_kernel(const __grid_constant__ QknrParams p) {
+  constexpr int HALF = D / 2;
+  constexpr int LPH = D / 16;    // lanes per head: each lane holds 8 + 8 elements
+  constexpr int HPI = 32 / LPH;  // heads per warp step
+  extern __shared__ __align__(128) uint8_t smem[];
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int NS = p.stages;
+  const uint32_t bar_base = smem_addr(smem);  // full[0..NS), empty[0..NS)
+  int32_t *meta = reinterpret_cast<int32_t *>(smem + 2 * 8 * kMaxStages);
+  const uint32_t stage_base = smem_addr(smem + kHeaderBytes);
+
+  const int64_t first = static_cast<int64_t>(blockIdx.x) * p.chunk;
+  if (first >= p.units) return;
+  const int n_units = static_cast<int>(p.chunk < p.units - first ? p.chunk : p.units - first);
+
+  const int nq = p.g * p.r;  // q heads per unit
+  const uint32_t qb = nq * D * 2, kb = p.g * D * 2, csb = D * 4;
+  const bool store = p.k_cache != nullptr;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(bar_base + 8 * i, 1);         // full: producer's arrive + transaction bytes
+      mbar_init(bar_base + 8 * (NS + i), 1);  // empty: the consuming warp's arrive
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ producer
+    bool abort = false;
+    for (int base = 0; base < n_units && !abort; base += 32) {
+      int64_t pos = 0;
+      int32_t slot = -1;
+      if (base + lane < n_units) {
+        const int64_t t = (first + base + lane) / p.splits;
+        pos = __ldg(p.positions + t);
+        if (pos < 0 || pos >= p.num_positions) {
+          set_status(p.status, NVB200_STATUS_BAD_POSITION);
+          pos = 0;
+        }
+        if (store) {
+          slot = __ldg(p.slots + t);
+          if (slot < -1 || slot >= p.num_slots) {
+            set_status(p.status, NVB200_STATUS_BAD_SLOT);
+            slot = -1;
+          }
+        }
+      }
+      const int cnt = min(32, n_units - base);
+      for (int j = 0; j < cnt; ++j) {
+        const int64_t pj = __shfl_sync(0xffffffffu, pos, j);
+        const int32_t sj = __shfl_sync(0xffffffffu, slot, j);
+        if (lane == 0) {
+          const int it = base + j;
+          const int st = it % NS;
+          const uint32_t ph = (it / NS) & 1;
+          const uint32_t full = bar_base + 8 * st, empty = bar_base + 8 * (NS + st);
+          if (!mbar_wait_bounded(empty, ph ^ 1)) {
+            set_status(p.status, NVB200_STATUS_WAIT_TIMEOUT);
+            abort = true;
+          } else {
+            meta[st] = sj;
+            const int64_t unit = first + it;
+            const int64_t t = unit / p.splits;
+            const int s = static_cast<int>(unit % p.splits);
+            const uint32_t sb = stage_base + st * p.stage_bytes;
+            const uint32_t vbytes = sj >= 0 ? kb : 0;
+            mbar_arrive_expect_tx(full, qb + kb + csb + vbytes);
+            bulk_g2s(sb, p.q + t * p.q_stride + static_cast<int64_t>(s) * nq * D, qb, full);
+            bulk_g2s(sb + qb, p.k + t * p.k_stride + static_cast<int64_t>(s) * p.g * D, kb, full);
+            if (vbytes) bulk_g2s(sb + qb + kb, p.v + t * p.v_stride + static_cast<int64_t>(s) * p.g * D, kb, full);
+            bulk_g2s(sb + qb + 2 * kb, p.cos_sin + pj * p.cs_stride, csb, full);
+          }
+        }
+        abort = __shfl_sync(0xffffffffu, abort, 0);
+        if (abort) break;
+      }
+    }
+    return;
+  }
+
+  // -------------------------------------------------------------------- consumers
+  const int cw = warp - 1;
+  const int j = lane % LPH;   // 8-element column block inside each half
+  const int hl = lane / LPH;  // head within the warp step
+  uint32_t wq1[4], wq2[4], wk1[4], wk2[4];
+  load_w8(p.q_w + 8 * j, wq1);
+  load_w8(p.q_w + HALF + 8 * j, wq2);
+  load_w8(p.k_w + 8 * j, wk1);
+  load_w8(p.k_w + HALF + 8 * j, wk2);
+  const int total = nq + p.g;
+
+  for (int it = cw; it < n_units; it += kConsumerWarps) {
+    const int st = it % NS;
+    const uint32_t ph = (it / NS) & 1;
+    const uint32_t full = bar_base + 8 * st, empty = bar_base + 8 * (NS + st);
+    if (!mbar_wait_bounded(full, ph)) {
+      if (lane == 0) set_status(p.status, NVB200_STATUS_WAIT_TIMEOUT);
+      break;
+    }
+    const int32_t slot = meta[st];
+    const uint32_t sb = stage_base + st * p.stage_bytes;
+    const uint32_t sq = sb, sk = sb + qb, sv = sb + qb + kb, scs = sb + qb + 2 * kb;
+
+    float c[8], s[8];
+    {
+      const float4 c0 = ld_shared_f4(scs + 32 * j), c1 = ld_shared_f4(scs + 32 * j + 16);
+      const float4 s0 = ld_shared_f4(scs + 4 * HALF + 32 * j), s1 = ld_shared_f4(scs + 4 * HALF + 32 * j + 16);
+      c[0] = c0.x, c[1] = c0.y, c[2] = c0.z, c[3] = c0.w, c[4] = c1.x, c[5] = c1.y, c[6] = c1.z, c[7] = c1.w;
+      s[0] = s0.x, s[1] = s0.y, s[2] = s0.z, s[3] = s0.w, s[4] = s1.x, s[5] = s1.y, s[6] = s1.z, s[7] = s1.w;
+    }
+
+    for (int h0 = 0; h0 < total; h0 += HPI) {
+      const int h = h0 + hl;
+      const bool active = h < total;
+      const bool isq = h < nq;
+      const uint32_t row = active ? (isq ? sq + h * D * 2 : sk + (h - nq) * D * 2) : sq;
+      const uint4 a = ld_shared_v4(row + 16 * j);
+      const uint4 b = ld_shared_v4(row + 2 * HALF + 16 * j);
+      float x1[8], x2[8];
+      unpack8(a, x1);
+      unpack8(b, x2);
+      float ss = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ss = fmaf(x1[i], x1[i], ss);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ss = fmaf(x2[i], x2[i], ss);
+#pragma unroll
+      for (int o = LPH / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      const float rstd = rsqrtf(ss / static_cast<float>(D) + p.eps);
+      uint32_t w1[4], w2[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        w1[i] = isq ? wq1[i] : wk1[i];
+        w2[i] = isq ? wq2[i] : wk2[i];
+      }
+      float y1[8], y2[8];
+      norm_rope8(x1, x2, rstd, w1, w2, c, s, y1, y2);
+      if (active) {
+        st_shared_v4(row + 16 * j, pack8(y1));
+        st_shared_v4(row + 2 * HALF + 16 * j, pack8(y2));
+      }
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      const int64_t unit = first + it;
+      const int64_t t = unit / p.splits;
+      const int sp = static_cast<int>(unit % p.splits);
+      bulk_s2g(p.q_out + (t * p.hq + static_cast<int64_t>(sp) * nq) * D, sq, qb);
+      if (p.k_out) bulk_s2g(p.k_out + (t * p.hkv + static_cast<int64_t>(sp) * p.g) * D, sk, kb);
+      if (slot >= 0) {
+        const int64_t off = (static_cast<int64_t>(slot) * p.hkv + static_cast<int64_t>(sp) * p.g) * D;
+        bulk_s2g(p.k_cache + off, sk, kb);
+        bulk_s2g(p.v_cache + off, sv, kb);
+      }
+      bulk_commit();
+      bulk_wait_read<0>();
+      mbar_arrive(empty);
+    }
+    __syncwarp();
+  }
+  if (lane == 0) bulk_wait<0>();
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Generic kernel for layouts the bulk engine cannot move (a row not 16-byte aligned, or D outside {64,128,256}).
+// One warp per (token, head); lane i holds the RoPE pairs (i, i + D/2), (i + 32, i + 32 + D/2), ...
+
+constexpr int kGenericWarps = 4;
+constexpr int kGenericMaxPairs = 8;  // D <= 512
+
+__global__ void __launch_bounds__(32 * kGenericWarps) qknr_generic_kernel(const __grid_constant__ QknrParams p,
+                                                                          int D) {
+  const int lane = threadIdx.x & 31;
+  const int64_t t = blockIdx.x;
+  const int h = blockIdx.y * kGenericWarps + (threadIdx.x >> 5);
+  if (h >= p.hq + p.hkv) return;
+  const int HALF = D / 2;
+  const bool isq = h < p.hq;
+  const int hk = h - p.hq;
+  const __nv_bfloat16 *x = isq ? p.q + t * p.q_stride + static_cast<int64_t>(h) * D
+                               : p.k + t * p.k_stride + static_cast<int64_t>(hk) * D;
+  const __nv_bfloat16 *w = isq ? p.q_w : p.k_w;
+
+  int64_t pos = p.positions[t];
+  if (pos < 0 || pos >= p.num_positions) {
+    if (lane == 0) set_status(p.status, NVB200_STATUS_BAD_POSITION);
+    pos = 0;
+  }
+  const float *cs = p.cos_sin + pos * p.cs_stride;
+
+  float x1[kGenericMaxPairs], x2[kGenericMaxPairs];
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < kGenericMaxPairs; ++k) {
+    const int i = lane + 32 * k;
+    x1[k] = x2[k] = 0.f;
+    if (i < HALF) {
+      x1[k] = __bfloat162float(x[i]);
+      x2[k] = __bfloat162float(x[i + HALF]);
+      ss = fmaf(x1[k], x1[k], ss);
+      ss = fmaf(x2[k], x2[k], ss);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  const float rstd = rsqrtf(ss / static_cast<float>(D) + p.eps);
+
+  int32_t slot = -1;
+  if (!isq && p.k_cache != nullptr) {
+    slot = p.slots[t];
+    if (slot < -1 || slot >= p.num_slots) {
+      if (lane == 0) set_status(p.status, NVB200_STATUS_BAD_SLOT);
+      slot = -1;
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < kGenericMaxPairs; ++k) {
+    const int i = lane + 32 * k;
+    if (i >= HALF) break;
+    const float n1 = __bfloat162float(__hmul(__float2bfloat16_rn(__fmul_rn(x1[k], rstd)), w[i]));
+    const float n2 = __bfloat162float(__hmul(__float2bfloat16_rn(__fmul_rn(x2[k], rstd)), w[i + HALF]));
+    const float c = cs[i], s = cs[i + HALF];
+    const __nv_bfloat16 y1 = __float2bfloat16_rn(__fsub_rn(__fmul_rn(n1, c), __fmul_rn(n2, s)));
+    const __nv_bfloat16 y2 = __float2bfloat16_rn(__fadd_rn(__fmul_rn(n2, c), __fmul_rn(n1, s)));
+    if (isq) {
+      __nv_bfloat16 *o = p.q_out + (t * p.hq + h) * D;
+      o[i] = y1;
+      o[i + HALF] = y2;
+    } else {
+      if (p.k_out) {
+        __nv_bfloat16 *o = p.k_out + (t * p.hkv + hk) * D;
+        o[i] = y1;
+        o[i + HALF] = y2;
+      }
+      if (slot >= 0) {
+        const int64_t off = (static_cast<int64_t>(slot) * p.hkv + hk) * D;
+        p.k_cache[off + i] = y1;
+        p.k_cache[off + i + HALF] = y2;
+      }
+    }
+  }
+  if (slot >= 0) {
+    const __nv_bfloat16 *vr = p.v + t * p.v_stride + static_cast<int64_t>(hk) * D;
+    __nv_bfloat16 *vo = p.v_cache + (static_cast<int64_t>(slot) * p.hkv + hk) * D;
+    for (int i = lane; i < D; i += 32) vo[i] = vr[i];
+  }
+}
+
+template <int D>
+int launch_bulk(QknrParams &p, int sms, cudaStream_t stream) {
+  const int smem = kHeaderBytes + p.stages * p.stage_bytes;
+  static int configured[64] = {0};  // per device: max dynamic shared memory raised once
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !configured[dev]) {
+    if (cudaFuncSetAttribute(qknr_bulk_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kHeaderBytes + kSmemBudget) != cudaSuccess)
+      return NVB200_ERR_CUDA;
+    configured[dev] = 1;
+  }
+  const int64_t grid = std::min<int64_t>(p.units, sms);
+  p.chunk = (p.units + grid - 1) / grid;
+  const int64_t blocks = (p.units + p.chunk - 1) / p.chunk;
+  qknr_bulk_kernel<D><<<static_cast<unsigned>(blocks), kThreads, smem, stream>>>(p);
+  return launch_status();
+}
+
+}  // namespace
+
+int qk_norm_rope_kv_launch(const nvb200_qk_norm_rope_kv_args *a, cudaStream_t stream) {
+  if (a == nullptr) return NVB200_ERR_ARG;
+  const int64_t T = a->num_tokens;
+  const int hq = a->num_q_heads, hkv = a->num_kv_heads, D = a->head_dim;
+  if (T < 0 || hq <= 0 || hkv <= 0 || D <= 0 || hq % hkv != 0 || D % 2 != 0) return NVB200_ERR_ARG;
+  if (D > 2 * 32 * kGenericMaxPairs) return NVB200_ERR_UNSUPPORTED;
+  if (T == 0) return NVB200_OK;
+  const bool store = a->k_cache != nullptr || a->v_cache != nullptr;
+  if (!a->q_out || !a->q || !a->k || !a->positions || !a->q_weight || !a->k_weight || !a->cos_sin) return NVB200_ERR_ARG;
+  if (store && (!a->k_cache || !a->v_cache || !a->slot_mapping || !a->v || a->num_slots <= 0)) return NVB200_ERR_ARG;
+  if (a->num_positions <= 0 || a->cos_sin_stride < D) return NVB200_ERR_ARG;
+  if (int rc = check_device()) return rc;
+
+  QknrParams p{};
+  p.q_out = static_cast<__nv_bfloat16 *>(a->q_out);
+  p.k_out = static_cast<__nv_bfloat16 *>(a->k_out);
+  p.q = static_cast<const __nv_bfloat16 *>(a->q);
+  p.k = static_cast<const __nv_bfloat16 *>(a->k);
+  p.v = static_cast<const __nv_bfloat16 *>(a->v);
+  p.q_stride = a->q_token_stride;
+  p.k_stride = a->k_token_stride;
+  p.v_stride = a->v_token_stride;
+  p.positions = a->positions;
+  p.slots = store ? a->slot_mapping : nullptr;
+  p.q_w = static_cast<const __nv_bfloat16 *>(a->q_weight);
+  p.k_w = static_cast<const __nv_bfloat16 *>(a->k_weight);
+  p.cos_sin = a->cos_sin;
+  p.cs_stride = a->cos_sin_stride;
+  p.num_positions = a->num_positions;
+  p.k_cache = store ? static_cast<__nv_bfloat16 *>(a->k_cache) : nullptr;
+  p.v_cache = store ? static_cast<__nv_bfloat16 *>(a->v_cache) : nullptr;
+  p.num_slots = store ? a->num_slots : 0;
+  p.num_tokens = T;
+  p.hq = hq;
+  p.hkv = hkv;
+  p.r = hq / hkv;
+  p.eps = a->eps;
+  p.status = a->status;
+
+  const bool rows16 = (a->q_token_stride * 2) % 16 == 0 && (a->k_token_stride * 2) % 16 == 0 &&
+                      (!store || (a->v_token_stride * 2) % 16 == 0) && (a->cos_sin_stride * 4) % 16 == 0;
+  const bool ptrs16 = aligned16(a->q_out) && aligned16(a->k_out) && aligned16(a->q) && aligned16(a->k) &&
+                      aligned16(a->v) && aligned16(a->cos_sin) && aligned16(a->q_weight) &&
+                      aligned16(a->k_weight) && aligned16(a->k_cache) && aligned16(a->v_cache);
+  const bool bulk = (D == 64 || D == 128 || D == 256) && rows16 && ptrs16;
+
+  if (!bulk) {
+    p.splits = 1;
+    p.g = hkv;
+    dim3 grid(static_cast<unsigned>(T), (hq + hkv + kGenericWarps - 1) / kGenericWarps);
+    if (T > 0x7fffffffLL) return NVB200_ERR_UNSUPPORTED;
+    qknr_generic_kernel<<<grid, 32 * kGenericWarps, 0, stream>>>(p, D);
+    return launch_status();
+  }
+
+  // Heads per unit: as many as possible while the units still cover every SM once.
+  const int sms = sm_count();
+  int splits = hkv;
+  for (int d = 1; d <= hkv; ++d) {
+    if (hkv % d == 0 && T * d >= sms) {
+      splits = d;
+      break;
+    }
+  }
+  p.splits = splits;
+  p.g = hkv / splits;
+  p.units = T * splits;
+  const int unit_bytes = (p.g * p.r + 2 * p.g) * D * 2 + D * 4;
+  p.stage_bytes = (unit_bytes + 127) / 128 * 128;
+  p.stages = std::max(2, std::min(kMaxStages, kSmemBudget / p.stage_bytes));
+  if (p.stage_bytes * 2 > kSmemBudget) return NVB200_ERR_UNSUPPORTED;  // > 100 KB per token: too many heads
+  switch (D) {
+    case 64: return launch_bulk<64>(p, sms, stream);
+    case 128: return launch_bulk<128>(p, sms, stream);
+    default: return launch_bulk<256>(p, sms, stream);
+  }
+}
+
+}  // namespace nvb200
+
+extern "C" int nvb200_qk_norm_rope_kv(const nvb200_qk_norm_rope_kv_args *args, nvb200_stream_t stream) {
+  return nvb200::qk_norm_rope_kv_launch(args, reinterpret_cast<cudaStream_t>(stream));
+}

@@ -1,0 +1,35 @@
+"""Tiled matmul C = A @ B on B200 (drop-in for nanovllm/kernels/matmul.py).
+
+Same call as the reference's `matmul` (nanovllm/kernels/matmul.py:84-99): A [M, K] @ B [K, N] -> C [M, N] in A's
+dtype, fp32 accumulation, B with any strides (e.g. an nn.Linear weight.t()), the same assertions. The work runs in
+`nvb200_matmul` (include/nvb200.h): bf16 and tf32 on the tcgen05 tensor cores (TMA-fed shared-memory stages, TMEM
+accumulators), fp32 "ieee" as exact fp32 FMA on the CUDA cores.
+"""
+import torch
+
+from nanovllm_b200 import _lib
+
+
+def matmul(a: torch.Tensor, b: torch.Tensor, input_precision: str = "ieee") -> torch.Tensor:
+    """a [M, K] @ b [K, N] -> [M, N] in a's dtype. input_precision only matters for fp32 inputs:
+    "ieee" = true fp32 FMA, "tf32" = tensor cores with tf32-rounded inputs."""
+    if not (a.ndim == 2 and b.ndim == 2 and a.shape[1] == b.shape[0]):
+        raise AssertionError((a.shape, b.shape))
+    if not (a.dtype == b.dtype and a.dtype in (torch.float32, torch.bfloat16)):
+        raise AssertionError((a.dtype, b.dtype))
+    if input_precision not in ("ieee", "tf32"):
+        raise AssertionError(input_precision)
+    M, K = a.shape
+    N = b.shape[1]
+    c = torch.empty((M, N), device=a.device, dtype=a.dtype)
+    if M and N:
+        code = _lib.DTYPE_CODE[a.dtype]
+        tf32 = int(a.dtype == torch.float32 and input_precision == "tf32")
+        args = (M, N, K, a.stride(0), a.stride(1), b.stride(0), b.stride(1))
+        ws_bytes = _lib.lib().nvb200_matmul_workspace_size(*args, code)
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=a.device) if ws_bytes else None
+        _lib.check(_lib.lib().nvb200_matmul(c.data_ptr(), a.data_ptr(), b.data_ptr(), *args, c.stride(0), c.stride(1),
+                                            code, tf32, _lib.ptr(ws), ws_bytes,
+                                            _lib.status_word(a.device).data_ptr(), _lib.stream_of(a)),
+                   "matmul")
+    return c

@@ -1,0 +1,80 @@
+"""Fused q/k RMSNorm + neox RoPE + paged KV-cache write on B200 (drop-in for nanovllm/kernels/qk_norm_rope_kv.py).
+
+Same call as the reference's `qk_norm_rope_kv` (nanovllm/kernels/qk_norm_rope_kv.py:92-125): the same arguments,
+the same assertions on them (:106-114), the same freshly allocated outputs (:115-116) and no launch when T == 0
+(:117). The work runs in `nvb200_qk_norm_rope_kv` (include/nvb200.h), a hand-written sm_100a kernel that stages each
+token's q/k/v rows and cos/sin row in shared memory with bulk copies, normalises and rotates them, and bulk-stores
+q_out, k_out and the k/v cache rows (slot -1 skipped).
+
+Differences from the reference, all widening what it accepts:
+  * kv_per_prog and num_warps are accepted and ignored (they tune the Triton launch). In particular the
+    reference's `Hkv % kv_per_prog == 0` requirement (:107, kv_per_prog = 4) does not apply, so 1 or 2 kv heads
+    per rank (tensor parallel 4/8 of Qwen3) work.
+  * Out-of-range positions or slots never fault: they are skipped and flagged in the device status word
+    (nanovllm_b200.status()).
+"""
+import ctypes
+
+import torch
+
+from nanovllm_b200 import _lib
+
+
+def _require(cond: bool, msg: str = "") -> None:
+    if not cond:
+        raise AssertionError(msg)
+
+
+def qk_norm_rope_kv(
+    q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, positions: torch.Tensor,
+    q_weight: torch.Tensor, k_weight: torch.Tensor, eps: float, cos_sin_cache: torch.Tensor,
+    k_cache: torch.Tensor, v_cache: torch.Tensor, slot_mapping: torch.Tensor | None, write_k: bool,
+    kv_per_prog: int | None = None, num_warps: int | None = None,
+) -> tuple[torch.Tensor, torch.Tensor | None]:
+    """q: [T, Hq, D], k, v: [T, Hkv, D] bf16, each with a contiguous head (any token stride: views of the qkv
+    output work). positions: [T] int64. cos_sin_cache: [max_pos, 1, D] or [max_pos, D] fp32 (cos | sin).
+    k_cache, v_cache: [blocks, block_size, Hkv, D] contiguous, or empty (then nothing is stored).
+    slot_mapping: [T] int32, -1 = don't store. Returns (q_out [T, Hq, D], k_out [T, Hkv, D] or None)."""
+    T, Hq, D = q.shape
+    Hkv = k.shape[1]
+    _require(q.dtype == k.dtype == v.dtype == torch.bfloat16 and k.shape == v.shape == (T, Hkv, D),
+             "q, k, v must be bf16 with k.shape == v.shape == (T, Hkv, D)")
+    _require(Hq % Hkv == 0 and D % 2 == 0, "Hq must be a multiple of Hkv and D even")
+    for x in (q, k, v):
+        _require(x.stride(2) == 1 and x.stride(1) == D, "each head must be contiguous: stride(2) == 1, stride(1) == D")
+    _require(positions.shape == (T,) and cos_sin_cache.dtype == torch.float32 and cos_sin_cache.shape[-1] == D,
+             "positions must be [T] and cos_sin_cache fp32 [..., D]")
+    _require(positions.dtype == torch.int64, "positions must be int64")
+    _require(cos_sin_cache.stride(-1) == 1 and cos_sin_cache.numel() == cos_sin_cache.shape[0] * D,
+             "cos_sin_cache must be [max_pos, D] or [max_pos, 1, D] rows with a unit last stride")
+    _require(q_weight.dtype == k_weight.dtype == torch.bfloat16 and q_weight.shape == k_weight.shape == (D,)
+             and q_weight.is_contiguous() and k_weight.is_contiguous(), "q/k weights must be contiguous bf16 [D]")
+    store = k_cache.numel() > 0
+    if store:
+        _require(k_cache.is_contiguous() and v_cache.is_contiguous() and k_cache.shape[-2:] == (Hkv, D),
+                 "k_cache, v_cache must be contiguous [..., Hkv, D]")
+        _require(v_cache.shape == k_cache.shape and k_cache.dtype == v_cache.dtype == torch.bfloat16,
+                 "v_cache must match k_cache (bf16)")
+        _require(slot_mapping is not None and slot_mapping.shape == (T,), "slot_mapping must be [T]")
+        _require(slot_mapping.dtype == torch.int32, "slot_mapping must be int32")
+    dev = q.device
+    _require(dev.type == "cuda", "q must be a CUDA tensor")
+    q_out = torch.empty(T, Hq, D, dtype=q.dtype, device=dev)
+    k_out = torch.empty(T, Hkv, D, dtype=k.dtype, device=dev) if write_k else None
+    if T:
+        a = _lib.QkNormRopeKvArgs()
+        a.q_out, a.k_out = q_out.data_ptr(), _lib.ptr(k_out)
+        a.q, a.k, a.v = q.data_ptr(), k.data_ptr(), v.data_ptr()
+        a.q_token_stride, a.k_token_stride, a.v_token_stride = q.stride(0), k.stride(0), v.stride(0)
+        a.positions = positions.data_ptr()
+        a.slot_mapping = slot_mapping.data_ptr() if store else None
+        a.q_weight, a.k_weight = q_weight.data_ptr(), k_weight.data_ptr()
+        a.cos_sin, a.cos_sin_stride, a.num_positions = (cos_sin_cache.data_ptr(), cos_sin_cache.stride(0),
+                                                        cos_sin_cache.shape[0])
+        if store:
+            a.k_cache, a.v_cache, a.num_slots = k_cache.data_ptr(), v_cache.data_ptr(), k_cache.numel() // (Hkv * D)
+        a.num_tokens, a.num_q_heads, a.num_kv_heads, a.head_dim = T, Hq, Hkv, D
+        a.eps = eps
+        a.status = _lib.status_word(dev).data_ptr()
+        _lib.check(_lib.lib().nvb200_qk_norm_rope_kv(ctypes.byref(a), _lib.stream_of(q)), "qk_norm_rope_kv")
+    return q_out, k_out

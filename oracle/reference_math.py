@@ -1,0 +1,153 @@
+"""CPU restatement of the reference's torch implementation of the pre-attention hot path.
+
+TEST INFRASTRUCTURE ONLY: the checker for nanovllm_b200 and the timed CPU baseline, never part of the product.
+
+The reference (R3pere/nano-vllm-triton-kernels) computes these ops with torch code in nanovllm/layers/; its Triton
+kernels reproduce that code's roundings. Each function below restates one piece of that torch code, op for op, so
+that on the same inputs it rounds at the same points (the `.float()` upcasts, the `.to(dtype)` downcasts, and the
+dtype multiplies). All functions are device-agnostic torch code: the parity tests run them on CPU tensors, and on
+CUDA tensors for the largest sizes (the same eager torch ops the reference's own tests compare against).
+
+Pinning: tests/golden/make_golden.py imports the reference itself (its layer modules, run eagerly on CPU), writes
+its outputs on seeded inputs to tests/golden/golden.pt, and tests/test_oracle.py checks every function here against
+those fixtures bit for bit.
+"""
+import math
+
+import torch
+import torch.nn.functional as F
+
+
+def rms_forward(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
+    """RMSNorm.rms_forward (nanovllm/layers/layernorm.py:20-30): fp32 mean of squares, x * rsqrt(var + eps) in fp32,
+    rounded to x's dtype, then multiplied by the weight in that dtype."""
+    orig = x.dtype
+    xf = x.float()
+    var = xf.pow(2).mean(dim=-1, keepdim=True)
+    xf = xf * torch.rsqrt(var + eps)
+    return xf.to(orig) * weight
+
+
+def add_rms_forward(x: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor,
+                    eps: float) -> tuple[torch.Tensor, torch.Tensor]:
+    """RMSNorm.add_rms_forward (nanovllm/layers/layernorm.py:32-44): s = x + residual in fp32; the new residual is
+    s rounded to x's dtype; the normalised output uses the unrounded s."""
+    orig = x.dtype
+    s = x.float() + residual.float()
+    new_residual = s.to(orig)
+    var = s.pow(2).mean(dim=-1, keepdim=True)
+    s = s * torch.rsqrt(var + eps)
+    return s.to(orig) * weight, new_residual
+
+
+def rope_cos_sin_cache(head_size: int, max_position: int, base: float) -> torch.Tensor:
+    """RotaryEmbedding.__init__ (nanovllm/layers/rotary_embedding.py:17-35): [max_position, 1, head_size] fp32 rows
+    of (cos | sin) of position * inv_freq, inv_freq = 1 / base^(2i / head_size)."""
+    inv_freq = 1.0 / (base ** (torch.arange(0, head_size, 2, dtype=torch.float) / head_size))
+    t = torch.arange(max_position, dtype=torch.float)
+    freqs = torch.einsum("i,j -> ij", t, inv_freq)
+    return torch.cat((freqs.cos(), freqs.sin()), dim=-1).unsqueeze_(1)
+
+
+def apply_rotary_emb(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+    """apply_rotary_emb (nanovllm/layers/rotary_embedding.py:6-14): neox halves, fp32 products rounded separately,
+    result rounded to x's dtype."""
+    x1, x2 = torch.chunk(x.float(), 2, dim=-1)
+    y1 = x1 * cos - x2 * sin
+    y2 = x2 * cos + x1 * sin
+    return torch.cat((y1, y2), dim=-1).to(x.dtype)
+
+
+def rotary(positions: torch.Tensor, q: torch.Tensor, k: torch.Tensor,
+           cos_sin_cache: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """RotaryEmbedding.forward (nanovllm/layers/rotary_embedding.py:37-48) for q [T, Hq, D], k [T, Hkv, D]."""
+    cos_sin = cos_sin_cache[positions]
+    if cos_sin.dim() == 2:  # a [max_pos, D] table: add the head axis
+        cos_sin = cos_sin.unsqueeze(1)
+    cos, sin = cos_sin.chunk(2, dim=-1)
+    return apply_rotary_emb(q, cos, sin), apply_rotary_emb(k, cos, sin)
+
+
+def store_kvcache(k: torch.Tensor, v: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                  slot_mapping: torch.Tensor) -> None:
+    """store_kvcache_kernel (nanovllm/layers/attention.py:11-31): row t of k and v ([Hkv * D] elements) goes to row
+    slot_mapping[t] of the flattened caches; slot -1 is skipped. In place."""
+    T, hkv, d = k.shape
+    keep = slot_mapping >= 0
+    rows = slot_mapping[keep].long()
+    k_cache.view(-1, hkv * d)[rows] = k.reshape(T, hkv * d)[keep]
+    v_cache.view(-1, hkv * d)[rows] = v.reshape(T, hkv * d)[keep]
+
+
+def qk_norm_rope_kv(q, k, v, positions, q_weight, k_weight, eps, cos_sin_cache, k_cache, v_cache, slot_mapping,
+                    write_k):
+    """The torch composition that nanovllm/kernels/qk_norm_rope_kv.py:92-125 replaces (q_norm, k_norm, rotary_emb,
+    store_kvcache; nanovllm/models/qwen3.py:99-103 and layers/attention.py:64-76). Mutates the caches in place
+    (unless they are empty) and returns (q_out, k_out or None)."""
+    qn = rms_forward(q, q_weight, eps)
+    kn = rms_forward(k, k_weight, eps)
+    qr, kr = rotary(positions, qn, kn, cos_sin_cache)
+    if k_cache.numel() > 0:
+        store_kvcache(kr, v, k_cache, v_cache, slot_mapping)
+    return qr.contiguous(), (kr.contiguous() if write_k else None)
+
+
+def silu_and_mul(x: torch.Tensor) -> torch.Tensor:
+    """SiluAndMul.silu_and_mul_compiled (nanovllm/layers/activation.py:15-18) run eagerly: silu of the gate half in
+    fp32 rounded to x's dtype, times the up half in x's dtype."""
+    n = x.shape[-1] // 2
+    gate, up = x[..., :n], x[..., n:2 * n]
+    return F.silu(gate) * up
+
+
+def matmul(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """The reference's matmul oracle (tests/test_kernels_matmul.py:52): the float64 product of the inputs."""
+    return a.double() @ b.double()
+
+
+def tf32_round(x: torch.Tensor) -> torch.Tensor:
+    """x (fp32) rounded to tf32 (10 explicit mantissa bits, round to nearest, ties away from zero as the tensor
+    core's operand conversion does for finite values); used to build the tf32 product reference a_tf32 @ b_tf32."""
+    i = x.contiguous().view(torch.int32)
+    i = (i + 0x1000) & ~0x1FFF
+    return i.view(torch.float32).reshape(x.shape)
+
+
+# Byte / flop counts of the reference's microbenchmarks (scripts/bench_qk_rope_kv.py:50-52,
+# scripts/bench_norm_act.py:3-5, scripts/bench_matmul.py:82).
+
+def qk_norm_rope_kv_bytes(T: int, hq: int, hkv: int, d: int, write_k: bool = False) -> int:
+    per_token = (hq + 2 * hkv) * d * 2 + 8 + 4 + d * 4 + (hq + 2 * hkv) * d * 2
+    return T * (per_token + (hkv * d * 2 if write_k else 0)) + 2 * d * 2
+
+
+def rms_norm_bytes(T: int, n: int) -> int:
+    return (2 * T * n + n) * 2
+
+
+def add_rms_norm_bytes(T: int, n: int) -> int:
+    return (4 * T * n + n) * 2
+
+
+def silu_and_mul_bytes(T: int, n: int) -> int:
+    return 3 * T * n * 2
+
+
+def matmul_flops(m: int, n: int, k: int) -> int:
+    return 2 * m * n * k
+
+
+def bf16_ulp_diff(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """Distance in bf16 steps between two bf16 tensors: bit patterns mapped to a monotonic integer line (the metric of
+    tests/test_kernels_qk_rope_kv.py:46-51 in the reference)."""
+    def line(t):
+        i = t.contiguous().view(torch.int16).to(torch.int32)
+        return torch.where(i < 0, -(i & 0x7FFF), i)
+    return (line(a) - line(b)).abs()
+
+
+def matmul_tolerance(dtype: str, prec: str, k: int) -> tuple[float, float]:
+    """(rtol, atol) of tests/test_kernels_matmul.py:21-25: atol scales with sqrt(K)."""
+    rtol, atol = {("fp32", "ieee"): (1e-4, 1e-4), ("fp32", "tf32"): (1e-2, 1e-2),
+                  ("bf16", "ieee"): (1.6e-2, 1e-2)}[(dtype, prec)]
+    return rtol, atol * math.sqrt(k)

@@ -1,0 +1,94 @@
+"""Parity of nanovllm_b200's matmul (nvb200_matmul) with the oracle: the float64 product of the inputs.
+
+Mirrors the reference's tests/test_kernels_matmul.py (same shapes, tolerances, seeds and the ieee != tf32 guard):
+  fp32 "ieee": rtol 1e-4, atol 1e-4 * sqrt(K);  fp32 "tf32": rtol 1e-2, atol 1e-2 * sqrt(K);
+  bf16:        rtol 1.6e-2, atol 1e-2 * sqrt(K).
+Plus the north-star's rtol 1e-3 for fp32/tf32: tf32 against the float64 product of the tf32-rounded inputs (the
+products the tensor cores form), and the BASELINE config-4 shapes (M in {32, 2048, 4096}, B = weight.t()).
+"""
+import math
+
+import pytest
+import torch
+
+from nanovllm_b200.kernels.matmul import matmul
+from oracle import reference_math as om
+
+pytestmark = pytest.mark.gpu
+
+DTYPES = {"fp32": torch.float32, "bf16": torch.bfloat16}
+PRECISIONS = [("fp32", "ieee"), ("fp32", "tf32"), ("bf16", "ieee")]
+SHAPES = [(1, 1024, 4096), (1, 3072, 1024), (7, 33, 65), (17, 129, 257), (100, 300, 70), (127, 255, 1000),
+          (512, 512, 512), (1000, 1000, 1000), (3, 5, 2)]
+
+
+def check(dev, M, N, K, dtype, prec, b_transposed):
+    torch.manual_seed(0)
+    a = torch.randn(M, K, device=dev, dtype=DTYPES[dtype])
+    if b_transposed:  # nn.Linear layout: weight [N, K], matmul uses weight.t()
+        b = torch.randn(N, K, device=dev, dtype=DTYPES[dtype]).t()
+    else:
+        b = torch.randn(K, N, device=dev, dtype=DTYPES[dtype])
+    c = matmul(a, b, input_precision=prec)
+    assert c.shape == (M, N) and c.dtype == a.dtype
+    rtol, atol = om.matmul_tolerance(dtype, prec, K)
+    torch.testing.assert_close(c.double(), om.matmul(a, b), rtol=rtol, atol=atol)
+    return a, b, c
+
+
+@pytest.mark.parametrize("M,N,K", SHAPES)
+@pytest.mark.parametrize("dtype,prec", PRECISIONS)
+@pytest.mark.parametrize("b_transposed", [False, True])
+def test_matmul(cuda, M, N, K, dtype, prec, b_transposed):
+    check(cuda, M, N, K, dtype, prec, b_transposed)
+
+
+def test_ieee_is_not_tf32(cuda):
+    torch.manual_seed(0)
+    a = torch.randn(256, 4096, device=cuda)
+    b = torch.randn(4096, 256, device=cuda)
+    ref = om.matmul(a, b)
+    err_ieee = (matmul(a, b, "ieee").double() - ref).abs().max().item()
+    err_tf32 = (matmul(a, b, "tf32").double() - ref).abs().max().item()
+    assert err_ieee < 1e-2 < err_tf32, (err_ieee, err_tf32)
+
+
+# A [M, K], B = randn(N, K).t() / sqrt(K)-scaled values.
+CONFIG4 = [(M, K, N) for M in (32, 2048, 4096) for K, N in ((1024, 4096), (1024, 6144), (3072, 1024), (4096, 4096))]
+
+
+@pytest.mark.parametrize("M,K,N", CONFIG4)
+@pytest.mark.parametrize("dtype,prec", PRECISIONS)
+def test_config4(cuda, M, K, N, dtype, prec):
+    g = torch.Generator(device=cuda).manual_seed(M + K + N)
+    s = 1 / math.sqrt(K)
+    a = (torch.randn(M, K, device=cuda, generator=g) * s).to(DTYPES[dtype])
+    b = (torch.randn(N, K, device=cuda, generator=g) * s).to(DTYPES[dtype]).t()
+    c = matmul(a, b, prec)
+    ref = om.matmul(a, b)
+    scale = ref.abs().max().item()
+    if dtype == "bf16":
+        torch.testing.assert_close(c.double(), ref, rtol=1.6e-2, atol=1e-2 * scale)
+    elif prec == "ieee":
+        torch.testing.assert_close(c.double(), ref, rtol=1e-3, atol=1e-5 * scale)
+    else:
+        # tf32 products are exact in fp32 accumulation terms; compare with the fp64 product of tf32 operands
+        ref_tf32 = om.matmul(om.tf32_round(a), om.tf32_round(b))
+        torch.testing.assert_close(c.double(), ref_tf32, rtol=1e-3, atol=1e-4 * scale)
+
+
+def test_zero_k(cuda):
+    a = torch.randn(5, 0, device=cuda)
+    b = torch.randn(0, 7, device=cuda)
+    assert torch.equal(matmul(a, b), torch.zeros(5, 7, device=cuda))
+
+
+def test_strided_operands(cuda):
+    """Both operands non-contiguous in both dims (every other row/column of a bigger buffer)."""
+    torch.manual_seed(1)
+    A = torch.randn(130, 2 * 96, device=cuda, dtype=torch.bfloat16)
+    B = torch.randn(2 * 96, 3 * 70, device=cuda, dtype=torch.bfloat16)
+    a, b = A[::2, ::2], B[::2, ::3]
+    c = matmul(a, b)
+    rtol, atol = om.matmul_tolerance("bf16", "ieee", 96)
+    torch.testing.assert_close(c.double(), om.matmul(a, b), rtol=rtol, atol=atol)

@@ -1,0 +1,288 @@
+"""Parity of nanovllm_b200's fused q/k RMSNorm + RoPE + paged KV write (nvb200_qk_norm_rope_kv) with the oracle.
+
+Mirrors the reference's tests/test_kernels_qk_rope_kv.py (same sizes, seeds style, slot pattern and checks):
+  norm stage   kernel run with an identity rotation table (cos = 1, sin = 0, all positions 0): its outputs are its
+               normed q and k; within MAX_ULP = 2 bf16 ulps of the oracle's RMSNorm (the sum-of-squares order
+               differs from torch's; the reference's own bound).
+  rope stage   the kernel's real output equals, bitwise, the oracle's rotary applied to the kernel's own normed q/k.
+  KV write     cache rows at kept slots equal k_out / v bitwise; every other row is untouched (slot -1 skipped).
+  end to end   within rtol 1.6e-2, atol 1e-2 of an all-fp32 computation (the north-star's bf16 tolerance).
+The oracle runs on CPU for these sizes; the full-size (T = 8192, Qwen3-8B) cases check the same properties with
+the oracle's torch ops run on the GPU.
+"""
+import pytest
+import torch
+
+from nanovllm_b200 import _lib, workloads
+from nanovllm_b200.kernels.qk_norm_rope_kv import qk_norm_rope_kv
+from oracle import reference_math as om
+
+pytestmark = pytest.mark.gpu
+
+MAX_ULP = 2
+TOKENS = [1, 7, 128, 4097]
+EPS = 1e-6
+D, MAX_POS, THETA, BLOCK = 128, 40960, 1e6, 256
+SHAPES = {"qwen3-0.6b": (16, 8), "qwen3-8b": (32, 8), "tp4-0.6b": (4, 2), "tp8-0.6b": (2, 1)}
+
+_tables = {}
+
+
+def table(dev, max_pos=MAX_POS):
+    key = (dev, max_pos)
+    if key not in _tables:
+        _tables[key] = om.rope_cos_sin_cache(D, max_pos, THETA).to(dev)
+    return _tables[key]
+
+
+def make_inputs(dev, tokens, random_positions, hq=16, hkv=8, seed_extra=0):
+    """The reference test's inputs (tests/test_kernels_qk_rope_kv.py:74-93): strided q/k/v views of a qkv output,
+    random or arange positions, distinct random slots of a 2T-slot cache with every 5th token -1, random cache."""
+    g = torch.Generator(device=dev).manual_seed(tokens * 2 + random_positions + 1000 * seed_extra)
+    q_w = (1 + 0.1 * torch.randn(D, device=dev, generator=g)).to(torch.bfloat16)
+    k_w = (1 + 0.1 * torch.randn(D, device=dev, generator=g)).to(torch.bfloat16)
+    qkv = torch.randn(tokens, (hq + 2 * hkv) * D, device=dev, generator=g).to(torch.bfloat16)
+    q, k, v = qkv.split([hq * D, hkv * D, hkv * D], dim=-1)
+    q, k, v = q.view(-1, hq, D), k.view(-1, hkv, D), v.view(-1, hkv, D)
+    if random_positions:
+        positions = torch.randint(0, MAX_POS, (tokens,), device=dev, generator=g)
+    else:
+        positions = torch.arange(tokens, device=dev)
+    num_blocks = (2 * tokens + BLOCK - 1) // BLOCK
+    slots = torch.randperm(num_blocks * BLOCK, device=dev, generator=g)[:tokens].to(torch.int32)
+    slots[4::5] = -1
+    cache = torch.randn(2, num_blocks, BLOCK, hkv, D, device=dev, generator=g).to(torch.bfloat16)
+    return dict(q_w=q_w, k_w=k_w, q=q, k=k, v=v, positions=positions, slots=slots, cache=cache, hkv=hkv)
+
+
+def identity_table(dev):
+    return torch.cat([torch.ones(D // 2), torch.zeros(D // 2)]).view(1, 1, D).to(dev)
+
+
+def run_fused(x, identity_rope=False, write_k=True):
+    cache = x["cache"].clone()
+    positions, cos_sin = x["positions"], table(x["q"].device)
+    if identity_rope:
+        positions = torch.zeros_like(positions)
+        cos_sin = identity_table(x["q"].device)
+    q_out, k_out = qk_norm_rope_kv(x["q"], x["k"], x["v"], positions, x["q_w"], x["k_w"], EPS, cos_sin, cache[0],
+                                   cache[1], x["slots"], write_k=write_k)
+    return dict(q=q_out, k_out=k_out, k_cache=cache[0], v_cache=cache[1])
+
+
+def cpu(t):
+    return t.detach().cpu()
+
+
+CASES = [(t, rp) for t in TOKENS for rp in (True, False)]
+IDS = [f"tokens={t}-{'random' if rp else 'arange'}" for t, rp in CASES]
+
+
+@pytest.mark.parametrize("shape", list(SHAPES))
+@pytest.mark.parametrize("tokens,random_positions", CASES, ids=IDS)
+def test_norm_stage(cuda, shape, tokens, random_positions):
+    hq, hkv = SHAPES[shape]
+    x = make_inputs(cuda, tokens, random_positions, hq, hkv)
+    normed = run_fused(x, identity_rope=True)
+    for name, out, w, inp in (("q", normed["q"], x["q_w"], x["q"]), ("k", normed["k_out"], x["k_w"], x["k"])):
+        ref = om.rms_forward(cpu(inp), cpu(w), EPS)
+        worst = int(om.bf16_ulp_diff(cpu(out), ref).max())
+        assert worst <= MAX_ULP, f"{name} norm: {worst} bf16 ulps from the oracle"
+
+
+@pytest.mark.parametrize("shape", list(SHAPES))
+@pytest.mark.parametrize("tokens,random_positions", CASES, ids=IDS)
+def test_rope_stage_bitwise(cuda, shape, tokens, random_positions):
+    hq, hkv = SHAPES[shape]
+    x = make_inputs(cuda, tokens, random_positions, hq, hkv)
+    normed, out = run_fused(x, identity_rope=True), run_fused(x)
+    qr, kr = om.rotary(cpu(x["positions"]), cpu(normed["q"]), cpu(normed["k_out"]), cpu(table(cuda)))
+    assert torch.equal(cpu(out["q"]), qr)
+    assert torch.equal(cpu(out["k_out"]), kr)
+
+
+@pytest.mark.parametrize("shape", list(SHAPES))
+@pytest.mark.parametrize("tokens,random_positions", CASES, ids=IDS)
+def test_kv_write(cuda, shape, tokens, random_positions):
+    hq, hkv = SHAPES[shape]
+    x = make_inputs(cuda, tokens, random_positions, hq, hkv)
+    out = run_fused(x)
+    check_kv_write(x, out, hkv)
+
+
+def check_kv_write(x, out, hkv):
+    slots = x["slots"]
+    real = slots >= 0
+    rows = slots[real].long()
+    assert torch.equal(out["k_cache"].view(-1, hkv, D)[rows], out["k_out"][real])
+    assert torch.equal(out["v_cache"].view(-1, hkv, D)[rows], x["v"][real])
+    untouched = torch.ones(x["cache"].shape[1] * BLOCK, dtype=torch.bool, device=slots.device)
+    untouched[rows] = False
+    for i, name in enumerate(("k_cache", "v_cache")):
+        before = x["cache"][i].view(-1, hkv, D)[untouched]
+        assert torch.equal(out[name].view(-1, hkv, D)[untouched], before), name
+
+
+def fp32_reference(x, positions, cos_sin):
+    """Everything in fp32 (no intermediate bf16 rounding): the north-star's tolerance reference."""
+    def norm(t, w):
+        t = t.float()
+        return t * torch.rsqrt(t.pow(2).mean(-1, keepdim=True) + EPS) * w.float()
+    cs = cos_sin[positions].view(-1, 1, D)
+    cos, sin = cs[..., :D // 2], cs[..., D // 2:]
+
+    def rot(t):
+        t1, t2 = t[..., :D // 2], t[..., D // 2:]
+        return torch.cat((t1 * cos - t2 * sin, t2 * cos + t1 * sin), -1)
+    return rot(norm(x["q"], x["q_w"])), rot(norm(x["k"], x["k_w"]))
+
+
+@pytest.mark.parametrize("shape", list(SHAPES))
+@pytest.mark.parametrize("tokens", [7, 4097])
+def test_end_to_end_within_bf16_tolerance(cuda, shape, tokens):
+    hq, hkv = SHAPES[shape]
+    x = make_inputs(cuda, tokens, True, hq, hkv)
+    out = run_fused(x)
+    rq, rk = fp32_reference(x, x["positions"], table(cuda))
+    torch.testing.assert_close(out["q"].float(), rq, rtol=1.6e-2, atol=1e-2)
+    torch.testing.assert_close(out["k_out"].float(), rk, rtol=1.6e-2, atol=1e-2)
+
+
+@pytest.mark.parametrize("case", ["fused_06b", "fused_8b"])
+def test_golden_fixture(cuda, case):
+    """Kernel on the fixture inputs vs the reference's own outputs (tests/golden/golden.pt)."""
+    import os
+    g = torch.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "golden.pt"))
+    c = g[case]
+    hq, hkv = c["hq"], c["hkv"]
+    qkv = c["qkv"].to(cuda)
+    q, k, v = qkv.split([hq * D, hkv * D, hkv * D], dim=-1)
+    q, k, v = q.view(-1, hq, D), k.view(-1, hkv, D), v.view(-1, hkv, D)
+    empty = torch.empty(0, device=cuda, dtype=torch.bfloat16)
+    q_out, k_out = qk_norm_rope_kv(q, k, v, c["positions"].to(cuda), c["q_w"].to(cuda), c["k_w"].to(cuda), g["eps"],
+                                   table(cuda, 4096), empty, empty, None, True)
+    for got, ref in ((q_out, c["q_out"]), (k_out, c["k_out"])):
+        torch.testing.assert_close(cpu(got).float(), ref.float(), rtol=1.6e-2, atol=1e-2)
+        assert (om.bf16_ulp_diff(cpu(got), ref) == 0).float().mean() > 0.9
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# Variants of the call: no cache, no k_out, T = 0, other head sizes, layouts that take the generic kernel.
+
+def test_empty_cache_stores_nothing(cuda):
+    x = make_inputs(cuda, 33, True)
+    empty = torch.empty(0, device=cuda, dtype=torch.bfloat16)
+    q_out, k_out = qk_norm_rope_kv(x["q"], x["k"], x["v"], x["positions"], x["q_w"], x["k_w"], EPS, table(cuda),
+                                   empty, empty, None, write_k=True)
+    ref_q, ref_k = om.qk_norm_rope_kv(cpu(x["q"]), cpu(x["k"]), cpu(x["v"]), cpu(x["positions"]), cpu(x["q_w"]),
+                                      cpu(x["k_w"]), EPS, cpu(table(cuda)), torch.empty(0), torch.empty(0), None,
+                                      True)
+    torch.testing.assert_close(cpu(q_out).float(), ref_q.float(), rtol=1.6e-2, atol=1e-2)
+    torch.testing.assert_close(cpu(k_out).float(), ref_k.float(), rtol=1.6e-2, atol=1e-2)
+
+
+def test_without_k_out(cuda):
+    x = make_inputs(cuda, 64, True)
+    a = run_fused(x, write_k=True)
+    b = run_fused(x, write_k=False)
+    assert b["k_out"] is None
+    assert torch.equal(a["q"], b["q"]) and torch.equal(a["k_cache"], b["k_cache"])
+    assert torch.equal(a["v_cache"], b["v_cache"])
+
+
+def test_zero_tokens(cuda):
+    x = make_inputs(cuda, 1, True)
+    q = x["q"][:0]
+    q_out, k_out = qk_norm_rope_kv(q, x["k"][:0], x["v"][:0], x["positions"][:0], x["q_w"], x["k_w"], EPS,
+                                   table(cuda), x["cache"][0], x["cache"][1], x["slots"][:0], True)
+    assert q_out.shape == (0, 16, D) and k_out.shape == (0, 8, D)
+
+
+@pytest.mark.parametrize("head_dim", [64, 256, 96])
+def test_other_head_dims(cuda, head_dim):
+    """D = 64 and 256 take the bulk kernel with 4 / 16 lanes per head; D = 96 the generic kernel."""
+    g = torch.Generator(device=cuda).manual_seed(head_dim)
+    T, hq, hkv = 37, 8, 2
+    qkv = torch.randn(T, (hq + 2 * hkv) * head_dim, device=cuda, generator=g).to(torch.bfloat16)
+    q, k, v = qkv.split([hq * head_dim, hkv * head_dim, hkv * head_dim], dim=-1)
+    q, k, v = q.view(T, hq, head_dim), k.view(T, hkv, head_dim), v.view(T, hkv, head_dim)
+    w = (1 + 0.1 * torch.randn(2, head_dim, device=cuda, generator=g)).to(torch.bfloat16)
+    tab = om.rope_cos_sin_cache(head_dim, 512, 1e4).to(cuda)
+    pos = torch.randint(0, 512, (T,), device=cuda, generator=g)
+    kc = torch.randn(1, 128, hkv, head_dim, device=cuda, generator=g).to(torch.bfloat16)
+    vc = torch.randn_like(kc)
+    slots = torch.randperm(128, device=cuda, generator=g)[:T].to(torch.int32)
+    slots[::3] = -1
+    kc2, vc2 = kc.clone(), vc.clone()
+    q_out, k_out = qk_norm_rope_kv(q, k, v, pos, w[0].contiguous(), w[1].contiguous(), EPS, tab, kc, vc, slots, True)
+    rq, rk = om.qk_norm_rope_kv(cpu(q), cpu(k), cpu(v), cpu(pos), cpu(w[0]), cpu(w[1]), EPS, cpu(tab), kc2.cpu(),
+                                vc2.cpu(), cpu(slots), True)
+    torch.testing.assert_close(cpu(q_out).float(), rq.float(), rtol=1.6e-2, atol=1e-2)
+    torch.testing.assert_close(cpu(k_out).float(), rk.float(), rtol=1.6e-2, atol=1e-2)
+    keep = slots >= 0
+    assert torch.equal(kc.view(-1, hkv, head_dim)[slots[keep].long()], k_out[keep])
+    assert torch.equal(vc.view(-1, hkv, head_dim)[slots[keep].long()], v[keep])
+
+
+def test_unaligned_token_stride_takes_generic_kernel(cuda):
+    """A qkv buffer whose row stride is not a multiple of 8 elements cannot be moved by the bulk engine; the
+    generic kernel must give the same bits as the bulk kernel's math allows (norm within 2 ulp, rope bitwise)."""
+    T, hq, hkv = 50, 16, 8
+    g = torch.Generator(device=cuda).manual_seed(7)
+    wide = torch.randn(T, (hq + 2 * hkv) * D + 3, device=cuda, generator=g).to(torch.bfloat16)
+    qkv = wide[:, 3:]
+    q, k, v = qkv.split([hq * D, hkv * D, hkv * D], dim=-1)
+    x = make_inputs(cuda, T, True)
+    x.update(q=q.view(T, hq, D), k=k.view(T, hkv, D), v=v.view(T, hkv, D))
+    normed, out = run_fused(x, identity_rope=True), run_fused(x)
+    for name, o, w, inp in (("q", normed["q"], x["q_w"], x["q"]), ("k", normed["k_out"], x["k_w"], x["k"])):
+        assert int(om.bf16_ulp_diff(cpu(o), om.rms_forward(cpu(inp), cpu(w), EPS)).max()) <= MAX_ULP, name
+    qr, kr = om.rotary(cpu(x["positions"]), cpu(normed["q"]), cpu(normed["k_out"]), cpu(table(cuda)))
+    assert torch.equal(cpu(out["q"]), qr) and torch.equal(cpu(out["k_out"]), kr)
+    check_kv_write(x, out, hkv)
+
+
+def test_out_of_range_indices_are_flagged_not_written(cuda):
+    """Slots past the cache and positions past the table are skipped (no fault) and reported in the status word."""
+    x = make_inputs(cuda, 16, True)
+    _lib.status(cuda, clear=True)
+    n_slots = x["cache"].shape[1] * BLOCK
+    bad = x["slots"].clone()
+    bad[3] = n_slots + 5  # past the end: must not be written
+    x2 = dict(x, slots=bad)
+    out = run_fused(x2)
+    assert _lib.status(cuda, clear=True) & _lib.STATUS_BAD_SLOT
+    ref = run_fused(dict(x, slots=torch.where(torch.arange(16, device=cuda) == 3, -1, x["slots"])))
+    assert torch.equal(out["k_cache"], ref["k_cache"]) and torch.equal(out["v_cache"], ref["v_cache"])
+    pos = x["positions"].clone()
+    pos[0] = MAX_POS + 1
+    run_fused(dict(x, positions=pos))
+    assert _lib.status(cuda, clear=True) & _lib.STATUS_BAD_POSITION
+    run_fused(x)
+    assert _lib.status(cuda) == 0
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# Full size (BASELINE config 3 at T = 8192, Qwen3-8B: 32 q / 8 kv heads, cache [1024, 256, 8, 128]): properties.
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_full_size_properties(cuda, world):
+    x = workloads.fused_inputs(8192, 32, 8, max_pos=32768, num_blocks=1024, device=cuda, seed=3,
+                               cache_fill="randn")
+    xs = workloads.shard_kv_heads(x, world - 1, world)  # the last rank's shard
+    hkv = xs["k"].shape[1]
+    cache = torch.stack([xs["k_cache"], xs["v_cache"]])
+    before = cache.clone()
+    q_out, k_out = qk_norm_rope_kv(xs["q"], xs["k"], xs["v"], xs["positions"], xs["q_w"], xs["k_w"], xs["eps"],
+                                   xs["cos_sin"], cache[0], cache[1], xs["slots"], True)
+    ident = identity_table(cuda)
+    nq, nk = qk_norm_rope_kv(xs["q"], xs["k"], xs["v"], torch.zeros_like(xs["positions"]), xs["q_w"], xs["k_w"],
+                             xs["eps"], ident, torch.empty(0, device=cuda), torch.empty(0, device=cuda), None, True)
+    # norm stage vs the oracle's RMSNorm (torch ops on the GPU at this size)
+    assert int(om.bf16_ulp_diff(nq, om.rms_forward(xs["q"], xs["q_w"], xs["eps"])).max()) <= MAX_ULP
+    assert int(om.bf16_ulp_diff(nk, om.rms_forward(xs["k"], xs["k_w"], xs["eps"])).max()) <= MAX_ULP
+    # rope stage bitwise
+    rq, rk = om.rotary(xs["positions"], nq, nk, xs["cos_sin"])
+    assert torch.equal(q_out, rq) and torch.equal(k_out, rk)
+    # exact slot placement and untouched slots
+    check_kv_write(dict(xs, cache=before), dict(k_cache=cache[0], v_cache=cache[1], k_out=k_out), hkv)
