@@ -10,8 +10,8 @@ Multi-GPU: sharded by KV head as nano-vllm's tensor parallelism lays it out (ran
 [r*8/N, (r+1)*8/N) and the q heads sharing them, and that slice of the cache); no collective on the data path.
 Weak scaling: the batch is 8192 * N tokens, so each rank moves the same bytes as the one-GPU run.
 
-A step is one kernel launch over one batch. Between steps an L2 flush (a 256 MiB write) runs outside the timed
-events; `value` = all ranks' algorithmic bytes / max over ranks of the summed CUDA-event kernel times.
+A step is one kernel launch over one batch. Between steps an L2 flush (a 256 MiB write, then a 256 MiB read of
+another buffer so no dirty lines are left to write back) runs outside the timed events; `value` = all ranks' algorithmic bytes / max over ranks of the summed CUDA-event kernel times.
 `e2e` = the same metric through the public Python API (nanovllm_b200.kernels.qk_norm_rope_kv) with the step's
 inputs (qkv, positions, slots) copied from pinned host memory and q_out copied back inside the timed region.
 `cpu_baseline` / `--impl reference`: the reference's torch implementation restated in oracle/ (bitwise equal to
@@ -250,7 +250,7 @@ def fused_workload(args, rank, world, dev, hq_total, hkv_total, max_pos, num_blo
                         "kv_heads_per_gpu": hkv, "cache_blocks": blocks, "block_size": 256,
                         "max_position": max_pos, "skip_fraction": 0.05, "write_k": False,
                         "parallelism": f"tp{world} (KV-head sharding, no collective)",
-                        "l2": "flushed between timed steps (256 MiB write outside the events)",
+                        "l2": "flushed between timed steps (256 MiB write + 256 MiB read, outside the events)",
                         "bytes_formula": "T*((Hq+2Hkv)*D*2 read + 8 + 4 + D*4 + (Hq+2Hkv)*D*2 written) + 2*D*2"})
 
 
@@ -387,12 +387,19 @@ def main():
     torch.backends.cuda.matmul.allow_tf32 = False
     peaks, peak_kind = load_peaks()
     wl = make_workload(args, rank, world, dev)
-    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    flush_w = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    flush_r = torch.ones(L2_FLUSH_BYTES // 4, dtype=torch.int32, device=dev)
     stream = torch.cuda.current_stream(dev)
+
+    def flush_l2():
+        # Write 256 MiB (evicts the step's lines), then read another 256 MiB so that the dirty lines of that
+        # write are written back here, not during the timed kernel.
+        flush_w.zero_()
+        flush_r.max()
 
     with torch.inference_mode():
         for _ in range(args.warmup):
-            flush.zero_()
+            flush_l2()
             wl["launch"]()
         torch.cuda.synchronize()
         starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
@@ -401,7 +408,7 @@ def main():
         with ClockSampler(local) as clocks:
             clocks.mark_start()
             for i in range(args.steps):
-                flush.zero_()
+                flush_l2()
                 starts[i].record(stream)
                 wl["launch"]()
                 ends[i].record(stream)

@@ -7,10 +7,11 @@
 // Design (bulk path, used whenever every row is 16-byte aligned, i.e. always for qkv_proj views):
 //   * Work unit = one token x a group of G kv heads and the G*R q heads that share them (GQA, R = Hq/Hkv).
 //     Large batches use G = Hkv (one unit per token); small batches split heads so that every SM gets work.
-//   * One persistent CTA per SM owns a contiguous range of units. Warp 0 is the producer: it prefetches 32
+//   * Two persistent CTAs per SM each own a contiguous range of units (one CTA per SM measured 30 % slower: a
+//     single producer cannot keep enough copies in flight). Warp 0 is the producer: it prefetches 32
 //     positions/slots at a time with one coalesced load and moves each unit's q rows, k rows, v rows (only when
 //     the slot is kept) and cos/sin row from HBM into a shared-memory stage with 1-D bulk copies
-//     (cp.async.bulk, completion counted on an mbarrier). Up to 16 stages are in flight per SM.
+//     (cp.async.bulk, completion counted on an mbarrier). Up to 8 stages are in flight per CTA.
 //   * Consumer warps (8) take units round robin. A warp normalises and rotates 32/LPH heads per step in place in
 //     shared memory, each lane holding 8 elements of the first half and the matching 8 of the second half
 //     (LPH = D/16 lanes per head), so RoPE pairs are lane-local and the sum of squares needs log2(LPH) shuffles.
@@ -25,11 +26,30 @@
 namespace nvb200 {
 namespace {
 
-constexpr int kConsumerWarps = 8;
+// Tuning constants (the defaults were chosen by measurement on B200; a build may override them with -D).
+#ifndef NVB200_QKNR_CONSUMERS
+#define NVB200_QKNR_CONSUMERS 8
+#endif
+#ifndef NVB200_QKNR_MAX_STAGES
+#define NVB200_QKNR_MAX_STAGES 8
+#endif
+#ifndef NVB200_QKNR_CTAS_PER_SM
+#define NVB200_QKNR_CTAS_PER_SM 2
+#endif
+#ifndef NVB200_QKNR_SMEM_BUDGET_KB
+#define NVB200_QKNR_SMEM_BUDGET_KB (200 / NVB200_QKNR_CTAS_PER_SM)
+#endif
+#ifndef NVB200_QKNR_DEFER_RELEASE
+#define NVB200_QKNR_DEFER_RELEASE 0
+#endif
+
+constexpr int kConsumerWarps = NVB200_QKNR_CONSUMERS;
 constexpr int kThreads = 32 * (1 + kConsumerWarps);
-constexpr int kMaxStages = 16;
-constexpr int kSmemBudget = 200 * 1024;  // stage bytes per CTA (1 CTA per SM)
-constexpr int kHeaderBytes = 512;        // mbarriers and per-stage slot numbers
+constexpr int kMaxStages = NVB200_QKNR_MAX_STAGES;
+constexpr int kCtasPerSm = NVB200_QKNR_CTAS_PER_SM;
+constexpr int kSmemBudget = NVB200_QKNR_SMEM_BUDGET_KB * 1024;  // stage bytes per CTA
+constexpr int kHeaderBytes = 512;                                   // mbarriers and per-stage slot numbers
+static_assert(2 * 8 * kMaxStages + 4 * kMaxStages <= kHeaderBytes, "header too small");
 
 struct QknrParams {
   __nv_bfloat16 *q_out;
@@ -91,7 +111,7 @@ NVB200_DEVICE void load_w8(const __nv_bfloat16 *p, uint32_t (&w)[4]) {
 // Bulk-copy pipeline kernel. D in {64, 128, 256}.
 
 template <int D>
-__global__ void __launch_bounds__(kThreads, 1) qknr_bulk_kernel(const __grid_constant__ QknrParams p) {
+__global__ void __launch_bounds__(kThreads, kCtasPerSm) qknr_bulk_kernel(const __grid_constant__ QknrParams p) {
   constexpr int HALF = D / 2;
   constexpr int LPH = D / 16;    // lanes per head: each lane holds 8 + 8 elements
   constexpr int HPI = 32 / LPH;  // heads per warp step
@@ -185,6 +205,10 @@ __global__ void __launch_bounds__(kThreads, 1) qknr_bulk_kernel(const __grid_con
   load_w8(p.k_w + 8 * j, wk1);
   load_w8(p.k_w + HALF + 8 * j, wk2);
   const int total = nq + p.g;
+  // Deferred release: a stage is handed back one unit later, once its bulk stores have read it, so the warp does
+  // not wait for that read. Needs more stages than consumer warps (each warp then holds at most two).
+  const bool defer = NVB200_QKNR_DEFER_RELEASE && NS > kConsumerWarps;
+  int pending_empty = -1;  // stage whose release waits for its bulk stores to finish reading shared memory
 
   for (int it = cw; it < n_units; it += kConsumerWarps) {
     const int st = it % NS;
@@ -251,12 +275,22 @@ __global__ void __launch_bounds__(kThreads, 1) qknr_bulk_kernel(const __grid_con
         bulk_s2g(p.v_cache + off, sv, kb);
       }
       bulk_commit();
-      bulk_wait_read<0>();
-      mbar_arrive(empty);
+      if (defer) {
+        bulk_wait_read<1>();  // the previous unit's stores have read their stage
+        if (pending_empty >= 0) mbar_arrive(pending_empty);
+        pending_empty = static_cast<int>(empty);
+      } else {
+        bulk_wait_read<0>();
+        mbar_arrive(empty);
+      }
     }
     __syncwarp();
   }
-  if (lane == 0) bulk_wait<0>();
+  if (lane == 0) {
+    bulk_wait_read<0>();
+    if (pending_empty >= 0) mbar_arrive(pending_empty);
+    bulk_wait<0>();
+  }
 }
 
 // ---------------------------------------------------------------------------------------------------------------
@@ -356,7 +390,7 @@ int launch_bulk(QknrParams &p, int sms, cudaStream_t stream) {
       return NVB200_ERR_CUDA;
     configured[dev] = 1;
   }
-  const int64_t grid = std::min<int64_t>(p.units, sms);
+  const int64_t grid = std::min<int64_t>(p.units, static_cast<int64_t>(sms) * kCtasPerSm);
   p.chunk = (p.units + grid - 1) / grid;
   const int64_t blocks = (p.units + p.chunk - 1) / p.chunk;
   qknr_bulk_kernel<D><<<static_cast<unsigned>(blocks), kThreads, smem, stream>>>(p);

@@ -10,7 +10,8 @@ import threading
 
 import torch
 
-LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libnvb200.so")
+# NVB200_LIBRARY may name another build of the same library (e.g. one compiled with different tile constants).
+LIB_PATH = os.environ.get("NVB200_LIBRARY") or os.path.join(os.path.dirname(os.path.abspath(__file__)), "libnvb200.so")
 
 # Return codes and dtype codes of nvb200.h.
 OK, ERR_ARG, ERR_UNSUPPORTED, ERR_CUDA, ERR_NO_DEVICE = 0, 1, 2, 3, 4

@@ -140,12 +140,25 @@ def fp32_reference(x, positions, cos_sin):
 @pytest.mark.parametrize("shape", list(SHAPES))
 @pytest.mark.parametrize("tokens", [7, 4097])
 def test_end_to_end_within_bf16_tolerance(cuda, shape, tokens):
+    """Values within rtol 1.6e-2 / atol 1e-2 of the oracle (the reference's implementation), and no further from an
+    all-fp32 computation than the oracle itself is. The reference rounds the normed head to bf16 before RoPE
+    (layers/layernorm.py:29), which alone moves a near-cancelling RoPE output by up to ~0.02 from the all-fp32
+    value; against fp32 the kernel must do as well as the oracle: no more elements outside the tolerance (x2 for
+    rounding-boundary noise) and a largest deviation within 1.5x of the oracle's."""
     hq, hkv = SHAPES[shape]
     x = make_inputs(cuda, tokens, True, hq, hkv)
     out = run_fused(x)
+    oq, ok = om.qk_norm_rope_kv(cpu(x["q"]), cpu(x["k"]), cpu(x["v"]), cpu(x["positions"]), cpu(x["q_w"]),
+                                cpu(x["k_w"]), EPS, cpu(table(cuda)), torch.empty(0), torch.empty(0), None, True)
+    torch.testing.assert_close(cpu(out["q"]).float(), oq.float(), rtol=1.6e-2, atol=1e-2)
+    torch.testing.assert_close(cpu(out["k_out"]).float(), ok.float(), rtol=1.6e-2, atol=1e-2)
     rq, rk = fp32_reference(x, x["positions"], table(cuda))
-    torch.testing.assert_close(out["q"].float(), rq, rtol=1.6e-2, atol=1e-2)
-    torch.testing.assert_close(out["k_out"].float(), rk, rtol=1.6e-2, atol=1e-2)
+    for got, ora, ref in ((out["q"], oq, rq), (out["k_out"], ok, rk)):
+        got, ora, ref = cpu(got).float(), ora.float(), cpu(ref)
+        bad_got = ((got - ref).abs() > 1e-2 + 1.6e-2 * ref.abs()).float().mean().item()
+        bad_ora = ((ora - ref).abs() > 1e-2 + 1.6e-2 * ref.abs()).float().mean().item()
+        assert bad_got <= 2 * bad_ora + 1e-5, (bad_got, bad_ora)
+        assert (got - ref).abs().max() <= 1.5 * (ora - ref).abs().max() + 1e-3
 
 
 @pytest.mark.parametrize("case", ["fused_06b", "fused_8b"])
