@@ -46,7 +46,11 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", default="fused8b", choices=["fused8b", "fused06b", "norm", "matmul"])
+    ap.add_argument("--workload", default="fused8b", choices=["fused8b", "fused06b", "norm", "matmul", "decode"])
+    ap.add_argument("--decode-worker", default=None, help=argparse.SUPPRESS)
+    ap.add_argument("--decode-backends", default="b200,compile,triton_fused")
+    ap.add_argument("--decode-batch", type=int, default=32)
+    ap.add_argument("--decode-ctx", type=int, default=1024)
     ap.add_argument("--tokens", type=int, default=8192, help="tokens per step at N = 1")
     ap.add_argument("--scaling", choices=["weak", "strong"], default="weak")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -373,8 +377,112 @@ def run_reference_arm(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------------------------------------------------------
+# one decode step of a Qwen3-0.6B-architecture model (28 layers, hidden 1024, 16 q / 8 kv heads,
+# head_dim 128, intermediate 3072, vocab 151936), random bf16 weights, batch 32 x 1024 tokens of context in the paged
+# cache (N(0,1)), whole-step CUDA graph replay, timed as the reference's scripts/bench_decode.py:82-95 times it
+# (CUDA events around 50 replays of graphs[("target", 1, bs)], median of 3). The reference's own ModelRunner builds
+# and captures the model (offline install of the reference in baseline/_ref); kernel_backend "b200" runs it on
+# nanovllm_b200 through nanovllm_b200.install(), "compile" / "triton_fused" are the reference's own backends.
+# Each backend runs in its own process (ModelRunner takes most of the GPU memory for its KV cache).
+
+QWEN3_06B = {"architectures": ["Qwen3ForCausalLM"], "model_type": "qwen3", "hidden_size": 1024,
+             "intermediate_size": 3072, "num_hidden_layers": 28, "num_attention_heads": 16, "num_key_value_heads": 8,
+             "head_dim": 128, "vocab_size": 151936, "max_position_embeddings": 40960, "rms_norm_eps": 1e-6,
+             "rope_theta": 1000000, "tie_word_embeddings": True, "torch_dtype": "bfloat16", "dtype": "bfloat16",
+             "hidden_act": "silu", "attention_bias": False}
+
+
+def decode_worker(backend: str, bs: int, ctx: int) -> dict:
+    import tempfile
+    ref = os.path.join(ROOT, "baseline", "_ref")
+    sys.path.insert(0, ref)
+    import nanovllm_b200
+    nanovllm_b200.install()
+    import nanovllm.engine.model_runner as mr
+    from nanovllm.config import Config
+
+    def random_weights(model, path):  # no checkpoint: random-init every parameter (norm weights around 1)
+        g = torch.Generator(device="cuda").manual_seed(0)
+        with torch.no_grad():
+            for name, p in model.named_parameters():
+                if name.endswith("norm.weight"):
+                    p.copy_(1 + 0.1 * torch.randn(p.shape, generator=g, device=p.device))
+                else:
+                    p.copy_(0.02 * torch.randn(p.shape, generator=g, device=p.device))
+    mr.load_model = random_weights
+    d = tempfile.mkdtemp()
+    with open(os.path.join(d, "config.json"), "w") as f:
+        json.dump(QWEN3_06B, f)
+    cfg = Config(d, kernel_backend=backend, max_num_seqs=bs, max_model_len=2048, max_num_batched_tokens=4096,
+                 gpu_memory_utilization=0.5)
+    runner = mr.ModelRunner(cfg, 0, [])
+    blocks_per_seq = (ctx + 1 + 255) // 256
+    assert cfg.num_kvcache_blocks >= bs * blocks_per_seq
+    g = torch.Generator(device="cuda").manual_seed(1)
+    runner.kv_caches["target"].normal_(generator=g)
+    gv = runner.graph_vars
+    gv["input_ids"][:bs] = torch.randint(0, QWEN3_06B["vocab_size"], (bs,), device="cuda", generator=g)
+    gv["positions"][:bs] = ctx
+    tables = torch.arange(bs * blocks_per_seq, dtype=torch.int32, device="cuda").view(bs, blocks_per_seq)
+    gv["block_tables"].zero_()
+    gv["block_tables"][:bs, :blocks_per_seq] = tables
+    gv["slot_mapping"].fill_(-1)
+    gv["slot_mapping"][:bs] = tables[:, ctx // 256] * 256 + ctx % 256
+    gv["context_lens"].zero_()
+    gv["context_lens"][:bs] = ctx + 1
+    graph = runner.graphs[("target", 1, bs)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for _ in range(10):
+        graph.replay()
+    per_run = []
+    for _ in range(3):
+        start.record()
+        for _ in range(50):
+            graph.replay()
+        end.record()
+        end.synchronize()
+        per_run.append(start.elapsed_time(end) / 50)
+    out = gv["outputs"]["target"][:bs].float()
+    res = {"backend": backend, "graph_replay_us": 1e3 * sorted(per_run)[1], "runs_us": [1e3 * x for x in per_run],
+           "finite": bool(torch.isfinite(out).all()), "kv_blocks": cfg.num_kvcache_blocks}
+    try:
+        runner.exit()
+    except Exception:
+        pass
+    return res
+
+
+def run_decode(args) -> None:
+    results = {}
+    for backend in args.decode_backends.split(","):
+        cmd = [sys.executable, os.path.abspath(__file__), "--decode-worker", backend, "--decode-batch",
+               str(args.decode_batch), "--decode-ctx", str(args.decode_ctx)]
+        out = subprocess.run(cmd, capture_output=True, text=True)
+        lines = [ln for ln in out.stdout.splitlines() if ln.startswith("{")]
+        if out.returncode == 0 and lines:
+            results[backend] = json.loads(lines[-1])
+        else:
+            results[backend] = {"backend": backend, "error": (out.stderr or out.stdout)[-800:]}
+    ours = results.get("b200", {})
+    line = {"metric": "decode-step graph replay us (Qwen3-0.6B arch, batch 32, ctx 1024)",
+            "value": ours.get("graph_replay_us"), "unit": "us", "n_gpus": 1, "steps": 150, "warmup": 10,
+            "ms_per_step": (ours.get("graph_replay_us") or 0) / 1e3, "higher_is_better": False, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (random-init weights, N(0,1) KV cache)",
+            "config": {"workload": "decode", "model": "Qwen3-0.6B architecture", "batch": args.decode_batch,
+                       "context": args.decode_ctx, "parallelism": "tp1", "graph": "whole-step CUDA graph"},
+            "backends": results}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse_args()
+    if args.decode_worker:
+        print(json.dumps(decode_worker(args.decode_worker, args.decode_batch, args.decode_ctx)), flush=True)
+        return
+    if args.workload == "decode":
+        run_decode(args)
+        return
     rank, world, local = setup_dist(args)
     if args.impl == "reference":
         run_reference_arm(args, rank, world)

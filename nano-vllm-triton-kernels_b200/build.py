@@ -69,7 +69,7 @@ def build(force: bool = False, verbose: bool = False) -> str:
                 fut.result()
     if jobs or not os.path.exists(LIB) or os.path.getmtime(LIB) < max(os.path.getmtime(o) for o in objs):
         tmp = LIB + ".tmp"
-        cmd = [nvcc(), *ARCH, "-shared", "-o", tmp, *objs, "-lcuda"]
+        cmd = [nvcc(), *ARCH, "-shared", "-o", tmp, *objs]
         res = subprocess.run(cmd, capture_output=True, text=True)
         if res.returncode != 0:
             sys.stderr.write(res.stdout + res.stderr)

@@ -1,12 +1,423 @@
-// tcgen05 (5th-generation tensor core) matmul for sm_100a: placeholder until the TMA/TMEM pipeline lands; every
-// call is routed to the SIMT kernel of matmul.cu.
+// tcgen05 (5th-generation tensor core) matmul for sm_100a: C[M, N] = A[M, K] @ B[K, N], fp32 accumulation in TMEM.
+//
+// Behaviour follows nanovllm/kernels/matmul.py:33-81 (tiles in GROUP_M-swizzled order, K tail zero-filled, masked
+// M/N edges); the machinery is Blackwell's:
+//   * Persistent kernel, one CTA per SM, 128 x BN output tiles (BN = 256, or 128 when that gives more tiles per SM).
+//   * Warp 0 (one elected lane) moves A and B tiles HBM -> shared memory with TMA (cp.async.bulk.tensor, 128-byte
+//     swizzle) into a 4-stage ring; completion is counted on mbarriers.
+//   * Warp 1 (one elected lane) issues tcgen05.mma (kind::f16 for bf16, kind::tf32 for fp32) from the shared-memory
+//     descriptors into a TMEM accumulator, and tcgen05.commit releases each stage when its MMAs are done. Two TMEM
+//     accumulators (2 x BN columns) let the epilogue of one tile overlap the MMAs of the next.
+//   * Warps 2-5 (the epilogue) read the accumulator with tcgen05.ld (each warp its 32-lane quarter), round to C's
+//     dtype and store.
+// Operand layouts: A and B may each be K-major (the contiguous dim is K: A row-major, B = weight.t()) or MN-major
+// (B row-major [K, N], A column-major); the instruction descriptor's major bits select it, so no transpose pass.
+// Any layout TMA cannot describe (a non-unit inner stride, or a row pitch that is not a multiple of 16 bytes) is
+// reported as unsupported and the caller runs the SIMT kernel instead.
+// No TMA multicast is used anywhere (this code may run in multi-GPU jobs).
+#include <algorithm>
+#include <cudaTypedefs.h>
+
 #include "common.cuh"
 
 namespace nvb200 {
+namespace {
 
-int matmul_tc_launch(void *, const void *, const void *, int64_t, int64_t, int64_t, int64_t, int64_t, int64_t,
-                     int64_t, int64_t, int64_t, int, int32_t *, cudaStream_t) {
-  return NVB200_ERR_UNSUPPORTED;
+constexpr int BM = 128;
+constexpr int kStages = 4;
+constexpr int kEpilogueWarps = 4;
+constexpr int kThreads = 32 * (2 + kEpilogueWarps);
+constexpr int kGroupM = 8;
+constexpr int kTileBytesA = BM * 128;  // one 128-byte swizzle row per M row (BK * elem = 128 B)
+
+struct TcParams {
+  void *c;
+  int64_t scm, scn;
+  int M, N, K;
+  int bn;          // tile N (256 or 128)
+  int tiles_m, tiles_n;
+  int k_blocks;    // ceil(K / BK)
+  uint32_t idesc;  // tcgen05 instruction descriptor
+  int a_mn_major, b_mn_major;
+  int elem_bytes;  // 2 (bf16) or 4 (fp32/tf32)
+  int c_is_f32;
+  int32_t *status;
+};
+
+// ---------------------------------------------------------------------------------------------------------------
+// PTX wrappers for TMA tensor loads, tcgen05 and TMEM.
+
+NVB200_DEVICE void tma_load_2d(uint32_t dst, const CUtensorMap *map, int c0, int c1, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+      ::"r"(dst), "l"(map), "r"(c0), "r"(c1), "r"(bar)
+      : "memory");
+}
+
+NVB200_DEVICE void prefetch_tmap(const CUtensorMap *map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
+}
+
+NVB200_DEVICE void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+NVB200_DEVICE void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+NVB200_DEVICE void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+NVB200_DEVICE void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+template <bool TF32>
+NVB200_DEVICE void tc_mma(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
+  if (TF32) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+  }
+}
+
+// Arrives on `bar` once every tcgen05.mma this thread issued so far has completed.
+NVB200_DEVICE void tc_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+               : "memory");
+}
+
+// 32 consecutive fp32 columns of this thread's TMEM lane.
+NVB200_DEVICE void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Shared-memory matrix descriptor, 128-byte swizzle (layout type 2), sm100 version bits = 1.
+NVB200_DEVICE uint64_t smem_desc(uint32_t addr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((addr >> 4) & 0x3FFF);
+  d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFF) << 16;
+  d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFF) << 32;
+  d |= 1ull << 46;
+  d |= 2ull << 61;
+  return d;
+}
+
+// GROUP_M-swizzled tile order (nanovllm/kernels/matmul.py:50-57).
+NVB200_DEVICE void tile_coords(int tile, int tiles_m, int tiles_n, int &pm, int &pn) {
+  const int in_group = kGroupM * tiles_n;
+  const int first_m = (tile / in_group) * kGroupM;
+  const int group_m = min(tiles_m - first_m, kGroupM);
+  pm = first_m + (tile % in_group) % group_m;
+  pn = (tile % in_group) / group_m;
+}
+
+// Stage layout (each operand tile 1024-byte aligned, as the 128-byte swizzle requires):
+//   A: BM x BK, K-major: row m at m * 128 B.            MN-major: BK rows of 128 B per 128-byte MN block.
+//   B: BN x BK, K-major: row n at n * 128 B.            MN-major: BK rows of 128 B per 128-byte MN block.
+// BK = 128 / elem_bytes (64 bf16, 32 tf32). One MMA consumes UK = 32 / elem_bytes of K (16 bf16, 8 tf32).
+template <bool TF32>
+__global__ void __launch_bounds__(kThreads, 1)
+    matmul_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                     const __grid_constant__ TcParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int tile_b_bytes = p.bn * 128;
+  const int stage_bytes = kTileBytesA + tile_b_bytes;
+  uint8_t *hdr = smem + kStages * stage_bytes;
+  const uint32_t bar_full = smem_addr(hdr);            // kStages x 8
+  const uint32_t bar_empty = bar_full + 8 * kStages;   // kStages x 8
+  const uint32_t bar_acc_full = bar_empty + 8 * kStages;  // 2 x 8
+  const uint32_t bar_acc_empty = bar_acc_full + 16;        // 2 x 8
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(hdr + 8 * (2 * kStages + 4));
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(hdr + 8 * (2 * kStages + 4) + 4);
+  const uint32_t stage0 = smem_addr(smem);
+  const int BK = 128 / p.elem_bytes;
+  const int UK = 32 / p.elem_bytes;
+  const int num_tiles = p.tiles_m * p.tiles_n;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(bar_full + 8 * i, 1);
+      mbar_init(bar_empty + 8 * i, 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(bar_acc_full + 8 * i, 1);
+      mbar_init(bar_acc_empty + 8 * i, kEpilogueWarps);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+    prefetch_tmap(&map_a);
+    prefetch_tmap(&map_b);
+  }
+  if (warp == 1) tmem_alloc(smem_addr(tmem_slot), 2 * p.bn <= 256 ? 256 : 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA producer
+    if (lane == 0) {
+      int it = 0;
+      for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
+        int pm, pn;
+        tile_coords(tile, p.tiles_m, p.tiles_n, pm, pn);
+        const int m0 = pm * BM, n0 = pn * p.bn;
+        for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
+          const int st = it % kStages;
+          const uint32_t ph = (it / kStages) & 1;
+          if (!mbar_wait_bounded(bar_empty + 8 * st, ph ^ 1)) {
+            set_status(p.status, NVB200_STATUS_WAIT_TIMEOUT);
+            *abort_flag = 1;
+            break;
+          }
+          const uint32_t sa = stage0 + st * stage_bytes, sb = sa + kTileBytesA;
+          const uint32_t full = bar_full + 8 * st;
+          mbar_arrive_expect_tx(full, stage_bytes);
+          const int k0 = kb * BK;
+          if (p.a_mn_major) {  // A^T stored [K][M]: boxes of 128 B along M, BK rows
+            for (int j = 0; j < BM / BK; ++j) tma_load_2d(sa + j * BK * 128, &map_a, m0 + j * BK, k0, full);
+          } else {
+            tma_load_2d(sa, &map_a, k0, m0, full);
+          }
+          if (p.b_mn_major) {  // B stored [K][N]: boxes of 128 B along N, BK rows
+            for (int j = 0; j < p.bn / BK; ++j) tma_load_2d(sb + j * BK * 128, &map_b, n0 + j * BK, k0, full);
+          } else {
+            tma_load_2d(sb, &map_b, k0, n0, full);
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    int it = 0, local = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+      const int buf = local & 1;
+      const uint32_t acc_ph = (local >> 1) & 1;
+      bool ok = mbar_wait_bounded(bar_acc_empty + 8 * buf, acc_ph ^ 1);
+      tc_fence_after();
+      const uint32_t d_tmem = tmem_base + buf * p.bn;
+      for (int kb = 0; kb < p.k_blocks && ok; ++kb, ++it) {
+        const int st = it % kStages;
+        const uint32_t ph = (it / kStages) & 1;
+        if (!mbar_wait_bounded(bar_full + 8 * st, ph)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t sa = stage0 + st * stage_bytes, sb = sa + kTileBytesA;
+          for (int k = 0; k < BK / UK; ++k) {
+            // K-major: the K step moves 32 B inside the swizzle row; SBO = 8 rows * 128 B.
+            // MN-major: the K step moves UK rows of 128 B; LBO = next 128-byte MN block (BK rows), SBO = 8 rows.
+            const uint64_t ad = p.a_mn_major ? smem_desc(sa + k * UK * 128, BK * 128, 1024)
+                                             : smem_desc(sa + k * 32, 16, 1024);
+            const uint64_t bd = p.b_mn_major ? smem_desc(sb + k * UK * 128, BK * 128, 1024)
+                                             : smem_desc(sb + k * 32, 16, 1024);
+            tc_mma<TF32>(d_tmem, ad, bd, p.idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          }
+          tc_commit(bar_empty + 8 * st);
+        }
+        __syncwarp();
+      }
+      if (!ok) {
+        if (lane == 0) set_status(p.status, NVB200_STATUS_WAIT_TIMEOUT);
+        *abort_flag = 1;
+        break;
+      }
+      if (lane == 0) tc_commit(bar_acc_full + 8 * buf);
+      __syncwarp();
+    }
+  } else {
+    // ---------------------------------------------------------------- epilogue: TMEM -> registers -> C
+    const int q = warp & 3;  // TMEM lane quarter this warp may read
+    int local = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+      int pm, pn;
+      tile_coords(tile, p.tiles_m, p.tiles_n, pm, pn);
+      const int buf = local & 1;
+      if (!mbar_wait_bounded(bar_acc_full + 8 * buf, (local >> 1) & 1)) {
+        if (lane == 0) set_status(p.status, NVB200_STATUS_WAIT_TIMEOUT);
+        *abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      const int row = pm * BM + q * 32 + lane;
+      for (int c0 = 0; c0 < p.bn; c0 += 32) {
+        float v[32];
+        tmem_ld32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * p.bn + c0, v);
+        const int col0 = pn * p.bn + c0;
+        if (row >= p.M || col0 >= p.N) continue;
+        if (p.c_is_f32) {
+          float *c = static_cast<float *>(p.c) + row * p.scm;
+          if (p.scn == 1 && col0 + 32 <= p.N && ((reinterpret_cast<uintptr_t>(c + col0) & 15) == 0)) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 4)
+              *reinterpret_cast<float4 *>(c + col0 + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (col0 + i < p.N) c[(col0 + i) * p.scn] = v[i];
+          }
+        } else {
+          __nv_bfloat16 *c = static_cast<__nv_bfloat16 *>(p.c) + row * p.scm;
+          if (p.scn == 1 && col0 + 32 <= p.N && ((reinterpret_cast<uintptr_t>(c + col0) & 15) == 0)) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 8) {
+              const float f[8] = {v[i], v[i + 1], v[i + 2], v[i + 3], v[i + 4], v[i + 5], v[i + 6], v[i + 7]};
+              *reinterpret_cast<uint4 *>(c + col0 + i) = pack8(f);
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (col0 + i < p.N) c[(col0 + i) * p.scn] = __float2bfloat16_rn(v[i]);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_acc_empty + 8 * buf);
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 2 * p.bn <= 256 ? 256 : 512);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Host side: tensor maps (cuTensorMapEncodeTiled through the runtime's driver entry point, so the library has no
+// link-time dependency on libcuda) and the launch.
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (fn == nullptr) {
+    void *ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
+}
+
+// 2-D map of a row-pitched matrix: inner dim `inner` contiguous elements, `outer` rows `pitch` elements apart,
+// box of `box_inner` x `box_outer`, 128-byte swizzle, out-of-range elements read as zero.
+bool make_map(CUtensorMap *map, const void *base, bool f32, int64_t inner, int64_t outer, int64_t pitch,
+              int box_inner, int box_outer) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return false;
+  const int es = f32 ? 4 : 2;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(pitch * es)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(box_inner), static_cast<cuuint32_t>(box_outer)};
+  cuuint32_t estr[2] = {1, 1};
+  const CUresult r = fn(map, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                        const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+template <bool TF32> int configure_once(int smem) {
+  static int configured[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && configured[dev] >= smem) return NVB200_OK;
+  if (cudaFuncSetAttribute(matmul_tc_kernel<TF32>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+    return NVB200_ERR_CUDA;
+  if (dev < 64) configured[dev] = smem;
+  return NVB200_OK;
+}
+
+}  // namespace
+
+int matmul_tc_launch(void *c, const void *a, const void *b, int64_t M, int64_t N, int64_t K, int64_t sam,
+                     int64_t sak, int64_t sbk, int64_t sbn, int64_t scm, int64_t scn, int dtype, int32_t *status,
+                     cudaStream_t stream) {
+  if (K <= 0 || M > 0x7fffffffLL || N > 0x7fffffffLL || K > 0x7fffffffLL) return NVB200_ERR_UNSUPPORTED;
+  const bool f32 = dtype == NVB200_F32;
+  const int es = f32 ? 4 : 2;
+  const int BK = 128 / es;
+  // Operand layouts TMA can read: one unit stride, the other a multiple of 16 bytes, base 16-byte aligned.
+  bool a_mn;
+  if (sak == 1 && (sam * es) % 16 == 0) a_mn = false;
+  else if (sam == 1 && (sak * es) % 16 == 0) a_mn = true;
+  else return NVB200_ERR_UNSUPPORTED;
+  bool b_mn;
+  if (sbk == 1 && (sbn * es) % 16 == 0) b_mn = false;
+  else if (sbn == 1 && (sbk * es) % 16 == 0) b_mn = true;
+  else return NVB200_ERR_UNSUPPORTED;
+  if (!aligned16(a) || !aligned16(b)) return NVB200_ERR_UNSUPPORTED;
+
+  const int sms = sm_count();
+  const int64_t tm = (M + BM - 1) / BM;
+  // BN = 256 unless 128 gives at least as many tiles as SMs where 256 does not.
+  int bn = 256;
+  if (tm * ((N + 255) / 256) < sms && tm * ((N + 127) / 128) > tm * ((N + 255) / 256)) bn = 128;
+
+  CUtensorMap map_a, map_b;
+  const bool ok_a = a_mn ? make_map(&map_a, a, f32, M, K, sak, BK, BK) : make_map(&map_a, a, f32, K, M, sam, BK, BM);
+  const bool ok_b = b_mn ? make_map(&map_b, b, f32, N, K, sbk, BK, BK) : make_map(&map_b, b, f32, K, N, sbn, BK, bn);
+  if (!ok_a || !ok_b) return NVB200_ERR_UNSUPPORTED;
+
+  TcParams p{};
+  p.c = c;
+  p.scm = scm;
+  p.scn = scn;
+  p.M = static_cast<int>(M);
+  p.N = static_cast<int>(N);
+  p.K = static_cast<int>(K);
+  p.bn = bn;
+  p.tiles_m = static_cast<int>(tm);
+  p.tiles_n = static_cast<int>((N + bn - 1) / bn);
+  p.k_blocks = static_cast<int>((K + BK - 1) / BK);
+  p.a_mn_major = a_mn;
+  p.b_mn_major = b_mn;
+  p.elem_bytes = es;
+  p.c_is_f32 = f32;
+  p.status = status;
+  // Instruction descriptor: D fp32 (bits 4-5 = 1), A/B format (bits 7-9, 10-12: 1 = bf16, 2 = tf32), major bits
+  // 15/16 (1 = MN-major), N >> 3 at bit 17, M >> 4 at bit 24.
+  const uint32_t fmt = f32 ? 2u : 1u;
+  p.idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | (static_cast<uint32_t>(a_mn) << 15) |
+            (static_cast<uint32_t>(b_mn) << 16) | (static_cast<uint32_t>(bn >> 3) << 17) |
+            (static_cast<uint32_t>(BM >> 4) << 24);
+  if (static_cast<int64_t>(p.tiles_m) * p.tiles_n > 0x7fffffffLL) return NVB200_ERR_UNSUPPORTED;
+
+  const int smem = 1024 + kStages * (kTileBytesA + bn * 128) + 256;
+  const int rc = f32 ? configure_once<true>(smem) : configure_once<false>(smem);
+  if (rc) return rc;
+  const int tiles = p.tiles_m * p.tiles_n;
+  const unsigned grid = static_cast<unsigned>(std::min(tiles, sms));
+  if (f32)
+    matmul_tc_kernel<true><<<grid, kThreads, smem, stream>>>(map_a, map_b, p);
+  else
+    matmul_tc_kernel<false><<<grid, kThreads, smem, stream>>>(map_a, map_b, p);
+  return launch_status();
 }
 
 }  // namespace nvb200

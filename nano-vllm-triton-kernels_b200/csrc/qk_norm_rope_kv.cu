@@ -75,6 +75,7 @@ struct QknrParams {
   int64_t units;    // T * S
   int64_t chunk;    // units per CTA
   int stages;       // pipeline depth
+  int consumers;    // consumer warps in use (<= NVB200_QKNR_CONSUMERS); each owns stages w, w + consumers, ...
   int stage_bytes;  // bytes per stage (multiple of 128)
   float eps;
   int32_t *status;
@@ -105,6 +106,12 @@ NVB200_DEVICE void norm_rope8(const float (&x1)[8], const float (&x2)[8], float 
 NVB200_DEVICE void load_w8(const __nv_bfloat16 *p, uint32_t (&w)[4]) {
   const uint4 v = __ldg(reinterpret_cast<const uint4 *>(p));
   w[0] = v.x, w[1] = v.y, w[2] = v.z, w[3] = v.w;
+}
+
+// Next unit after `it` whose stage (unit % NS) belongs to the same consumer warp (stages w, w + W, w + 2W, ...).
+NVB200_DEVICE int next_unit(int it, int NS, int W) {
+  const int st = it % NS;
+  return st + W < NS ? it + W : it - st + NS + st % W;
 }
 
 // ---------------------------------------------------------------------------------------------------------------
@@ -207,10 +214,15 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) qknr_bulk_kernel(const _
   const int total = nq + p.g;
   // Deferred release: a stage is handed back one unit later, once its bulk stores have read it, so the warp does
   // not wait for that read. Needs more stages than consumer warps (each warp then holds at most two).
-  const bool defer = NVB200_QKNR_DEFER_RELEASE && NS > kConsumerWarps;
+  const bool defer = NVB200_QKNR_DEFER_RELEASE && NS >= 2 * p.consumers;
   int pending_empty = -1;  // stage whose release waits for its bulk stores to finish reading shared memory
 
-  for (int it = cw; it < n_units; it += kConsumerWarps) {
+  // Warp cw owns stages cw, cw + W, ... and consumes exactly the units that land in them, in order. Every waiter
+  // of a stage's full barrier thus sees each of its phases, which the parity wait requires (a warp that could run
+  // two phases ahead of a stage would read a parity that aliases an older phase).
+  const int W = p.consumers;
+  if (cw >= W) return;
+  for (int it = cw; it < n_units; it = next_unit(it, NS, W)) {
     const int st = it % NS;
     const uint32_t ph = (it / NS) & 1;
     const uint32_t full = bar_base + 8 * st, empty = bar_base + 8 * (NS + st);
@@ -468,8 +480,10 @@ int qk_norm_rope_kv_launch(const nvb200_qk_norm_rope_kv_args *a, cudaStream_t st
   p.units = T * splits;
   const int unit_bytes = (p.g * p.r + 2 * p.g) * D * 2 + D * 4;
   p.stage_bytes = (unit_bytes + 127) / 128 * 128;
-  p.stages = std::max(2, std::min(kMaxStages, kSmemBudget / p.stage_bytes));
-  if (p.stage_bytes * 2 > kSmemBudget) return NVB200_ERR_UNSUPPORTED;  // > 100 KB per token: too many heads
+  p.stages = std::min(kMaxStages, kSmemBudget / p.stage_bytes);
+  if (p.stages < 2) return NVB200_ERR_UNSUPPORTED;  // a unit larger than half the budget: too many heads
+  p.consumers = std::min(kConsumerWarps, p.stages);
+  if (p.stages % p.consumers) p.stages -= p.stages % p.consumers;  // every warp owns the same number of stages
   switch (D) {
     case 64: return launch_bulk<64>(p, sms, stream);
     case 128: return launch_bulk<128>(p, sms, stream);

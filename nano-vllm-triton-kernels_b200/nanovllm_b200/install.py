@@ -1,0 +1,102 @@
+"""Registers the B200 kernels as kernel_backend="b200" in an importable reference nano-vllm, without editing it.
+
+The reference selects its kernels with the module-global string `nanovllm.kernels.backend`, which
+`ModelRunner.__init__` sets from `Config.kernel_backend` before building the model
+(nanovllm/engine/model_runner.py:83) and the layers read once in `__init__`. install():
+
+1. lets `Config.__post_init__` accept "b200" (it asserts the backend is compile/triton/triton_fused,
+   nanovllm/config.py:39);
+2. makes the kernel names the layers bound at import (nanovllm/layers/layernorm.py:5, layers/activation.py:6,
+   layers/attention.py:7) and the `nanovllm.kernels.*` module attributes resolve to the b200 functions whenever
+   `nanovllm.kernels.backend == "b200"`; every other backend keeps the reference's own kernels;
+3. makes `Qwen3Attention` (nanovllm/models/qwen3.py:73-75) take the fused path for "b200" as for "triton_fused",
+   so q/k norm, RoPE and the KV write run as one kernel inside Attention.forward (layers/attention.py:64-76);
+4. makes the tensor-parallel worker processes (spawned, nanovllm/engine/llm_engine.py:24-30) run install() too.
+
+Call it once, before constructing `LLM(..., kernel_backend="b200")`.
+"""
+import functools
+
+BACKEND = "b200"
+_installed = False
+
+
+def _by_backend(kernels_mod, ours, theirs):
+    @functools.wraps(theirs)
+    def fn(*args, **kwargs):
+        return (ours if kernels_mod.backend == BACKEND else theirs)(*args, **kwargs)
+    fn.__b200__ = ours
+    return fn
+
+
+def _model_runner(config, rank, event):
+    """Spawned TP worker entry: register the backend in this fresh process, then run the reference's ModelRunner."""
+    install()
+    from nanovllm.engine.model_runner import ModelRunner
+    return ModelRunner(config, rank, event)
+
+
+def install() -> None:
+    global _installed
+    if _installed:
+        return
+    import nanovllm.config as config_mod
+    import nanovllm.engine.llm_engine as engine_mod
+    import nanovllm.kernels as kernels_mod
+    import nanovllm.kernels.matmul as ref_matmul
+    import nanovllm.kernels.qk_norm_rope_kv as ref_fused
+    import nanovllm.kernels.rms_norm as ref_norm
+    import nanovllm.kernels.swiglu as ref_swiglu
+    import nanovllm.layers.activation as activation_mod
+    import nanovllm.layers.attention as attention_mod
+    import nanovllm.layers.layernorm as layernorm_mod
+    import nanovllm.models.qwen3 as qwen3_mod
+
+    from nanovllm_b200.kernels import matmul as b200_matmul
+    from nanovllm_b200.kernels import qk_norm_rope_kv as b200_fused
+    from nanovllm_b200.kernels import rms_norm as b200_norm
+    from nanovllm_b200.kernels import swiglu as b200_swiglu
+
+    # 1. Config accepts "b200".
+    post_init = config_mod.Config.__post_init__
+
+    def __post_init__(self):
+        if self.kernel_backend != BACKEND:
+            return post_init(self)
+        self.kernel_backend = "triton_fused"
+        try:
+            post_init(self)
+        finally:
+            self.kernel_backend = BACKEND
+    config_mod.Config.__post_init__ = __post_init__
+
+    # 2. Kernel names resolve by backend.
+    pairs = [
+        (ref_norm, "rms_norm", b200_norm.rms_norm), (ref_norm, "fused_add_rms_norm", b200_norm.fused_add_rms_norm),
+        (ref_swiglu, "silu_and_mul", b200_swiglu.silu_and_mul),
+        (ref_fused, "qk_norm_rope_kv", b200_fused.qk_norm_rope_kv), (ref_matmul, "matmul", b200_matmul.matmul),
+        (layernorm_mod, "rms_norm", b200_norm.rms_norm),
+        (layernorm_mod, "fused_add_rms_norm", b200_norm.fused_add_rms_norm),
+        (activation_mod, "silu_and_mul", b200_swiglu.silu_and_mul),
+        (attention_mod, "qk_norm_rope_kv", b200_fused.qk_norm_rope_kv),
+    ]
+    for mod, name, ours in pairs:
+        setattr(mod, name, _by_backend(kernels_mod, ours, getattr(mod, name)))
+
+    # 3. Qwen3Attention treats "b200" as a fused backend.
+    attn_init = qwen3_mod.Qwen3Attention.__init__
+
+    @functools.wraps(attn_init)
+    def __init__(self, *args, **kwargs):
+        if kernels_mod.backend != BACKEND:
+            return attn_init(self, *args, **kwargs)
+        kernels_mod.backend = "triton_fused"
+        try:
+            attn_init(self, *args, **kwargs)
+        finally:
+            kernels_mod.backend = BACKEND
+    qwen3_mod.Qwen3Attention.__init__ = __init__
+
+    # 4. Spawned tensor-parallel workers register the backend before building their ModelRunner.
+    engine_mod.ModelRunner = _model_runner
+    _installed = True

@@ -1,0 +1,75 @@
+"""nanovllm_b200.install() against the reference package, on CPU (no kernels run).
+
+Needs an importable reference nano-vllm: the offline install under baseline/_ref, or the path in
+$NANOVLLM_REFERENCE. Checks that kernel_backend="b200" is accepted by Config, that the layers' kernel names resolve
+to the b200 functions only while the backend is "b200", and that Qwen3Attention takes the fused path for it.
+"""
+import json
+import os
+import sys
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+CANDIDATES = [os.path.join(ROOT, "baseline", "_ref"), os.environ.get("NANOVLLM_REFERENCE", "")]
+REF = next((p for p in CANDIDATES if p and os.path.isdir(os.path.join(p, "nanovllm"))), None)
+pytestmark = pytest.mark.skipif(REF is None, reason="no importable reference nano-vllm")
+
+QWEN3_06B = {"architectures": ["Qwen3ForCausalLM"], "model_type": "qwen3", "hidden_size": 1024,
+             "intermediate_size": 3072, "num_hidden_layers": 28, "num_attention_heads": 16,
+             "num_key_value_heads": 8, "head_dim": 128, "vocab_size": 151936, "max_position_embeddings": 40960,
+             "rms_norm_eps": 1e-6, "rope_theta": 1000000, "tie_word_embeddings": True, "torch_dtype": "bfloat16",
+             "hidden_act": "silu", "attention_bias": False}
+
+
+@pytest.fixture(scope="module")
+def ref():
+    if REF not in sys.path:
+        sys.path.insert(0, REF)
+    import nanovllm_b200
+    nanovllm_b200.install()
+    import nanovllm.kernels as kernels
+    return kernels
+
+
+def test_config_accepts_b200(ref, tmp_path):
+    (tmp_path / "config.json").write_text(json.dumps(QWEN3_06B))
+    from nanovllm.config import Config
+    cfg = Config(str(tmp_path), kernel_backend="b200")
+    assert cfg.kernel_backend == "b200"
+    with pytest.raises(AssertionError):
+        Config(str(tmp_path), kernel_backend="nonsense")
+
+
+def test_kernel_names_follow_the_backend(ref):
+    import nanovllm.layers.activation as act
+    import nanovllm.layers.attention as att
+    import nanovllm.layers.layernorm as ln
+    from nanovllm_b200.kernels import qk_norm_rope_kv, rms_norm, swiglu
+    assert ln.rms_norm.__b200__ is rms_norm.rms_norm
+    assert ln.fused_add_rms_norm.__b200__ is rms_norm.fused_add_rms_norm
+    assert act.silu_and_mul.__b200__ is swiglu.silu_and_mul
+    assert att.qk_norm_rope_kv.__b200__ is qk_norm_rope_kv.qk_norm_rope_kv
+
+
+def test_qwen3_attention_is_fused_for_b200(ref):
+    import torch
+    import torch.distributed as dist
+    from nanovllm.models.qwen3 import Qwen3Attention
+    if not dist.is_initialized():
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        os.environ.setdefault("MASTER_PORT", "29617")
+        dist.init_process_group("gloo", rank=0, world_size=1)
+    old = ref.backend
+    try:
+        ref.backend = "b200"
+        with torch.device("meta"):
+            a = Qwen3Attention(1024, 16, 8, max_position=4096, head_dim=128, rope_theta=1e6)
+        assert a.fused_norm_rope and a.attn.norm_rope is not None
+        assert ref.backend == "b200"
+        ref.backend = "compile"
+        with torch.device("meta"):
+            b = Qwen3Attention(1024, 16, 8, max_position=4096, head_dim=128, rope_theta=1e6)
+        assert not b.fused_norm_rope
+    finally:
+        ref.backend = old
