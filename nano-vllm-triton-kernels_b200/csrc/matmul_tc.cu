@@ -39,6 +39,8 @@ struct TcParams {
   int k_blocks;    // ceil(K / BK)
   uint32_t idesc;  // tcgen05 instruction descriptor
   int a_mn_major, b_mn_major;
+  uint32_t a_sbo, b_sbo;    // descriptor stride byte offsets (MN-major: bytes between groups of k rows)
+  uint32_t a_swz, b_swz;    // descriptor layout types (2 = 128-byte swizzle, 1 = 128-byte swizzle of 32-byte atoms)
   int elem_bytes;  // 2 (bf16) or 4 (fp32/tf32)
   int c_is_f32;
   int32_t *status;
@@ -110,14 +112,16 @@ NVB200_DEVICE void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// Shared-memory matrix descriptor, 128-byte swizzle (layout type 2), sm100 version bits = 1.
-NVB200_DEVICE uint64_t smem_desc(uint32_t addr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+// Shared-memory matrix descriptor (sm100 version bits = 1). layout: 2 = 128-byte swizzle of 16-byte chunks (what
+// TMA's SWIZZLE_128B writes), 1 = 128-byte swizzle of 32-byte chunks (TMA's SWIZZLE_128B_ATOM_32B), the form
+// 32-bit (tf32) MN-major operands need.
+NVB200_DEVICE uint64_t smem_desc(uint32_t addr, uint32_t lbo_bytes, uint32_t sbo_bytes, uint32_t layout) {
   uint64_t d = 0;
   d |= static_cast<uint64_t>((addr >> 4) & 0x3FFF);
   d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFF) << 16;
   d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFF) << 32;
   d |= 1ull << 46;
-  d |= 2ull << 61;
+  d |= static_cast<uint64_t>(layout) << 61;
   return d;
 }
 
@@ -230,11 +234,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t sa = stage0 + st * stage_bytes, sb = sa + kTileBytesA;
           for (int k = 0; k < BK / UK; ++k) {
             // K-major: the K step moves 32 B inside the swizzle row; SBO = 8 rows * 128 B.
-            // MN-major: the K step moves UK rows of 128 B; LBO = next 128-byte MN block (BK rows), SBO = 8 rows.
-            const uint64_t ad = p.a_mn_major ? smem_desc(sa + k * UK * 128, BK * 128, 1024)
-                                             : smem_desc(sa + k * 32, 16, 1024);
-            const uint64_t bd = p.b_mn_major ? smem_desc(sb + k * UK * 128, BK * 128, 1024)
-                                             : smem_desc(sb + k * 32, 16, 1024);
+            // MN-major: the K step moves UK rows of 128 B; LBO = next 128-byte MN block (BK rows), SBO = one
+            // swizzle atom of k rows (8 rows, or 4 rows for the 32-byte-atom swizzle).
+            const uint64_t ad = p.a_mn_major ? smem_desc(sa + k * UK * 128, BK * 128, p.a_sbo, p.a_swz)
+                                             : smem_desc(sa + k * 32, 16, 1024, 2);
+            const uint64_t bd = p.b_mn_major ? smem_desc(sb + k * UK * 128, BK * 128, p.b_sbo, p.b_swz)
+                                             : smem_desc(sb + k * 32, 16, 1024, 2);
             tc_mma<TF32>(d_tmem, ad, bd, p.idesc, (kb > 0 || k > 0) ? 1u : 0u);
           }
           tc_commit(bar_empty + 8 * st);
@@ -325,9 +330,10 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 // 2-D map of a row-pitched matrix: inner dim `inner` contiguous elements, `outer` rows `pitch` elements apart,
-// box of `box_inner` x `box_outer`, 128-byte swizzle, out-of-range elements read as zero.
+// box of `box_inner` x `box_outer`, 128-byte swizzle (of 16-byte chunks, or of 32-byte chunks when atom32),
+// out-of-range elements read as zero.
 bool make_map(CUtensorMap *map, const void *base, bool f32, int64_t inner, int64_t outer, int64_t pitch,
-              int box_inner, int box_outer) {
+              int box_inner, int box_outer, bool atom32 = false) {
   auto fn = encode_fn();
   if (fn == nullptr) return false;
   const int es = f32 ? 4 : 2;
@@ -337,7 +343,8 @@ bool make_map(CUtensorMap *map, const void *base, bool f32, int64_t inner, int64
   cuuint32_t estr[2] = {1, 1};
   const CUresult r = fn(map, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
                         const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        atom32 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
@@ -379,9 +386,10 @@ int matmul_tc_launch(void *c, const void *a, const void *b, int64_t M, int64_t N
   int bn = 256;
   if (tm * ((N + 255) / 256) < sms && tm * ((N + 127) / 128) > tm * ((N + 255) / 256)) bn = 128;
 
+  // 32-bit MN-major operands use the 32-byte-atom swizzle (4-row atoms); everything else the 16-byte one.
   CUtensorMap map_a, map_b;
-  const bool ok_a = a_mn ? make_map(&map_a, a, f32, M, K, sak, BK, BK) : make_map(&map_a, a, f32, K, M, sam, BK, BM);
-  const bool ok_b = b_mn ? make_map(&map_b, b, f32, N, K, sbk, BK, BK) : make_map(&map_b, b, f32, K, N, sbn, BK, bn);
+  const bool ok_a = a_mn ? make_map(&map_a, a, f32, M, K, sak, BK, BK, f32) : make_map(&map_a, a, f32, K, M, sam, BK, BM);
+  const bool ok_b = b_mn ? make_map(&map_b, b, f32, N, K, sbk, BK, BK, f32) : make_map(&map_b, b, f32, K, N, sbn, BK, bn);
   if (!ok_a || !ok_b) return NVB200_ERR_UNSUPPORTED;
 
   TcParams p{};
@@ -397,6 +405,8 @@ int matmul_tc_launch(void *c, const void *a, const void *b, int64_t M, int64_t N
   p.k_blocks = static_cast<int>((K + BK - 1) / BK);
   p.a_mn_major = a_mn;
   p.b_mn_major = b_mn;
+  p.a_swz = p.b_swz = f32 ? 1u : 2u;
+  p.a_sbo = p.b_sbo = f32 ? 512u : 1024u;
   p.elem_bytes = es;
   p.c_is_f32 = f32;
   p.status = status;

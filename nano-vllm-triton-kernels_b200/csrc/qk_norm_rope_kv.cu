@@ -76,6 +76,9 @@ struct QknrParams {
   int64_t chunk;    // units per CTA
   int stages;       // pipeline depth
   int consumers;    // consumer warps in use (<= NVB200_QKNR_CONSUMERS); each owns stages w, w + consumers, ...
+  int qkv_row;      // 1: q, k, v are consecutive in memory (one qkv_proj row per token) and a unit is a whole
+                    // token, so one bulk copy moves the unit's q | k | v (v is then read for skipped slots too,
+                    // as the reference's byte count assumes)
   int stage_bytes;  // bytes per stage (multiple of 128)
   float eps;
   int32_t *status;
@@ -187,11 +190,16 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) qknr_bulk_kernel(const _
             const int64_t t = unit / p.splits;
             const int s = static_cast<int>(unit % p.splits);
             const uint32_t sb = stage_base + st * p.stage_bytes;
-            const uint32_t vbytes = sj >= 0 ? kb : 0;
-            mbar_arrive_expect_tx(full, qb + kb + csb + vbytes);
-            bulk_g2s(sb, p.q + t * p.q_stride + static_cast<int64_t>(s) * nq * D, qb, full);
-            bulk_g2s(sb + qb, p.k + t * p.k_stride + static_cast<int64_t>(s) * p.g * D, kb, full);
-            if (vbytes) bulk_g2s(sb + qb + kb, p.v + t * p.v_stride + static_cast<int64_t>(s) * p.g * D, kb, full);
+            if (p.qkv_row) {
+              mbar_arrive_expect_tx(full, qb + 2 * kb + csb);
+              bulk_g2s(sb, p.q + t * p.q_stride, qb + 2 * kb, full);
+            } else {
+              const uint32_t vbytes = sj >= 0 ? kb : 0;
+              mbar_arrive_expect_tx(full, qb + kb + csb + vbytes);
+              bulk_g2s(sb, p.q + t * p.q_stride + static_cast<int64_t>(s) * nq * D, qb, full);
+              bulk_g2s(sb + qb, p.k + t * p.k_stride + static_cast<int64_t>(s) * p.g * D, kb, full);
+              if (vbytes) bulk_g2s(sb + qb + kb, p.v + t * p.v_stride + static_cast<int64_t>(s) * p.g * D, kb, full);
+            }
             bulk_g2s(sb + qb + 2 * kb, p.cos_sin + pj * p.cs_stride, csb, full);
           }
         }
@@ -478,6 +486,9 @@ int qk_norm_rope_kv_launch(const nvb200_qk_norm_rope_kv_args *a, cudaStream_t st
   p.splits = splits;
   p.g = hkv / splits;
   p.units = T * splits;
+  p.qkv_row = splits == 1 && store && a->k == p.q + static_cast<int64_t>(hq) * D &&
+              a->v == p.k + static_cast<int64_t>(hkv) * D && a->q_token_stride == a->k_token_stride &&
+              a->k_token_stride == a->v_token_stride;
   const int unit_bytes = (p.g * p.r + 2 * p.g) * D * 2 + D * 4;
   p.stage_bytes = (unit_bytes + 127) / 128 * 128;
   p.stages = std::min(kMaxStages, kSmemBudget / p.stage_bytes);

@@ -105,11 +105,14 @@ def matmul(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
     return a.double() @ b.double()
 
 
-def tf32_round(x: torch.Tensor) -> torch.Tensor:
-    """x (fp32) rounded to tf32 (10 explicit mantissa bits, round to nearest, ties away from zero as the tensor
-    core's operand conversion does for finite values); used to build the tf32 product reference a_tf32 @ b_tf32."""
+def tf32_round(x: torch.Tensor, mode: str = "rz") -> torch.Tensor:
+    """x (fp32) reduced to tf32 (10 explicit mantissa bits): "rz" drops the low 13 bits (what the tensor core does
+    with fp32 operands it reads as tf32), "rna" rounds to nearest, ties away from zero (cvt.rna.tf32.f32). Used to
+    build the tf32 product reference a_tf32 @ b_tf32."""
     i = x.contiguous().view(torch.int32)
-    i = (i + 0x1000) & ~0x1FFF
+    if mode == "rna":
+        i = i + 0x1000
+    i = i & ~0x1FFF
     return i.view(torch.float32).reshape(x.shape)
 
 
