@@ -29,6 +29,7 @@ constexpr int kEpilogueWarps = 4;
 constexpr int kThreads = 32 * (2 + kEpilogueWarps);
 constexpr int kGroupM = 8;
 constexpr int kTileBytesA = BM * 128;  // one 128-byte swizzle row per M row (BK * elem = 128 B)
+constexpr int kMaxStages2 = 8;         // CTA-pair kernel: stage ring capacity
 
 struct TcParams {
   void *c;
@@ -37,6 +38,7 @@ struct TcParams {
   int bn;          // tile N (256 or 128)
   int tiles_m, tiles_n;
   int k_blocks;    // ceil(K / BK)
+  int stages;      // CTA-pair kernel: pipeline depth
   uint32_t idesc;  // tcgen05 instruction descriptor
   int a_mn_major, b_mn_major;
   uint32_t a_sbo, b_sbo;    // descriptor stride byte offsets (MN-major: bytes between groups of k rows)
@@ -68,6 +70,70 @@ NVB200_DEVICE void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
 
 NVB200_DEVICE void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
   asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+NVB200_DEVICE void tmem_alloc2(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+NVB200_DEVICE void tmem_dealloc2(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+NVB200_DEVICE uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Address of the same shared-memory location in CTA `rank` of this cluster.
+NVB200_DEVICE uint32_t map_to_cta(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+
+NVB200_DEVICE void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+NVB200_DEVICE void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+// TMA load whose completion is counted on the pair leader's mbarrier (cta_group::2; no multicast).
+NVB200_DEVICE void tma_load_2d_pair(uint32_t dst, const CUtensorMap *map, int c0, int c1, uint32_t leader_bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+      "[%4];" ::"r"(dst), "l"(map), "r"(c0), "r"(c1), "r"(leader_bar)
+      : "memory");
+}
+
+template <bool TF32>
+NVB200_DEVICE void tc_mma2(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
+  if (TF32) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+  }
+}
+
+// Arrives on `bar` (same offset) in both CTAs of the pair once this thread's tcgen05.mma ops have completed.
+NVB200_DEVICE void tc_commit_pair(uint32_t bar) {
+  const uint16_t mask = 3;
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;"
+               ::"r"(bar), "h"(mask)
+               : "memory");
 }
 
 NVB200_DEVICE void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
@@ -132,6 +198,42 @@ NVB200_DEVICE void tile_coords(int tile, int tiles_m, int tiles_n, int &pm, int 
   const int group_m = min(tiles_m - first_m, kGroupM);
   pm = first_m + (tile % in_group) % group_m;
   pn = (tile % in_group) / group_m;
+}
+
+// Epilogue: this thread's accumulator row (one TMEM lane) -> C[row, col0 .. col0 + ncols), 32 columns per
+// tcgen05.ld, rounded to C's dtype. Every lane of the warp must call it (tcgen05.ld is warp-wide).
+NVB200_DEVICE void store_tile_rows(const TcParams &p, uint32_t taddr, int row, int col_base, int ncols) {
+  for (int c0 = 0; c0 < ncols; c0 += 32) {
+    float v[32];
+    tmem_ld32(taddr + c0, v);
+    const int col0 = col_base + c0;
+    if (row >= p.M || col0 >= p.N) continue;
+    if (p.c_is_f32) {
+      float *c = static_cast<float *>(p.c) + row * p.scm;
+      if (p.scn == 1 && col0 + 32 <= p.N && ((reinterpret_cast<uintptr_t>(c + col0) & 15) == 0)) {
+#pragma unroll
+        for (int i = 0; i < 32; i += 4)
+          *reinterpret_cast<float4 *>(c + col0 + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (col0 + i < p.N) c[(col0 + i) * p.scn] = v[i];
+      }
+    } else {
+      __nv_bfloat16 *c = static_cast<__nv_bfloat16 *>(p.c) + row * p.scm;
+      if (p.scn == 1 && col0 + 32 <= p.N && ((reinterpret_cast<uintptr_t>(c + col0) & 15) == 0)) {
+#pragma unroll
+        for (int i = 0; i < 32; i += 8) {
+          const float f[8] = {v[i], v[i + 1], v[i + 2], v[i + 3], v[i + 4], v[i + 5], v[i + 6], v[i + 7]};
+          *reinterpret_cast<uint4 *>(c + col0 + i) = pack8(f);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (col0 + i < p.N) c[(col0 + i) * p.scn] = __float2bfloat16_rn(v[i]);
+      }
+    }
+  }
 }
 
 // Stage layout (each operand tile 1024-byte aligned, as the 128-byte swizzle requires):
@@ -268,38 +370,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
-      const int row = pm * BM + q * 32 + lane;
-      for (int c0 = 0; c0 < p.bn; c0 += 32) {
-        float v[32];
-        tmem_ld32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * p.bn + c0, v);
-        const int col0 = pn * p.bn + c0;
-        if (row >= p.M || col0 >= p.N) continue;
-        if (p.c_is_f32) {
-          float *c = static_cast<float *>(p.c) + row * p.scm;
-          if (p.scn == 1 && col0 + 32 <= p.N && ((reinterpret_cast<uintptr_t>(c + col0) & 15) == 0)) {
-#pragma unroll
-            for (int i = 0; i < 32; i += 4)
-              *reinterpret_cast<float4 *>(c + col0 + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
-          } else {
-#pragma unroll
-            for (int i = 0; i < 32; ++i)
-              if (col0 + i < p.N) c[(col0 + i) * p.scn] = v[i];
-          }
-        } else {
-          __nv_bfloat16 *c = static_cast<__nv_bfloat16 *>(p.c) + row * p.scm;
-          if (p.scn == 1 && col0 + 32 <= p.N && ((reinterpret_cast<uintptr_t>(c + col0) & 15) == 0)) {
-#pragma unroll
-            for (int i = 0; i < 32; i += 8) {
-              const float f[8] = {v[i], v[i + 1], v[i + 2], v[i + 3], v[i + 4], v[i + 5], v[i + 6], v[i + 7]};
-              *reinterpret_cast<uint4 *>(c + col0 + i) = pack8(f);
-            }
-          } else {
-#pragma unroll
-            for (int i = 0; i < 32; ++i)
-              if (col0 + i < p.N) c[(col0 + i) * p.scn] = __float2bfloat16_rn(v[i]);
-          }
-        }
-      }
+      store_tile_rows(p, tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * p.bn, pm * BM + q * 32 + lane,
+                      pn * p.bn, p.bn);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar_acc_empty + 8 * buf);
@@ -310,6 +382,164 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, 2 * p.bn <= 256 ? 256 : 512);
+  }
+}
+
+
+// ---------------------------------------------------------------------------------------------------------------
+// CTA-pair kernel (cluster of 2 on neighbouring SMs, tcgen05.mma.cta_group::2): the pair computes a 256 x BN tile.
+// CTA r holds rows [128 r, 128 r + 128) of the A tile and columns [r BN/2, (r + 1) BN/2) of the B tile, so each
+// SM loads a third less operand data per FLOP than a lone 128 x BN tile. The leader (rank 0) issues the MMAs;
+// both CTAs' TMA loads count on the leader's full barrier; tcgen05.commit multicasts stage releases and
+// accumulator-ready signals to both CTAs; each CTA's epilogue drains its own 128 TMEM lanes and tells the leader
+// through a cluster-scope arrive when its accumulator buffer is free. No TMA load uses multicast.
+template <bool TF32>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    matmul_tc2_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                      const __grid_constant__ TcParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+  const int half_bn = p.bn / 2;
+  const int tile_b_bytes = half_bn * 128;
+  const int stage_bytes = kTileBytesA + tile_b_bytes;
+  const int stages = p.stages;
+  uint8_t *hdr = smem + stages * stage_bytes;
+  const uint32_t bar_full = smem_addr(hdr);                 // stages x 8 (used in the leader)
+  const uint32_t bar_empty = bar_full + 8 * kMaxStages2;    // stages x 8 (both CTAs)
+  const uint32_t bar_acc_full = bar_empty + 8 * kMaxStages2;  // 2 x 8 (both CTAs)
+  const uint32_t bar_acc_empty = bar_acc_full + 16;           // 2 x 8 (used in the leader)
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(hdr + 16 * kMaxStages2 + 32);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(hdr + 16 * kMaxStages2 + 36);
+  const uint32_t stage0 = smem_addr(smem);
+  const int BK = 128 / p.elem_bytes;
+  const int UK = 32 / p.elem_bytes;
+  const int num_tiles = p.tiles_m * p.tiles_n;  // 256-row tiles
+  const int cluster = blockIdx.x >> 1, clusters = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < stages; ++i) {
+      mbar_init(bar_full + 8 * i, 1);
+      mbar_init(bar_empty + 8 * i, 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(bar_acc_full + 8 * i, 1);
+      mbar_init(bar_acc_empty + 8 * i, 2 * kEpilogueWarps);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+    prefetch_tmap(&map_a);
+    prefetch_tmap(&map_b);
+  }
+  if (warp == 1) tmem_alloc2(smem_addr(tmem_slot), 2 * p.bn <= 256 ? 256 : 512);
+  tc_fence_before();
+  cluster_sync();  // both CTAs' barriers initialised and TMEM allocated before any cross-CTA traffic
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA producer (both CTAs)
+    if (lane == 0) {
+      int it = 0;
+      for (int tile = cluster; tile < num_tiles && !*abort_flag; tile += clusters) {
+        int pm, pn;
+        tile_coords(tile, p.tiles_m, p.tiles_n, pm, pn);
+        const int m0 = pm * 2 * BM + static_cast<int>(rank) * BM;
+        const int n0 = pn * p.bn + static_cast<int>(rank) * half_bn;
+        for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
+          const int st = it % stages;
+          const uint32_t ph = (it / stages) & 1;
+          if (!mbar_wait_bounded(bar_empty + 8 * st, ph ^ 1)) {
+            set_status(p.status, NVB200_STATUS_WAIT_TIMEOUT);
+            *abort_flag = 1;
+            break;
+          }
+          const uint32_t sa = stage0 + st * stage_bytes, sb = sa + kTileBytesA;
+          const uint32_t full = map_to_cta(bar_full + 8 * st, 0);
+          if (leader) mbar_arrive_expect_tx(bar_full + 8 * st, 2 * stage_bytes);
+          const int k0 = kb * BK;
+          if (p.a_mn_major) {
+            for (int j = 0; j < BM / BK; ++j) tma_load_2d_pair(sa + j * BK * 128, &map_a, m0 + j * BK, k0, full);
+          } else {
+            tma_load_2d_pair(sa, &map_a, k0, m0, full);
+          }
+          if (p.b_mn_major) {
+            for (int j = 0; j < half_bn / BK; ++j) tma_load_2d_pair(sb + j * BK * 128, &map_b, n0 + j * BK, k0, full);
+          } else {
+            tma_load_2d_pair(sb, &map_b, k0, n0, full);
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer (leader only)
+    if (leader) {
+      int it = 0, local = 0;
+      for (int tile = cluster; tile < num_tiles; tile += clusters, ++local) {
+        const int buf = local & 1;
+        bool ok = mbar_wait_bounded(bar_acc_empty + 8 * buf, ((local >> 1) & 1) ^ 1);
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * p.bn;
+        for (int kb = 0; kb < p.k_blocks && ok; ++kb, ++it) {
+          const int st = it % stages;
+          if (!mbar_wait_bounded(bar_full + 8 * st, (it / stages) & 1)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          if (lane == 0) {
+            const uint32_t sa = stage0 + st * stage_bytes, sb = sa + kTileBytesA;
+            for (int k = 0; k < BK / UK; ++k) {
+              const uint64_t ad = p.a_mn_major ? smem_desc(sa + k * UK * 128, BK * 128, p.a_sbo, p.a_swz)
+                                               : smem_desc(sa + k * 32, 16, 1024, 2);
+              const uint64_t bd = p.b_mn_major ? smem_desc(sb + k * UK * 128, BK * 128, p.b_sbo, p.b_swz)
+                                               : smem_desc(sb + k * 32, 16, 1024, 2);
+              tc_mma2<TF32>(d_tmem, ad, bd, p.idesc, (kb > 0 || k > 0) ? 1u : 0u);
+            }
+            tc_commit_pair(bar_empty + 8 * st);
+          }
+          __syncwarp();
+        }
+        if (!ok) {
+          if (lane == 0) set_status(p.status, NVB200_STATUS_WAIT_TIMEOUT);
+          *abort_flag = 1;
+          break;
+        }
+        if (lane == 0) tc_commit_pair(bar_acc_full + 8 * buf);
+        __syncwarp();
+      }
+    }
+  } else {
+    // ---------------------------------------------------------------- epilogue (both CTAs, own TMEM lanes)
+    const int q = warp & 3;
+    const uint32_t leader_acc_empty = map_to_cta(bar_acc_empty, 0);
+    int local = 0;
+    for (int tile = cluster; tile < num_tiles; tile += clusters, ++local) {
+      int pm, pn;
+      tile_coords(tile, p.tiles_m, p.tiles_n, pm, pn);
+      const int buf = local & 1;
+      if (!mbar_wait_bounded(bar_acc_full + 8 * buf, (local >> 1) & 1)) {
+        if (lane == 0) set_status(p.status, NVB200_STATUS_WAIT_TIMEOUT);
+        *abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      store_tile_rows(p, tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * p.bn,
+                      pm * 2 * BM + static_cast<int>(rank) * BM + q * 32 + lane, pn * p.bn, p.bn);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(leader_acc_empty + 8 * buf);
+    }
+  }
+
+  tc_fence_before();
+  cluster_sync();  // the peer's MMAs and remote arrivals are done before TMEM and shared memory go away
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc2(tmem_base, 2 * p.bn <= 256 ? 256 : 512);
   }
 }
 
@@ -349,14 +579,14 @@ bool make_map(CUtensorMap *map, const void *base, bool f32, int64_t inner, int64
   return r == CUDA_SUCCESS;
 }
 
-template <bool TF32> int configure_once(int smem) {
-  static int configured[64] = {0};
+template <typename Kernel> int configure_once(Kernel kernel, int smem, int slot) {
+  static int configured[4][64] = {{0}};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 64 && configured[dev] >= smem) return NVB200_OK;
-  if (cudaFuncSetAttribute(matmul_tc_kernel<TF32>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+  if (dev < 64 && configured[slot][dev] >= smem) return NVB200_OK;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return NVB200_ERR_CUDA;
-  if (dev < 64) configured[dev] = smem;
+  if (dev < 64) configured[slot][dev] = smem;
   return NVB200_OK;
 }
 
@@ -381,15 +611,20 @@ int matmul_tc_launch(void *c, const void *a, const void *b, int64_t M, int64_t N
   if (!aligned16(a) || !aligned16(b)) return NVB200_ERR_UNSUPPORTED;
 
   const int sms = sm_count();
-  const int64_t tm = (M + BM - 1) / BM;
-  // BN = 256 unless 128 gives at least as many tiles as SMs where 256 does not.
+  // CTA pairs (256-row tiles) when M fills at least two 128-row tiles and the pairs get enough tiles to keep
+  // every SM busy; single CTAs (128-row tiles) otherwise.
+  const int64_t tm1 = (M + BM - 1) / BM;
+  const int64_t tm2 = (M + 2 * BM - 1) / (2 * BM);
+  const bool pair = tm1 >= 2 && tm2 * ((N + 255) / 256) * 2 >= sms;
   int bn = 256;
-  if (tm * ((N + 255) / 256) < sms && tm * ((N + 127) / 128) > tm * ((N + 255) / 256)) bn = 128;
+  if (!pair && tm1 * ((N + 255) / 256) < sms && tm1 * ((N + 127) / 128) > tm1 * ((N + 255) / 256)) bn = 128;
+  const int box_n = pair ? bn / 2 : bn;  // B rows (K-major) or columns (MN-major) one CTA loads per stage
 
   // 32-bit MN-major operands use the 32-byte-atom swizzle (4-row atoms); everything else the 16-byte one.
   CUtensorMap map_a, map_b;
   const bool ok_a = a_mn ? make_map(&map_a, a, f32, M, K, sak, BK, BK, f32) : make_map(&map_a, a, f32, K, M, sam, BK, BM);
-  const bool ok_b = b_mn ? make_map(&map_b, b, f32, N, K, sbk, BK, BK, f32) : make_map(&map_b, b, f32, K, N, sbn, BK, bn);
+  const bool ok_b = b_mn ? make_map(&map_b, b, f32, N, K, sbk, BK, BK, f32)
+                         : make_map(&map_b, b, f32, K, N, sbn, BK, box_n);
   if (!ok_a || !ok_b) return NVB200_ERR_UNSUPPORTED;
 
   TcParams p{};
@@ -400,7 +635,7 @@ int matmul_tc_launch(void *c, const void *a, const void *b, int64_t M, int64_t N
   p.N = static_cast<int>(N);
   p.K = static_cast<int>(K);
   p.bn = bn;
-  p.tiles_m = static_cast<int>(tm);
+  p.tiles_m = static_cast<int>(pair ? tm2 : tm1);
   p.tiles_n = static_cast<int>((N + bn - 1) / bn);
   p.k_blocks = static_cast<int>((K + BK - 1) / BK);
   p.a_mn_major = a_mn;
@@ -411,17 +646,31 @@ int matmul_tc_launch(void *c, const void *a, const void *b, int64_t M, int64_t N
   p.c_is_f32 = f32;
   p.status = status;
   // Instruction descriptor: D fp32 (bits 4-5 = 1), A/B format (bits 7-9, 10-12: 1 = bf16, 2 = tf32), major bits
-  // 15/16 (1 = MN-major), N >> 3 at bit 17, M >> 4 at bit 24.
+  // 15/16 (1 = MN-major), N >> 3 at bit 17, M >> 4 at bit 24 (M = 256 for a CTA pair).
   const uint32_t fmt = f32 ? 2u : 1u;
+  const int mma_m = pair ? 2 * BM : BM;
   p.idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | (static_cast<uint32_t>(a_mn) << 15) |
             (static_cast<uint32_t>(b_mn) << 16) | (static_cast<uint32_t>(bn >> 3) << 17) |
-            (static_cast<uint32_t>(BM >> 4) << 24);
+            (static_cast<uint32_t>(mma_m >> 4) << 24);
   if (static_cast<int64_t>(p.tiles_m) * p.tiles_n > 0x7fffffffLL) return NVB200_ERR_UNSUPPORTED;
-
-  const int smem = 1024 + kStages * (kTileBytesA + bn * 128) + 256;
-  const int rc = f32 ? configure_once<true>(smem) : configure_once<false>(smem);
-  if (rc) return rc;
   const int tiles = p.tiles_m * p.tiles_n;
+
+  if (pair) {
+    const int stage_bytes = kTileBytesA + (bn / 2) * 128;
+    p.stages = std::min(kMaxStages2, (200 * 1024) / stage_bytes);
+    const int smem = 1024 + p.stages * stage_bytes + 256;
+    const int rc = f32 ? configure_once(matmul_tc2_kernel<true>, smem, 2) : configure_once(matmul_tc2_kernel<false>, smem, 3);
+    if (rc) return rc;
+    const unsigned grid = 2u * static_cast<unsigned>(std::min(tiles, sms / 2));
+    if (f32)
+      matmul_tc2_kernel<true><<<grid, kThreads, smem, stream>>>(map_a, map_b, p);
+    else
+      matmul_tc2_kernel<false><<<grid, kThreads, smem, stream>>>(map_a, map_b, p);
+    return launch_status();
+  }
+  const int smem = 1024 + kStages * (kTileBytesA + bn * 128) + 256;
+  const int rc = f32 ? configure_once(matmul_tc_kernel<true>, smem, 0) : configure_once(matmul_tc_kernel<false>, smem, 1);
+  if (rc) return rc;
   const unsigned grid = static_cast<unsigned>(std::min(tiles, sms));
   if (f32)
     matmul_tc_kernel<true><<<grid, kThreads, smem, stream>>>(map_a, map_b, p);
