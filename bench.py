@@ -419,6 +419,7 @@ def decode_worker(backend: str, bs: int, ctx: int) -> dict:
     runner = mr.ModelRunner(cfg, 0, [])
     blocks_per_seq = (ctx + 1 + 255) // 256
     assert cfg.num_kvcache_blocks >= bs * blocks_per_seq
+    torch.inference_mode().__enter__()  # the runner's graph buffers are inference tensors
     g = torch.Generator(device="cuda").manual_seed(1)
     runner.kv_caches["target"].normal_(generator=g)
     gv = runner.graph_vars

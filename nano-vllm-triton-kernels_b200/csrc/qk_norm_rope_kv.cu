@@ -7,12 +7,13 @@
 // Design (bulk path, used whenever every row is 16-byte aligned, i.e. always for qkv_proj views):
 //   * Work unit = one token x a group of G kv heads and the G*R q heads that share them (GQA, R = Hq/Hkv).
 //     Large batches use G = Hkv (one unit per token); small batches split heads so that every SM gets work.
-//   * Two persistent CTAs per SM each own a contiguous range of units (one CTA per SM measured 30 % slower: a
-//     single producer cannot keep enough copies in flight). Warp 0 is the producer: it prefetches 32
+//   * Two or three persistent CTAs per SM (by unit size) each own a contiguous range of units (one CTA per SM
+//     measured 30 % slower: a single producer cannot keep enough copies in flight). Warp 0 is the producer: it
+//     prefetches 32
 //     positions/slots at a time with one coalesced load and moves each unit's q rows, k rows, v rows (only when
 //     the slot is kept) and cos/sin row from HBM into a shared-memory stage with 1-D bulk copies
 //     (cp.async.bulk, completion counted on an mbarrier). Up to 8 stages are in flight per CTA.
-//   * Consumer warps (8) take units round robin. A warp normalises and rotates 32/LPH heads per step in place in
+//   * Consumer warps (8 or 6) each own a fixed set of stages and take the units that land in them. A warp normalises and rotates 32/LPH heads per step in place in
 //     shared memory, each lane holding 8 elements of the first half and the matching 8 of the second half
 //     (LPH = D/16 lanes per head), so RoPE pairs are lane-local and the sum of squares needs log2(LPH) shuffles.
 //   * The finished q rows go to q_out, the k rows to k_out and/or k_cache[slot], and the v rows straight from the
@@ -26,30 +27,39 @@
 namespace nvb200 {
 namespace {
 
-// Tuning constants (the defaults were chosen by measurement on B200; a build may override them with -D).
-#ifndef NVB200_QKNR_CONSUMERS
-#define NVB200_QKNR_CONSUMERS 8
+// Launch shapes, chosen per call by the size of a work unit (one shared-memory stage). Measured on B200 (bench.py,
+// T = 8192): units of >= 11 KB (a Qwen3-8B token, 12.8 KB) run best as 2 CTAs per SM with 8 consumer warps and
+// 8 stages; smaller units (a Qwen3-0.6B token, 8.7 KB) as 3 CTAs per SM with 6 consumer warps. A build may
+// override the constants with -D for tuning sweeps.
+#ifndef NVB200_QKNR_LARGE_CONSUMERS
+#define NVB200_QKNR_LARGE_CONSUMERS 8
 #endif
-#ifndef NVB200_QKNR_MAX_STAGES
-#define NVB200_QKNR_MAX_STAGES 8
+#ifndef NVB200_QKNR_LARGE_CTAS
+#define NVB200_QKNR_LARGE_CTAS 2
 #endif
-#ifndef NVB200_QKNR_CTAS_PER_SM
-#define NVB200_QKNR_CTAS_PER_SM 2
+#ifndef NVB200_QKNR_LARGE_STAGES
+#define NVB200_QKNR_LARGE_STAGES 8
 #endif
-#ifndef NVB200_QKNR_SMEM_BUDGET_KB
-#define NVB200_QKNR_SMEM_BUDGET_KB (200 / NVB200_QKNR_CTAS_PER_SM)
+#ifndef NVB200_QKNR_SMALL_CONSUMERS
+#define NVB200_QKNR_SMALL_CONSUMERS 6
 #endif
-#ifndef NVB200_QKNR_DEFER_RELEASE
-#define NVB200_QKNR_DEFER_RELEASE 0
+#ifndef NVB200_QKNR_SMALL_CTAS
+#define NVB200_QKNR_SMALL_CTAS 3
+#endif
+#ifndef NVB200_QKNR_SMALL_STAGES
+#define NVB200_QKNR_SMALL_STAGES 8
+#endif
+#ifndef NVB200_QKNR_SMALL_UNIT_BYTES
+#define NVB200_QKNR_SMALL_UNIT_BYTES (11 * 1024)
 #endif
 
-constexpr int kConsumerWarps = NVB200_QKNR_CONSUMERS;
-constexpr int kThreads = 32 * (1 + kConsumerWarps);
-constexpr int kMaxStages = NVB200_QKNR_MAX_STAGES;
-constexpr int kCtasPerSm = NVB200_QKNR_CTAS_PER_SM;
-constexpr int kSmemBudget = NVB200_QKNR_SMEM_BUDGET_KB * 1024;  // stage bytes per CTA
-constexpr int kHeaderBytes = 512;                                   // mbarriers and per-stage slot numbers
-static_assert(2 * 8 * kMaxStages + 4 * kMaxStages <= kHeaderBytes, "header too small");
+constexpr int kHeaderBytes = 512;  // mbarriers and per-stage slot numbers
+constexpr int kMaxStagesAny = 16;
+static_assert(2 * 8 * kMaxStagesAny + 4 * kMaxStagesAny <= kHeaderBytes, "header too small");
+static_assert(NVB200_QKNR_LARGE_STAGES <= kMaxStagesAny && NVB200_QKNR_SMALL_STAGES <= kMaxStagesAny, "stages");
+
+// Shared memory of a CTA when `ctas` share an SM (228 KB per SM, 1 KB reserved per CTA).
+constexpr int stage_budget(int ctas) { return (228 * 1024) / ctas - 1024 - kHeaderBytes; }
 
 struct QknrParams {
   __nv_bfloat16 *q_out;
@@ -75,7 +85,7 @@ struct QknrParams {
   int64_t units;    // T * S
   int64_t chunk;    // units per CTA
   int stages;       // pipeline depth
-  int consumers;    // consumer warps in use (<= NVB200_QKNR_CONSUMERS); each owns stages w, w + consumers, ...
+  int consumers;    // consumer warps in use (<= the launch shape's W); each owns stages w, w + consumers, ...
   int qkv_row;      // 1: q, k, v are consecutive in memory (one qkv_proj row per token) and a unit is a whole
                     // token, so one bulk copy moves the unit's q | k | v (v is then read for skipped slots too,
                     // as the reference's byte count assumes)
@@ -120,8 +130,8 @@ NVB200_DEVICE int next_unit(int it, int NS, int W) {
 // ---------------------------------------------------------------------------------------------------------------
 // Bulk-copy pipeline kernel. D in {64, 128, 256}.
 
-template <int D>
-__global__ void __launch_bounds__(kThreads, kCtasPerSm) qknr_bulk_kernel(const __grid_constant__ QknrParams p) {
+template <int D, int W, int CTAS>
+__global__ void __launch_bounds__(32 * (1 + W), CTAS) qknr_bulk_kernel(const __grid_constant__ QknrParams p) {
   constexpr int HALF = D / 2;
   constexpr int LPH = D / 16;    // lanes per head: each lane holds 8 + 8 elements
   constexpr int HPI = 32 / LPH;  // heads per warp step
@@ -131,7 +141,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) qknr_bulk_kernel(const _
   const int lane = threadIdx.x & 31;
   const int NS = p.stages;
   const uint32_t bar_base = smem_addr(smem);  // full[0..NS), empty[0..NS)
-  int32_t *meta = reinterpret_cast<int32_t *>(smem + 2 * 8 * kMaxStages);
+  int32_t *meta = reinterpret_cast<int32_t *>(smem + 2 * 8 * kMaxStagesAny);
   const uint32_t stage_base = smem_addr(smem + kHeaderBytes);
 
   const int64_t first = static_cast<int64_t>(blockIdx.x) * p.chunk;
@@ -220,17 +230,13 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) qknr_bulk_kernel(const _
   load_w8(p.k_w + 8 * j, wk1);
   load_w8(p.k_w + HALF + 8 * j, wk2);
   const int total = nq + p.g;
-  // Deferred release: a stage is handed back one unit later, once its bulk stores have read it, so the warp does
-  // not wait for that read. Needs more stages than consumer warps (each warp then holds at most two).
-  const bool defer = NVB200_QKNR_DEFER_RELEASE && NS >= 2 * p.consumers;
-  int pending_empty = -1;  // stage whose release waits for its bulk stores to finish reading shared memory
 
   // Warp cw owns stages cw, cw + W, ... and consumes exactly the units that land in them, in order. Every waiter
   // of a stage's full barrier thus sees each of its phases, which the parity wait requires (a warp that could run
   // two phases ahead of a stage would read a parity that aliases an older phase).
-  const int W = p.consumers;
-  if (cw >= W) return;
-  for (int it = cw; it < n_units; it = next_unit(it, NS, W)) {
+  const int nw = p.consumers;
+  if (cw >= nw) return;
+  for (int it = cw; it < n_units; it = next_unit(it, NS, nw)) {
     const int st = it % NS;
     const uint32_t ph = (it / NS) & 1;
     const uint32_t full = bar_base + 8 * st, empty = bar_base + 8 * (NS + st);
@@ -295,22 +301,12 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) qknr_bulk_kernel(const _
         bulk_s2g(p.v_cache + off, sv, kb);
       }
       bulk_commit();
-      if (defer) {
-        bulk_wait_read<1>();  // the previous unit's stores have read their stage
-        if (pending_empty >= 0) mbar_arrive(pending_empty);
-        pending_empty = static_cast<int>(empty);
-      } else {
-        bulk_wait_read<0>();
-        mbar_arrive(empty);
-      }
+      bulk_wait_read<0>();  // the stores have read the stage: hand it back to the producer
+      mbar_arrive(empty);
     }
     __syncwarp();
   }
-  if (lane == 0) {
-    bulk_wait_read<0>();
-    if (pending_empty >= 0) mbar_arrive(pending_empty);
-    bulk_wait<0>();
-  }
+  if (lane == 0) bulk_wait<0>();
 }
 
 // ---------------------------------------------------------------------------------------------------------------
@@ -398,23 +394,34 @@ __global__ void __launch_bounds__(32 * kGenericWarps) qknr_generic_kernel(const 
   }
 }
 
-template <int D>
+template <int D, int W, int CTAS, int MAX_STAGES>
 int launch_bulk(QknrParams &p, int sms, cudaStream_t stream) {
+  constexpr int budget = stage_budget(CTAS);
+  p.stages = std::min(MAX_STAGES, budget / p.stage_bytes);
+  if (p.stages < 2) return NVB200_ERR_UNSUPPORTED;  // a unit larger than half the budget: too many heads
+  p.consumers = std::min(W, p.stages);
+  p.stages -= p.stages % p.consumers;  // every consumer warp owns the same number of stages
   const int smem = kHeaderBytes + p.stages * p.stage_bytes;
   static int configured[64] = {0};  // per device: max dynamic shared memory raised once
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 64 && !configured[dev]) {
-    if (cudaFuncSetAttribute(qknr_bulk_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             kHeaderBytes + kSmemBudget) != cudaSuccess)
+    if (cudaFuncSetAttribute(qknr_bulk_kernel<D, W, CTAS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kHeaderBytes + budget) != cudaSuccess)
       return NVB200_ERR_CUDA;
     configured[dev] = 1;
   }
-  const int64_t grid = std::min<int64_t>(p.units, static_cast<int64_t>(sms) * kCtasPerSm);
+  const int64_t grid = std::min<int64_t>(p.units, static_cast<int64_t>(sms) * CTAS);
   p.chunk = (p.units + grid - 1) / grid;
   const int64_t blocks = (p.units + p.chunk - 1) / p.chunk;
-  qknr_bulk_kernel<D><<<static_cast<unsigned>(blocks), kThreads, smem, stream>>>(p);
+  qknr_bulk_kernel<D, W, CTAS><<<static_cast<unsigned>(blocks), 32 * (1 + W), smem, stream>>>(p);
   return launch_status();
+}
+
+template <int D> int launch_bulk_shaped(QknrParams &p, int sms, cudaStream_t stream) {
+  if (p.stage_bytes >= NVB200_QKNR_SMALL_UNIT_BYTES)
+    return launch_bulk<D, NVB200_QKNR_LARGE_CONSUMERS, NVB200_QKNR_LARGE_CTAS, NVB200_QKNR_LARGE_STAGES>(p, sms, stream);
+  return launch_bulk<D, NVB200_QKNR_SMALL_CONSUMERS, NVB200_QKNR_SMALL_CTAS, NVB200_QKNR_SMALL_STAGES>(p, sms, stream);
 }
 
 }  // namespace
@@ -491,14 +498,10 @@ int qk_norm_rope_kv_launch(const nvb200_qk_norm_rope_kv_args *a, cudaStream_t st
               a->k_token_stride == a->v_token_stride;
   const int unit_bytes = (p.g * p.r + 2 * p.g) * D * 2 + D * 4;
   p.stage_bytes = (unit_bytes + 127) / 128 * 128;
-  p.stages = std::min(kMaxStages, kSmemBudget / p.stage_bytes);
-  if (p.stages < 2) return NVB200_ERR_UNSUPPORTED;  // a unit larger than half the budget: too many heads
-  p.consumers = std::min(kConsumerWarps, p.stages);
-  if (p.stages % p.consumers) p.stages -= p.stages % p.consumers;  // every warp owns the same number of stages
   switch (D) {
-    case 64: return launch_bulk<64>(p, sms, stream);
-    case 128: return launch_bulk<128>(p, sms, stream);
-    default: return launch_bulk<256>(p, sms, stream);
+    case 64: return launch_bulk_shaped<64>(p, sms, stream);
+    case 128: return launch_bulk_shaped<128>(p, sms, stream);
+    default: return launch_bulk_shaped<256>(p, sms, stream);
   }
 }
 
