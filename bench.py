@@ -419,34 +419,34 @@ def decode_worker(backend: str, bs: int, ctx: int) -> dict:
     runner = mr.ModelRunner(cfg, 0, [])
     blocks_per_seq = (ctx + 1 + 255) // 256
     assert cfg.num_kvcache_blocks >= bs * blocks_per_seq
-    torch.inference_mode().__enter__()  # the runner's graph buffers are inference tensors
-    g = torch.Generator(device="cuda").manual_seed(1)
-    runner.kv_caches["target"].normal_(generator=g)
-    gv = runner.graph_vars
-    gv["input_ids"][:bs] = torch.randint(0, QWEN3_06B["vocab_size"], (bs,), device="cuda", generator=g)
-    gv["positions"][:bs] = ctx
-    tables = torch.arange(bs * blocks_per_seq, dtype=torch.int32, device="cuda").view(bs, blocks_per_seq)
-    gv["block_tables"].zero_()
-    gv["block_tables"][:bs, :blocks_per_seq] = tables
-    gv["slot_mapping"].fill_(-1)
-    gv["slot_mapping"][:bs] = tables[:, ctx // 256] * 256 + ctx % 256
-    gv["context_lens"].zero_()
-    gv["context_lens"][:bs] = ctx + 1
-    graph = runner.graphs[("target", 1, bs)]
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    for _ in range(10):
-        graph.replay()
-    per_run = []
-    for _ in range(3):
-        start.record()
-        for _ in range(50):
+    with torch.inference_mode():  # the runner's graph buffers are inference tensors
+        g = torch.Generator(device="cuda").manual_seed(1)
+        runner.kv_caches["target"].normal_(generator=g)
+        gv = runner.graph_vars
+        gv["input_ids"][:bs] = torch.randint(0, QWEN3_06B["vocab_size"], (bs,), device="cuda", generator=g)
+        gv["positions"][:bs] = ctx
+        tables = torch.arange(bs * blocks_per_seq, dtype=torch.int32, device="cuda").view(bs, blocks_per_seq)
+        gv["block_tables"].zero_()
+        gv["block_tables"][:bs, :blocks_per_seq] = tables
+        gv["slot_mapping"].fill_(-1)
+        gv["slot_mapping"][:bs] = tables[:, ctx // 256] * 256 + ctx % 256
+        gv["context_lens"].zero_()
+        gv["context_lens"][:bs] = ctx + 1
+        graph = runner.graphs[("target", 1, bs)]
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        for _ in range(10):
             graph.replay()
-        end.record()
-        end.synchronize()
-        per_run.append(start.elapsed_time(end) / 50)
-    out = gv["outputs"]["target"][:bs].float()
-    res = {"backend": backend, "graph_replay_us": 1e3 * sorted(per_run)[1], "runs_us": [1e3 * x for x in per_run],
-           "finite": bool(torch.isfinite(out).all()), "kv_blocks": cfg.num_kvcache_blocks}
+        per_run = []
+        for _ in range(3):
+            start.record()
+            for _ in range(50):
+                graph.replay()
+            end.record()
+            end.synchronize()
+            per_run.append(start.elapsed_time(end) / 50)
+        out = gv["outputs"]["target"][:bs].float()
+        res = {"backend": backend, "graph_replay_us": 1e3 * sorted(per_run)[1], "runs_us": [1e3 * x for x in per_run],
+               "finite": bool(torch.isfinite(out).all()), "kv_blocks": cfg.num_kvcache_blocks}
     try:
         runner.exit()
     except Exception:

@@ -9,7 +9,8 @@
 //     descriptors into a TMEM accumulator, and tcgen05.commit releases each stage when its MMAs are done. Two TMEM
 //     accumulators (2 x BN columns) let the epilogue of one tile overlap the MMAs of the next.
 //   * Warps 2-5 (the epilogue) read the accumulator with tcgen05.ld (each warp its 32-lane quarter), round to C's
-//     dtype and store.
+//     dtype, stage 32 x 32 chunks in swizzled shared memory and write them with TMA stores (a thread holds one row,
+//     so direct stores would scatter every warp instruction over 32 rows).
 // Operand layouts: A and B may each be K-major (the contiguous dim is K: A row-major, B = weight.t()) or MN-major
 // (B row-major [K, N], A column-major); the instruction descriptor's major bits select it, so no transpose pass.
 // Any layout TMA cannot describe (a non-unit inner stride, or a row pitch that is not a multiple of 16 bytes) is
@@ -45,6 +46,9 @@ struct TcParams {
   uint32_t a_swz, b_swz;    // descriptor layout types (2 = 128-byte swizzle, 1 = 128-byte swizzle of 32-byte atoms)
   int elem_bytes;  // 2 (bf16) or 4 (fp32/tf32)
   int c_is_f32;
+  int c_tma;          // 1: C is written by TMA stores from shared-memory staging (row-major C, 16-byte pitch)
+  uint32_t epi_off;   // byte offset of the epilogue staging buffers in shared memory
+  uint32_t hdr_off;   // byte offset of the barriers / TMEM slot
   int32_t *status;
 };
 
@@ -236,6 +240,54 @@ NVB200_DEVICE void store_tile_rows(const TcParams &p, uint32_t taddr, int row, i
   }
 }
 
+NVB200_DEVICE void tma_store_2d(const CUtensorMap *map, int c0, int c1, uint32_t src) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(map), "r"(c0),
+               "r"(c1), "r"(src)
+               : "memory");
+}
+
+// Epilogue through shared memory: per 32-column chunk, each lane converts its row (one TMEM lane) and writes it
+// into a 32 x 32 staging tile (rows of 64 B for bf16 / 128 B for fp32, 16-byte chunks XOR-swizzled as TMA's
+// SWIZZLE_64B / SWIZZLE_128B expect, so the 32 lanes' writes hit distinct banks); lane 0 then TMA-stores the tile,
+// which clips rows >= M and columns >= N. Two staging tiles per warp alternate; a tile is rewritten only after the
+// store issued from it two chunks earlier has read it. `stage` = the warp's two tiles, `chunks` counts its stores.
+NVB200_DEVICE void store_tile_tma(const TcParams &p, const CUtensorMap *map_c, uint32_t taddr, int row0, int col_base,
+                                  int ncols, uint32_t stage, int &chunks) {
+  const int lane = threadIdx.x & 31;
+  const int row_bytes = p.c_is_f32 ? 128 : 64;
+  for (int c0 = 0; c0 < ncols; c0 += 32) {
+    float v[32];
+    tmem_ld32(taddr + c0, v);
+    if (row0 >= p.M || col_base + c0 >= p.N) continue;
+    const uint32_t buf = stage + (chunks & 1) * 32 * row_bytes;
+    if (chunks >= 2 && lane == 0) bulk_wait_read<1>();
+    __syncwarp();
+    const uint32_t row_addr = buf + lane * row_bytes;
+    if (p.c_is_f32) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const uint4 w = make_uint4(__float_as_uint(v[4 * j]), __float_as_uint(v[4 * j + 1]),
+                                   __float_as_uint(v[4 * j + 2]), __float_as_uint(v[4 * j + 3]));
+        st_shared_v4(row_addr + ((j ^ (lane & 7)) << 4), w);
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float f[8] = {v[8 * j], v[8 * j + 1], v[8 * j + 2], v[8 * j + 3],
+                            v[8 * j + 4], v[8 * j + 5], v[8 * j + 6], v[8 * j + 7]};
+        st_shared_v4(row_addr + ((j ^ ((lane >> 1) & 3)) << 4), pack8(f));
+      }
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_2d(map_c, col_base + c0, row0, buf);
+      bulk_commit();
+    }
+    ++chunks;
+  }
+}
+
 // Stage layout (each operand tile 1024-byte aligned, as the 128-byte swizzle requires):
 //   A: BM x BK, K-major: row m at m * 128 B.            MN-major: BK rows of 128 B per 128-byte MN block.
 //   B: BN x BK, K-major: row n at n * 128 B.            MN-major: BK rows of 128 B per 128-byte MN block.
@@ -243,14 +295,14 @@ NVB200_DEVICE void store_tile_rows(const TcParams &p, uint32_t taddr, int row, i
 template <bool TF32>
 __global__ void __launch_bounds__(kThreads, 1)
     matmul_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-                     const __grid_constant__ TcParams p) {
+                     const __grid_constant__ CUtensorMap map_c, const __grid_constant__ TcParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int tile_b_bytes = p.bn * 128;
   const int stage_bytes = kTileBytesA + tile_b_bytes;
-  uint8_t *hdr = smem + kStages * stage_bytes;
+  uint8_t *hdr = smem + p.hdr_off;
   const uint32_t bar_full = smem_addr(hdr);            // kStages x 8
   const uint32_t bar_empty = bar_full + 8 * kStages;   // kStages x 8
   const uint32_t bar_acc_full = bar_empty + 8 * kStages;  // 2 x 8
@@ -359,6 +411,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ---------------------------------------------------------------- epilogue: TMEM -> registers -> C
     const int q = warp & 3;  // TMEM lane quarter this warp may read
+    const uint32_t epi_stage = smem_addr(smem) + p.epi_off + (warp - 2) * 64 * (p.c_is_f32 ? 128 : 64);
+    int chunks = 0;
     int local = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
       int pm, pn;
@@ -370,14 +424,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
-      store_tile_rows(p, tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * p.bn, pm * BM + q * 32 + lane,
-                      pn * p.bn, p.bn);
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * p.bn;
+      if (p.c_tma)
+        store_tile_tma(p, &map_c, taddr, pm * BM + q * 32, pn * p.bn, p.bn, epi_stage, chunks);
+      else
+        store_tile_rows(p, taddr, pm * BM + q * 32 + lane, pn * p.bn, p.bn);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar_acc_empty + 8 * buf);
     }
   }
 
+  if (warp >= 2 && lane == 0) bulk_wait<0>();  // epilogue TMA stores complete
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
@@ -396,7 +454,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 template <bool TF32>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     matmul_tc2_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-                      const __grid_constant__ TcParams p) {
+                      const __grid_constant__ CUtensorMap map_c, const __grid_constant__ TcParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5;
@@ -407,7 +465,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const int tile_b_bytes = half_bn * 128;
   const int stage_bytes = kTileBytesA + tile_b_bytes;
   const int stages = p.stages;
-  uint8_t *hdr = smem + stages * stage_bytes;
+  uint8_t *hdr = smem + p.hdr_off;
   const uint32_t bar_full = smem_addr(hdr);                 // stages x 8 (used in the leader)
   const uint32_t bar_empty = bar_full + 8 * kMaxStages2;    // stages x 8 (both CTAs)
   const uint32_t bar_acc_full = bar_empty + 8 * kMaxStages2;  // 2 x 8 (both CTAs)
@@ -516,6 +574,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     // ---------------------------------------------------------------- epilogue (both CTAs, own TMEM lanes)
     const int q = warp & 3;
     const uint32_t leader_acc_empty = map_to_cta(bar_acc_empty, 0);
+    const uint32_t epi_stage = smem_addr(smem) + p.epi_off + (warp - 2) * 64 * (p.c_is_f32 ? 128 : 64);
+    int chunks = 0;
     int local = 0;
     for (int tile = cluster; tile < num_tiles; tile += clusters, ++local) {
       int pm, pn;
@@ -527,14 +587,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
-      store_tile_rows(p, tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * p.bn,
-                      pm * 2 * BM + static_cast<int>(rank) * BM + q * 32 + lane, pn * p.bn, p.bn);
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * p.bn;
+      const int row0 = pm * 2 * BM + static_cast<int>(rank) * BM + q * 32;
+      if (p.c_tma)
+        store_tile_tma(p, &map_c, taddr, row0, pn * p.bn, p.bn, epi_stage, chunks);
+      else
+        store_tile_rows(p, taddr, row0 + lane, pn * p.bn, p.bn);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(leader_acc_empty + 8 * buf);
     }
   }
 
+  if (warp >= 2 && lane == 0) bulk_wait<0>();  // epilogue TMA stores complete
   tc_fence_before();
   cluster_sync();  // the peer's MMAs and remote arrivals are done before TMEM and shared memory go away
   if (warp == 1) {
@@ -578,6 +643,25 @@ bool make_map(CUtensorMap *map, const void *base, bool f32, int64_t inner, int64
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
+
+// Map of C for the epilogue's TMA stores: [M, N] row-major with pitch `pitch`, boxes of 32 x 32 elements, the
+// swizzle matching the staging tiles (64-byte rows for bf16, 128-byte rows for fp32).
+bool make_map_c(CUtensorMap *map, void *base, bool f32, int64_t M, int64_t N, int64_t pitch) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return false;
+  const int es = f32 ? 4 : 2;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(M)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(pitch * es)};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  const CUresult r = fn(map, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, dims,
+                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        f32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                        CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+constexpr int kMaxDynamicSmem = 227 * 1024;
 
 template <typename Kernel> int configure_once(Kernel kernel, int smem, int slot) {
   static int configured[4][64] = {{0}};
@@ -645,6 +729,11 @@ int matmul_tc_launch(void *c, const void *a, const void *b, int64_t M, int64_t N
   p.elem_bytes = es;
   p.c_is_f32 = f32;
   p.status = status;
+  // C through shared memory and TMA stores when C is row-major with a 16-byte pitch; direct stores otherwise.
+  CUtensorMap map_c;
+  p.c_tma = scn == 1 && (scm * es) % 16 == 0 && aligned16(c) && make_map_c(&map_c, c, f32, M, N, scm);
+  if (!p.c_tma) map_c = map_a;  // unused
+  const int epi_bytes = p.c_tma ? kEpilogueWarps * 2 * 32 * 32 * es : 0;
   // Instruction descriptor: D fp32 (bits 4-5 = 1), A/B format (bits 7-9, 10-12: 1 = bf16, 2 = tf32), major bits
   // 15/16 (1 = MN-major), N >> 3 at bit 17, M >> 4 at bit 24 (M = 256 for a CTA pair).
   const uint32_t fmt = f32 ? 2u : 1u;
@@ -655,27 +744,33 @@ int matmul_tc_launch(void *c, const void *a, const void *b, int64_t M, int64_t N
   if (static_cast<int64_t>(p.tiles_m) * p.tiles_n > 0x7fffffffLL) return NVB200_ERR_UNSUPPORTED;
   const int tiles = p.tiles_m * p.tiles_n;
 
+  // Shared memory: 1 KB alignment slack | stages | epilogue staging | 256 B of barriers and the TMEM slot.
   if (pair) {
     const int stage_bytes = kTileBytesA + (bn / 2) * 128;
-    p.stages = std::min(kMaxStages2, (200 * 1024) / stage_bytes);
-    const int smem = 1024 + p.stages * stage_bytes + 256;
+    p.stages = std::min(kMaxStages2, (kMaxDynamicSmem - 1024 - 256 - epi_bytes) / stage_bytes);
+    p.epi_off = p.stages * stage_bytes;
+    p.hdr_off = p.epi_off + epi_bytes;
+    const int smem = 1024 + p.hdr_off + 256;
     const int rc = f32 ? configure_once(matmul_tc2_kernel<true>, smem, 2) : configure_once(matmul_tc2_kernel<false>, smem, 3);
     if (rc) return rc;
     const unsigned grid = 2u * static_cast<unsigned>(std::min(tiles, sms / 2));
     if (f32)
-      matmul_tc2_kernel<true><<<grid, kThreads, smem, stream>>>(map_a, map_b, p);
+      matmul_tc2_kernel<true><<<grid, kThreads, smem, stream>>>(map_a, map_b, map_c, p);
     else
-      matmul_tc2_kernel<false><<<grid, kThreads, smem, stream>>>(map_a, map_b, p);
+      matmul_tc2_kernel<false><<<grid, kThreads, smem, stream>>>(map_a, map_b, map_c, p);
     return launch_status();
   }
-  const int smem = 1024 + kStages * (kTileBytesA + bn * 128) + 256;
+  p.epi_off = kStages * (kTileBytesA + bn * 128);
+  p.hdr_off = p.epi_off + epi_bytes;
+  const int smem = 1024 + p.hdr_off + 256;
+  if (smem > kMaxDynamicSmem) return NVB200_ERR_UNSUPPORTED;
   const int rc = f32 ? configure_once(matmul_tc_kernel<true>, smem, 0) : configure_once(matmul_tc_kernel<false>, smem, 1);
   if (rc) return rc;
   const unsigned grid = static_cast<unsigned>(std::min(tiles, sms));
   if (f32)
-    matmul_tc_kernel<true><<<grid, kThreads, smem, stream>>>(map_a, map_b, p);
+    matmul_tc_kernel<true><<<grid, kThreads, smem, stream>>>(map_a, map_b, map_c, p);
   else
-    matmul_tc_kernel<false><<<grid, kThreads, smem, stream>>>(map_a, map_b, p);
+    matmul_tc_kernel<false><<<grid, kThreads, smem, stream>>>(map_a, map_b, map_c, p);
   return launch_status();
 }
 

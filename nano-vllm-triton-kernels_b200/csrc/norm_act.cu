@@ -8,10 +8,10 @@
 // where T(.) rounds to the tensor dtype (bf16, fp16 or fp32) and the product of two bf16/fp16 values is exact in
 // fp32, so T(a * b) equals torch's dtype multiply.
 //
-// These ops are HBM-bound (bytes per row: rms 2n, add_rms 4n, silu 3n elements). Rows of up to 2048 bf16 elements
-// (1024 fp32) live in registers: a group of L lanes (L a power of two <= 32) owns a row, each lane moves 16-byte
-// vectors, so a warp keeps 4-8 independent 16-byte loads in flight per lane and the sum of squares takes log2(L)
-// shuffles. Longer rows use one CTA per row with a second pass over the row (served from L2).
+// These ops are HBM-bound (bytes per row: rms 2n, add_rms 4n, silu 3n elements). Every row lives in registers, up
+// to 4 16-byte vectors per thread: rows of up to 1024 bf16 elements (512 fp32) take a group of L lanes (L a power of
+// two <= 32, sum of squares by log2(L) shuffles), rows up to 32768 bf16 elements one CTA each (block reduction).
+// Longer rows take a CTA and a second pass over the row (served from L2).
 #include <algorithm>
 
 #include "common.cuh"
@@ -20,44 +20,54 @@ namespace nvb200 {
 namespace {
 
 constexpr int kRowThreads = 256;
-constexpr int kMaxVecPerLane = 8;
+constexpr int kVecPerThread = 4;        // 16-byte vectors a thread holds of its row
+constexpr int kMaxBlockThreads = 1024;  // block-per-row kernel: threads per row
 
-// VEC consecutive elements of type T as fp32.
+// VEC consecutive elements of type T: raw 16-byte (or scalar) loads and stores, and conversion to/from fp32.
 template <typename T, int VEC> struct VecIO;
 template <> struct VecIO<__nv_bfloat16, 8> {
-  static NVB200_DEVICE void load(const __nv_bfloat16 *p, float (&f)[8]) {
-    unpack8(*reinterpret_cast<const uint4 *>(p), f);
-  }
+  using Raw = uint4;
+  static NVB200_DEVICE Raw load_raw(const __nv_bfloat16 *p) { return *reinterpret_cast<const uint4 *>(p); }
+  static NVB200_DEVICE void unpack(const Raw &r, float (&f)[8]) { unpack8(r, f); }
+  static NVB200_DEVICE void load(const __nv_bfloat16 *p, float (&f)[8]) { unpack8(load_raw(p), f); }
   static NVB200_DEVICE void store(__nv_bfloat16 *p, const float (&f)[8]) { *reinterpret_cast<uint4 *>(p) = pack8(f); }
 };
 template <> struct VecIO<__half, 8> {
-  static NVB200_DEVICE void load(const __half *p, float (&f)[8]) {
-    union { uint4 u; __half2 h[4]; } v;
-    v.u = *reinterpret_cast<const uint4 *>(p);
+  using Raw = uint4;
+  static NVB200_DEVICE Raw load_raw(const __half *p) { return *reinterpret_cast<const uint4 *>(p); }
+  static NVB200_DEVICE void unpack(const Raw &r, float (&f)[8]) {
+    const uint32_t w[4] = {r.x, r.y, r.z, r.w};
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const float2 t = __half22float2(v.h[i]);
+      const float2 t = __half22float2(*reinterpret_cast<const __half2 *>(&w[i]));
       f[2 * i] = t.x;
       f[2 * i + 1] = t.y;
     }
   }
+  static NVB200_DEVICE void load(const __half *p, float (&f)[8]) { unpack(load_raw(p), f); }
   static NVB200_DEVICE void store(__half *p, const float (&f)[8]) {
-    union { uint4 u; __half2 h[4]; } v;
+    uint32_t w[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) v.h[i] = __floats2half2_rn(f[2 * i], f[2 * i + 1]);
-    *reinterpret_cast<uint4 *>(p) = v.u;
+    for (int i = 0; i < 4; ++i) {
+      const __half2 h = __floats2half2_rn(f[2 * i], f[2 * i + 1]);
+      w[i] = *reinterpret_cast<const uint32_t *>(&h);
+    }
+    *reinterpret_cast<uint4 *>(p) = make_uint4(w[0], w[1], w[2], w[3]);
   }
 };
 template <> struct VecIO<float, 4> {
-  static NVB200_DEVICE void load(const float *p, float (&f)[4]) {
-    const float4 v = *reinterpret_cast<const float4 *>(p);
-    f[0] = v.x, f[1] = v.y, f[2] = v.z, f[3] = v.w;
-  }
+  using Raw = float4;
+  static NVB200_DEVICE Raw load_raw(const float *p) { return *reinterpret_cast<const float4 *>(p); }
+  static NVB200_DEVICE void unpack(const Raw &v, float (&f)[4]) { f[0] = v.x, f[1] = v.y, f[2] = v.z, f[3] = v.w; }
+  static NVB200_DEVICE void load(const float *p, float (&f)[4]) { unpack(load_raw(p), f); }
   static NVB200_DEVICE void store(float *p, const float (&f)[4]) {
     *reinterpret_cast<float4 *>(p) = make_float4(f[0], f[1], f[2], f[3]);
   }
 };
 template <typename T> struct VecIO<T, 1> {
+  using Raw = T;
+  static NVB200_DEVICE Raw load_raw(const T *p) { return *p; }
+  static NVB200_DEVICE void unpack(const Raw &r, float (&f)[1]) { f[0] = Elem<T>::to_f(r); }
   static NVB200_DEVICE void load(const T *p, float (&f)[1]) { f[0] = Elem<T>::to_f(*p); }
   static NVB200_DEVICE void store(T *p, const float (&f)[1]) { *p = Elem<T>::from_f(f[0]); }
 };
@@ -81,30 +91,19 @@ template <typename T> NVB200_DEVICE float norm_out(float v, float rstd, float w)
   return __fmul_rn(round_to<T>(__fmul_rn(v, rstd)), w);
 }
 
+// Loads this thread's vectors of one row (x, plus the residual for ADD, summed in fp32); returns its partial sum of
+// squares.
 template <typename T, int VEC, bool ADD>
-__global__ void __launch_bounds__(kRowThreads) row_norm_kernel(const __grid_constant__ RowArgs a) {
-  const int L = a.lanes;
-  const int64_t row = static_cast<int64_t>(blockIdx.x) * (kRowThreads / L) + threadIdx.x / L;
-  const int li = threadIdx.x % L;
-  const bool live = row < a.rows;
-  const T *x = static_cast<const T *>(a.x);
-  const T *r = static_cast<const T *>(a.r);
-  const T *w = static_cast<const T *>(a.w);
-  int64_t xoff = 0, roff = 0;
-  if (live) {
-    xoff = (row / a.rows_per_group) * a.x_group_stride + (row % a.rows_per_group) * a.x_row_stride;
-    roff = row * a.r_row_stride;
-  }
-  float v[kMaxVecPerLane][VEC];
+NVB200_DEVICE float load_row(const T *x, const T *r, int n, int first, int step, float (&v)[kVecPerThread][VEC]) {
   float ss = 0.f;
 #pragma unroll
-  for (int k = 0; k < kMaxVecPerLane; ++k) {
-    const int col = (k * L + li) * VEC;
-    if (live && col < a.n) {
-      VecIO<T, VEC>::load(x + xoff + col, v[k]);
+  for (int k = 0; k < kVecPerThread; ++k) {
+    const int col = (first + k * step) * VEC;
+    if (col < n) {
+      VecIO<T, VEC>::load(x + col, v[k]);
       if (ADD) {
         float rv[VEC];
-        VecIO<T, VEC>::load(r + roff + col, rv);
+        VecIO<T, VEC>::load(r + col, rv);
 #pragma unroll
         for (int e = 0; e < VEC; ++e) v[k][e] = __fadd_rn(v[k][e], rv[e]);
       }
@@ -112,15 +111,16 @@ __global__ void __launch_bounds__(kRowThreads) row_norm_kernel(const __grid_cons
       for (int e = 0; e < VEC; ++e) ss = fmaf(v[k][e], v[k][e], ss);
     }
   }
-  for (int o = L / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-  if (!live) return;
-  const float rstd = rsqrtf(ss / static_cast<float>(a.n) + a.eps);
-  T *y = static_cast<T *>(a.y) + row * a.n;
-  T *so = ADD ? static_cast<T *>(a.res_out) + row * a.n : nullptr;
+  return ss;
+}
+
+template <typename T, int VEC, bool ADD>
+NVB200_DEVICE void store_row(T *y, T *so, const T *w, int n, int first, int step, float rstd,
+                             const float (&v)[kVecPerThread][VEC]) {
 #pragma unroll
-  for (int k = 0; k < kMaxVecPerLane; ++k) {
-    const int col = (k * L + li) * VEC;
-    if (col < a.n) {
+  for (int k = 0; k < kVecPerThread; ++k) {
+    const int col = (first + k * step) * VEC;
+    if (col < n) {
       float wv[VEC], out[VEC];
       VecIO<T, VEC>::load(w + col, wv);
       if (ADD) VecIO<T, VEC>::store(so + col, v[k]);
@@ -131,7 +131,49 @@ __global__ void __launch_bounds__(kRowThreads) row_norm_kernel(const __grid_cons
   }
 }
 
-// Rows longer than the register kernel holds: one CTA per row, sum of squares first, then a second pass.
+// A group of L lanes (a power of two <= 32) per row; a CTA holds 256 / L rows.
+template <typename T, int VEC, bool ADD>
+__global__ void __launch_bounds__(kRowThreads) row_norm_kernel(const __grid_constant__ RowArgs a) {
+  const int L = a.lanes;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * (kRowThreads / L) + threadIdx.x / L;
+  const int li = threadIdx.x % L;
+  const bool live = row < a.rows;
+  const T *x = static_cast<const T *>(a.x);
+  const T *r = static_cast<const T *>(a.r);
+  float v[kVecPerThread][VEC];
+  float ss = 0.f;
+  if (live) {
+    const int64_t xoff = (row / a.rows_per_group) * a.x_group_stride + (row % a.rows_per_group) * a.x_row_stride;
+    ss = load_row<T, VEC, ADD>(x + xoff, ADD ? r + row * a.r_row_stride : nullptr, a.n, li, L, v);
+  }
+  for (int o = L / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if (!live) return;
+  const float rstd = rsqrtf(ss / static_cast<float>(a.n) + a.eps);
+  store_row<T, VEC, ADD>(static_cast<T *>(a.y) + row * a.n, ADD ? static_cast<T *>(a.res_out) + row * a.n : nullptr,
+                         static_cast<const T *>(a.w), a.n, li, L, rstd, v);
+}
+
+// One CTA (blockDim.x threads, a multiple of 32) per row, the row in registers, a block-wide sum of squares.
+template <typename T, int VEC, bool ADD>
+__global__ void __launch_bounds__(kMaxBlockThreads) block_row_norm_kernel(const __grid_constant__ RowArgs a) {
+  __shared__ float partial[kMaxBlockThreads / 32];
+  const int64_t row = blockIdx.x;
+  const T *x = static_cast<const T *>(a.x) + (row / a.rows_per_group) * a.x_group_stride +
+               (row % a.rows_per_group) * a.x_row_stride;
+  const T *r = ADD ? static_cast<const T *>(a.r) + row * a.r_row_stride : nullptr;
+  float v[kVecPerThread][VEC];
+  float ss = load_row<T, VEC, ADD>(x, r, a.n, threadIdx.x, blockDim.x, v);
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((threadIdx.x & 31) == 0) partial[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+  for (int i = 0; i < static_cast<int>(blockDim.x >> 5); ++i) tot += partial[i];
+  const float rstd = rsqrtf(tot / static_cast<float>(a.n) + a.eps);
+  store_row<T, VEC, ADD>(static_cast<T *>(a.y) + row * a.n, ADD ? static_cast<T *>(a.res_out) + row * a.n : nullptr,
+                         static_cast<const T *>(a.w), a.n, threadIdx.x, blockDim.x, rstd, v);
+}
+
+// Rows longer than a CTA holds in registers: one CTA per row, sum of squares first, then a second pass.
 template <typename T, bool ADD>
 __global__ void __launch_bounds__(kRowThreads) long_row_norm_kernel(const __grid_constant__ RowArgs a) {
   __shared__ float partial[kRowThreads / 32];
@@ -165,26 +207,33 @@ __global__ void __launch_bounds__(kRowThreads) long_row_norm_kernel(const __grid
   }
 }
 
-template <typename T, bool ADD> int launch_norm(RowArgs &a, bool vec_ok, cudaStream_t stream) {
-  constexpr int VEC = sizeof(T) == 4 ? 4 : 8;
-  const int vec = vec_ok && a.n % VEC == 0 ? VEC : 1;
-  const int nvec = a.n / vec;
-  if (nvec > 32 * kMaxVecPerLane) {
-    if (a.rows > 0x7fffffffLL) return NVB200_ERR_UNSUPPORTED;
-    long_row_norm_kernel<T, ADD><<<static_cast<unsigned>(a.rows), kRowThreads, 0, stream>>>(a);
+template <typename T, int VEC, bool ADD> int launch_norm_vec(RowArgs &a, cudaStream_t stream) {
+  const int nvec = (a.n + VEC - 1) / VEC;
+  if (nvec <= 32 * kVecPerThread) {
+    int L = 1;
+    while (L < 32 && L * kVecPerThread < nvec) L *= 2;
+    a.lanes = L;
+    const int64_t rows_per_block = kRowThreads / L;
+    const int64_t blocks = (a.rows + rows_per_block - 1) / rows_per_block;
+    if (blocks > 0x7fffffffLL) return NVB200_ERR_UNSUPPORTED;
+    row_norm_kernel<T, VEC, ADD><<<static_cast<unsigned>(blocks), kRowThreads, 0, stream>>>(a);
     return launch_status();
   }
-  int L = 1;
-  while (L < 32 && (L * 4 < nvec || L * kMaxVecPerLane < nvec)) L *= 2;
-  a.lanes = L;
-  const int64_t rows_per_block = kRowThreads / L;
-  const int64_t blocks = (a.rows + rows_per_block - 1) / rows_per_block;
-  if (blocks > 0x7fffffffLL) return NVB200_ERR_UNSUPPORTED;
-  if (vec == VEC)
-    row_norm_kernel<T, VEC, ADD><<<static_cast<unsigned>(blocks), kRowThreads, 0, stream>>>(a);
-  else
-    row_norm_kernel<T, 1, ADD><<<static_cast<unsigned>(blocks), kRowThreads, 0, stream>>>(a);
+  if (a.rows > 0x7fffffffLL) return NVB200_ERR_UNSUPPORTED;
+  if (nvec <= kMaxBlockThreads * kVecPerThread) {
+    int threads = 64;
+    while (threads * kVecPerThread < nvec) threads *= 2;
+    block_row_norm_kernel<T, VEC, ADD><<<static_cast<unsigned>(a.rows), threads, 0, stream>>>(a);
+    return launch_status();
+  }
+  long_row_norm_kernel<T, ADD><<<static_cast<unsigned>(a.rows), kRowThreads, 0, stream>>>(a);
   return launch_status();
+}
+
+template <typename T, bool ADD> int launch_norm(RowArgs &a, bool vec_ok, cudaStream_t stream) {
+  constexpr int VEC = sizeof(T) == 4 ? 4 : 8;
+  if (vec_ok && a.n % VEC == 0) return launch_norm_vec<T, VEC, ADD>(a, stream);
+  return launch_norm_vec<T, 1, ADD>(a, stream);
 }
 
 template <bool ADD> int dispatch_norm(RowArgs &a, bool vec_ok, int dtype, cudaStream_t stream) {
@@ -199,7 +248,8 @@ template <bool ADD> int dispatch_norm(RowArgs &a, bool vec_ok, int dtype, cudaSt
 int elem_size(int dtype) { return dtype == NVB200_F32 ? 4 : 2; }
 
 // ---------------------------------------------------------------------------------------------------------------
-// SiLU x Mul: one thread per VEC outputs, grid-stride over rows * n / VEC.
+// SiLU x Mul: thread (x, y) owns vector column x of rows y*R, y*R + 1, ... (R rows per step, all loads of a step
+// issued before any math), grid-stride over row groups; no division on the index path.
 
 template <typename T> NVB200_DEVICE float silu_mul(float g, float u) {
   // torch's silu: x / (1 + exp(-x)) in fp32, rounded to T; then T(silu * up) (exact product for 16-bit T).
@@ -207,21 +257,38 @@ template <typename T> NVB200_DEVICE float silu_mul(float g, float u) {
   return __fmul_rn(round_to<T>(sl), u);
 }
 
+constexpr int kSiluThreads = 128;
+constexpr int kSiluRows = 4;
+
 template <typename T, int VEC>
-__global__ void __launch_bounds__(256) silu_and_mul_kernel(T *out, const T *x, int64_t rows, int n,
-                                                            int64_t x_row_stride) {
+__global__ void __launch_bounds__(kSiluThreads) silu_and_mul_kernel(T *out, const T *x, int64_t rows, int n,
+                                                                     int64_t x_row_stride) {
   const int nv = n / VEC;
-  const int64_t total = rows * nv;
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t row = i / nv;
-    const int col = static_cast<int>(i - row * nv) * VEC;
-    float g[VEC], u[VEC], o[VEC];
-    VecIO<T, VEC>::load(x + row * x_row_stride + col, g);
-    VecIO<T, VEC>::load(x + row * x_row_stride + n + col, u);
+  const int cv = blockIdx.x * kSiluThreads + threadIdx.x;
+  if (cv >= nv) return;
+  const int col = cv * VEC;
+  for (int64_t r0 = static_cast<int64_t>(blockIdx.y) * kSiluRows; r0 < rows;
+       r0 += static_cast<int64_t>(gridDim.y) * kSiluRows) {
+    typename VecIO<T, VEC>::Raw gr[kSiluRows], ur[kSiluRows];
 #pragma unroll
-    for (int e = 0; e < VEC; ++e) o[e] = silu_mul<T>(g[e], u[e]);
-    VecIO<T, VEC>::store(out + row * n + col, o);
+    for (int i = 0; i < kSiluRows; ++i) {
+      if (r0 + i < rows) {
+        const T *src = x + (r0 + i) * x_row_stride + col;
+        gr[i] = VecIO<T, VEC>::load_raw(src);
+        ur[i] = VecIO<T, VEC>::load_raw(src + n);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < kSiluRows; ++i) {
+      if (r0 + i < rows) {
+        float g[VEC], u[VEC], o[VEC];
+        VecIO<T, VEC>::unpack(gr[i], g);
+        VecIO<T, VEC>::unpack(ur[i], u);
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) o[e] = silu_mul<T>(g[e], u[e]);
+        VecIO<T, VEC>::store(out + (r0 + i) * n + col, o);
+      }
+    }
   }
 }
 
@@ -229,16 +296,18 @@ template <typename T> int launch_silu(void *out, const void *x, int64_t rows, in
                                       bool vec_ok, cudaStream_t stream) {
   constexpr int VEC = sizeof(T) == 4 ? 4 : 8;
   const bool vec = vec_ok && n % VEC == 0;
-  const int64_t items = rows * (vec ? n / VEC : n);
-  const int64_t want = (items + 255) / 256;
-  const int64_t cap = static_cast<int64_t>(sm_count()) * 8;  // 8 CTAs of 256 threads per SM, grid-stride beyond
-  const unsigned blocks = static_cast<unsigned>(std::max<int64_t>(1, std::min(want, cap)));
+  const int64_t nv = vec ? n / VEC : n;
+  const int64_t gx = (nv + kSiluThreads - 1) / kSiluThreads;
+  if (gx > 0x7fffffffLL) return NVB200_ERR_UNSUPPORTED;
+  const int64_t want_y = (rows + kSiluRows - 1) / kSiluRows;
+  const int64_t cap_y = std::max<int64_t>(1, static_cast<int64_t>(sm_count()) * 16 / gx);  // ~16 CTAs per SM
+  const dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(std::min<int64_t>(std::min(want_y, cap_y), 65535)));
   if (vec)
-    silu_and_mul_kernel<T, VEC><<<blocks, 256, 0, stream>>>(static_cast<T *>(out), static_cast<const T *>(x), rows,
-                                                            static_cast<int>(n), stride);
+    silu_and_mul_kernel<T, VEC><<<grid, kSiluThreads, 0, stream>>>(static_cast<T *>(out), static_cast<const T *>(x),
+                                                                    rows, static_cast<int>(n), stride);
   else
-    silu_and_mul_kernel<T, 1><<<blocks, 256, 0, stream>>>(static_cast<T *>(out), static_cast<const T *>(x), rows,
-                                                          static_cast<int>(n), stride);
+    silu_and_mul_kernel<T, 1><<<grid, kSiluThreads, 0, stream>>>(static_cast<T *>(out), static_cast<const T *>(x),
+                                                                  rows, static_cast<int>(n), stride);
   return launch_status();
 }
 
