@@ -91,16 +91,21 @@ template <typename T> NVB200_DEVICE float norm_out(float v, float rstd, float w)
   return __fmul_rn(round_to<T>(__fmul_rn(v, rstd)), w);
 }
 
-// Loads this thread's vectors of one row (x, plus the residual for ADD, summed in fp32); returns its partial sum of
-// squares.
+template <typename T, int VEC> using RawVec = typename VecIO<T, VEC>::Raw;
+
+// Loads this thread's vectors of one row (x, plus the residual for ADD, summed in fp32) and the matching weight
+// vectors (raw, issued with the row's loads so the store pass does not wait for them); returns the thread's
+// partial sum of squares.
 template <typename T, int VEC, bool ADD>
-NVB200_DEVICE float load_row(const T *x, const T *r, int n, int first, int step, float (&v)[kVecPerThread][VEC]) {
+NVB200_DEVICE float load_row(const T *x, const T *r, const T *w, int n, int first, int step,
+                             float (&v)[kVecPerThread][VEC], RawVec<T, VEC> (&wr)[kVecPerThread]) {
   float ss = 0.f;
 #pragma unroll
   for (int k = 0; k < kVecPerThread; ++k) {
     const int col = (first + k * step) * VEC;
     if (col < n) {
       VecIO<T, VEC>::load(x + col, v[k]);
+      wr[k] = VecIO<T, VEC>::load_raw(w + col);
       if (ADD) {
         float rv[VEC];
         VecIO<T, VEC>::load(r + col, rv);
@@ -115,14 +120,14 @@ NVB200_DEVICE float load_row(const T *x, const T *r, int n, int first, int step,
 }
 
 template <typename T, int VEC, bool ADD>
-NVB200_DEVICE void store_row(T *y, T *so, const T *w, int n, int first, int step, float rstd,
-                             const float (&v)[kVecPerThread][VEC]) {
+NVB200_DEVICE void store_row(T *y, T *so, int n, int first, int step, float rstd, const float (&v)[kVecPerThread][VEC],
+                             const RawVec<T, VEC> (&wr)[kVecPerThread]) {
 #pragma unroll
   for (int k = 0; k < kVecPerThread; ++k) {
     const int col = (first + k * step) * VEC;
     if (col < n) {
       float wv[VEC], out[VEC];
-      VecIO<T, VEC>::load(w + col, wv);
+      VecIO<T, VEC>::unpack(wr[k], wv);
       if (ADD) VecIO<T, VEC>::store(so + col, v[k]);
 #pragma unroll
       for (int e = 0; e < VEC; ++e) out[e] = norm_out<T>(v[k][e], rstd, wv[e]);
@@ -141,16 +146,18 @@ __global__ void __launch_bounds__(kRowThreads) row_norm_kernel(const __grid_cons
   const T *x = static_cast<const T *>(a.x);
   const T *r = static_cast<const T *>(a.r);
   float v[kVecPerThread][VEC];
+  RawVec<T, VEC> wr[kVecPerThread];
   float ss = 0.f;
   if (live) {
     const int64_t xoff = (row / a.rows_per_group) * a.x_group_stride + (row % a.rows_per_group) * a.x_row_stride;
-    ss = load_row<T, VEC, ADD>(x + xoff, ADD ? r + row * a.r_row_stride : nullptr, a.n, li, L, v);
+    ss = load_row<T, VEC, ADD>(x + xoff, ADD ? r + row * a.r_row_stride : nullptr, static_cast<const T *>(a.w), a.n,
+                               li, L, v, wr);
   }
   for (int o = L / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
   if (!live) return;
   const float rstd = rsqrtf(ss / static_cast<float>(a.n) + a.eps);
   store_row<T, VEC, ADD>(static_cast<T *>(a.y) + row * a.n, ADD ? static_cast<T *>(a.res_out) + row * a.n : nullptr,
-                         static_cast<const T *>(a.w), a.n, li, L, rstd, v);
+                         a.n, li, L, rstd, v, wr);
 }
 
 // One CTA (blockDim.x threads, a multiple of 32) per row, the row in registers, a block-wide sum of squares.
@@ -162,7 +169,8 @@ __global__ void __launch_bounds__(kMaxBlockThreads) block_row_norm_kernel(const 
                (row % a.rows_per_group) * a.x_row_stride;
   const T *r = ADD ? static_cast<const T *>(a.r) + row * a.r_row_stride : nullptr;
   float v[kVecPerThread][VEC];
-  float ss = load_row<T, VEC, ADD>(x, r, a.n, threadIdx.x, blockDim.x, v);
+  RawVec<T, VEC> wr[kVecPerThread];
+  float ss = load_row<T, VEC, ADD>(x, r, static_cast<const T *>(a.w), a.n, threadIdx.x, blockDim.x, v, wr);
   for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
   if ((threadIdx.x & 31) == 0) partial[threadIdx.x >> 5] = ss;
   __syncthreads();
@@ -170,7 +178,7 @@ __global__ void __launch_bounds__(kMaxBlockThreads) block_row_norm_kernel(const 
   for (int i = 0; i < static_cast<int>(blockDim.x >> 5); ++i) tot += partial[i];
   const float rstd = rsqrtf(tot / static_cast<float>(a.n) + a.eps);
   store_row<T, VEC, ADD>(static_cast<T *>(a.y) + row * a.n, ADD ? static_cast<T *>(a.res_out) + row * a.n : nullptr,
-                         static_cast<const T *>(a.w), a.n, threadIdx.x, blockDim.x, rstd, v);
+                         a.n, threadIdx.x, blockDim.x, rstd, v, wr);
 }
 
 // Rows longer than a CTA holds in registers: one CTA per row, sum of squares first, then a second pass.

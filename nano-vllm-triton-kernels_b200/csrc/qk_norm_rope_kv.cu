@@ -163,58 +163,75 @@ __global__ void __launch_bounds__(32 * (1 + W), CTAS) qknr_bulk_kernel(const __g
 
   if (warp == 0) {
     // ------------------------------------------------------------------ producer
+    // Units go in batches of B = min(NS, 32). For each unit of a batch, lane 0 first issues the q/k/v copies, which
+    // do not depend on its position or slot; then, as the batch's positions arrive, its slot number and cos/sin
+    // row, with the arrive that sets the stage's byte count (copies may complete before it: the count may go
+    // negative in between). Lanes load the next batch's positions and slots while this batch is issued, so the
+    // index loads' latency is hidden after the first batch. B <= NS keeps every stage a batch waits for owned by an
+    // earlier, fully issued batch.
+    const int B = NS < 32 ? NS : 32;
+    const uint32_t v_bytes = store ? kb : 0;  // v is only read when the cache is written
     bool abort = false;
-    for (int base = 0; base < n_units && !abort; base += 32) {
-      int64_t pos = 0;
-      int32_t slot = -1;
-      if (base + lane < n_units) {
-        const int64_t t = (first + base + lane) / p.splits;
-        pos = __ldg(p.positions + t);
-        if (pos < 0 || pos >= p.num_positions) {
-          set_status(p.status, NVB200_STATUS_BAD_POSITION);
-          pos = 0;
-        }
-        if (store) {
-          slot = __ldg(p.slots + t);
-          if (slot < -1 || slot >= p.num_slots) {
-            set_status(p.status, NVB200_STATUS_BAD_SLOT);
-            slot = -1;
+    int64_t pos_next = 0;
+    int32_t slot_next = -1;
+    if (lane < B && lane < n_units) {
+      const int64_t t = (first + lane) / p.splits;
+      pos_next = __ldg(p.positions + t);
+      if (store) slot_next = __ldg(p.slots + t);
+    }
+    for (int base = 0; base < n_units && !abort; base += B) {
+      const int64_t pos = pos_next;
+      const int32_t slot = slot_next;
+      if (base + B + lane < n_units && lane < B) {
+        const int64_t t = (first + base + B + lane) / p.splits;
+        pos_next = __ldg(p.positions + t);
+        if (store) slot_next = __ldg(p.slots + t);
+      }
+      const int cnt = min(B, n_units - base);
+      if (lane == 0) {
+        for (int j = 0; j < cnt; ++j) {
+          const int it = base + j;
+          const int st = it % NS;
+          const uint32_t full = bar_base + 8 * st, empty = bar_base + 8 * (NS + st);
+          if (!mbar_wait_bounded(empty, ((it / NS) & 1) ^ 1)) {
+            set_status(p.status, NVB200_STATUS_WAIT_TIMEOUT);
+            abort = true;
+            break;
+          }
+          const int64_t unit = first + it;
+          const int64_t t = unit / p.splits;
+          const int s = static_cast<int>(unit % p.splits);
+          const uint32_t sb = stage_base + st * p.stage_bytes;
+          if (p.qkv_row) {
+            bulk_g2s(sb, p.q + t * p.q_stride, qb + 2 * kb, full);
+          } else {
+            bulk_g2s(sb, p.q + t * p.q_stride + static_cast<int64_t>(s) * nq * D, qb, full);
+            bulk_g2s(sb + qb, p.k + t * p.k_stride + static_cast<int64_t>(s) * p.g * D, kb, full);
+            if (v_bytes) bulk_g2s(sb + qb + kb, p.v + t * p.v_stride + static_cast<int64_t>(s) * p.g * D, kb, full);
           }
         }
       }
-      const int cnt = min(32, n_units - base);
+      abort = __shfl_sync(0xffffffffu, abort, 0);
+      if (abort) break;
       for (int j = 0; j < cnt; ++j) {
-        const int64_t pj = __shfl_sync(0xffffffffu, pos, j);
-        const int32_t sj = __shfl_sync(0xffffffffu, slot, j);
+        int64_t pj = __shfl_sync(0xffffffffu, pos, j);
+        int32_t sj = __shfl_sync(0xffffffffu, slot, j);
         if (lane == 0) {
+          if (pj < 0 || pj >= p.num_positions) {
+            set_status(p.status, NVB200_STATUS_BAD_POSITION);
+            pj = 0;
+          }
+          if (sj < -1 || sj >= p.num_slots) {
+            set_status(p.status, NVB200_STATUS_BAD_SLOT);
+            sj = -1;
+          }
           const int it = base + j;
           const int st = it % NS;
-          const uint32_t ph = (it / NS) & 1;
-          const uint32_t full = bar_base + 8 * st, empty = bar_base + 8 * (NS + st);
-          if (!mbar_wait_bounded(empty, ph ^ 1)) {
-            set_status(p.status, NVB200_STATUS_WAIT_TIMEOUT);
-            abort = true;
-          } else {
-            meta[st] = sj;
-            const int64_t unit = first + it;
-            const int64_t t = unit / p.splits;
-            const int s = static_cast<int>(unit % p.splits);
-            const uint32_t sb = stage_base + st * p.stage_bytes;
-            if (p.qkv_row) {
-              mbar_arrive_expect_tx(full, qb + 2 * kb + csb);
-              bulk_g2s(sb, p.q + t * p.q_stride, qb + 2 * kb, full);
-            } else {
-              const uint32_t vbytes = sj >= 0 ? kb : 0;
-              mbar_arrive_expect_tx(full, qb + kb + csb + vbytes);
-              bulk_g2s(sb, p.q + t * p.q_stride + static_cast<int64_t>(s) * nq * D, qb, full);
-              bulk_g2s(sb + qb, p.k + t * p.k_stride + static_cast<int64_t>(s) * p.g * D, kb, full);
-              if (vbytes) bulk_g2s(sb + qb + kb, p.v + t * p.v_stride + static_cast<int64_t>(s) * p.g * D, kb, full);
-            }
-            bulk_g2s(sb + qb + 2 * kb, p.cos_sin + pj * p.cs_stride, csb, full);
-          }
+          const uint32_t full = bar_base + 8 * st;
+          meta[st] = sj;
+          mbar_arrive_expect_tx(full, qb + kb + v_bytes + csb);
+          bulk_g2s(stage_base + st * p.stage_bytes + qb + 2 * kb, p.cos_sin + pj * p.cs_stride, csb, full);
         }
-        abort = __shfl_sync(0xffffffffu, abort, 0);
-        if (abort) break;
       }
     }
     return;
@@ -306,7 +323,7 @@ __global__ void __launch_bounds__(32 * (1 + W), CTAS) qknr_bulk_kernel(const __g
     }
     __syncwarp();
   }
-  if (lane == 0) bulk_wait<0>();
+  // Stores still in flight may finish after the CTA exits; their shared-memory reads are done (waited above).
 }
 
 // ---------------------------------------------------------------------------------------------------------------
