@@ -215,8 +215,16 @@ __global__ void __launch_bounds__(kRowThreads) long_row_norm_kernel(const __grid
   }
 }
 
+constexpr int kFewRows = 512;  // below this many rows, rows of >= 64 vectors take a CTA each, one vector a thread
+
 template <typename T, int VEC, bool ADD> int launch_norm_vec(RowArgs &a, cudaStream_t stream) {
   const int nvec = (a.n + VEC - 1) / VEC;
+  if (a.rows <= kFewRows && nvec >= 64 && nvec <= kMaxBlockThreads) {
+    // Decode-sized batches: spread each row over a CTA so every thread does one vector (short serial chain).
+    const int threads = (nvec + 31) / 32 * 32;
+    block_row_norm_kernel<T, VEC, ADD><<<static_cast<unsigned>(a.rows), threads, 0, stream>>>(a);
+    return launch_status();
+  }
   if (nvec <= 32 * kVecPerThread) {
     int L = 1;
     while (L < 32 && L * kVecPerThread < nvec) L *= 2;
@@ -266,20 +274,20 @@ template <typename T> NVB200_DEVICE float silu_mul(float g, float u) {
 }
 
 constexpr int kSiluThreads = 128;
-constexpr int kSiluRows = 4;
+constexpr int kSiluManyRows = 1024;  // from this many rows on, a thread takes 4 rows per step; below, 1
 
-template <typename T, int VEC>
+template <typename T, int VEC, int ROWS>
 __global__ void __launch_bounds__(kSiluThreads) silu_and_mul_kernel(T *out, const T *x, int64_t rows, int n,
                                                                      int64_t x_row_stride) {
   const int nv = n / VEC;
   const int cv = blockIdx.x * kSiluThreads + threadIdx.x;
   if (cv >= nv) return;
   const int col = cv * VEC;
-  for (int64_t r0 = static_cast<int64_t>(blockIdx.y) * kSiluRows; r0 < rows;
-       r0 += static_cast<int64_t>(gridDim.y) * kSiluRows) {
-    typename VecIO<T, VEC>::Raw gr[kSiluRows], ur[kSiluRows];
+  for (int64_t r0 = static_cast<int64_t>(blockIdx.y) * ROWS; r0 < rows;
+       r0 += static_cast<int64_t>(gridDim.y) * ROWS) {
+    typename VecIO<T, VEC>::Raw gr[ROWS], ur[ROWS];
 #pragma unroll
-    for (int i = 0; i < kSiluRows; ++i) {
+    for (int i = 0; i < ROWS; ++i) {
       if (r0 + i < rows) {
         const T *src = x + (r0 + i) * x_row_stride + col;
         gr[i] = VecIO<T, VEC>::load_raw(src);
@@ -287,7 +295,7 @@ __global__ void __launch_bounds__(kSiluThreads) silu_and_mul_kernel(T *out, cons
       }
     }
 #pragma unroll
-    for (int i = 0; i < kSiluRows; ++i) {
+    for (int i = 0; i < ROWS; ++i) {
       if (r0 + i < rows) {
         float g[VEC], u[VEC], o[VEC];
         VecIO<T, VEC>::unpack(gr[i], g);
@@ -307,15 +315,21 @@ template <typename T> int launch_silu(void *out, const void *x, int64_t rows, in
   const int64_t nv = vec ? n / VEC : n;
   const int64_t gx = (nv + kSiluThreads - 1) / kSiluThreads;
   if (gx > 0x7fffffffLL) return NVB200_ERR_UNSUPPORTED;
-  const int64_t want_y = (rows + kSiluRows - 1) / kSiluRows;
+  // Many rows: 4 rows per step (8 loads in flight per thread). Few rows (decode): one row per step, so that each
+  // thread's serial work stays short and more CTAs share the rows.
+  const int rows_per_step = rows >= kSiluManyRows ? 4 : 1;
+  const int64_t want_y = (rows + rows_per_step - 1) / rows_per_step;
   const int64_t cap_y = std::max<int64_t>(1, static_cast<int64_t>(sm_count()) * 16 / gx);  // ~16 CTAs per SM
   const dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(std::min<int64_t>(std::min(want_y, cap_y), 65535)));
-  if (vec)
-    silu_and_mul_kernel<T, VEC><<<grid, kSiluThreads, 0, stream>>>(static_cast<T *>(out), static_cast<const T *>(x),
-                                                                    rows, static_cast<int>(n), stride);
+  T *o = static_cast<T *>(out);
+  const T *i = static_cast<const T *>(x);
+  const int ni = static_cast<int>(n);
+  if (vec && rows_per_step == 4)
+    silu_and_mul_kernel<T, VEC, 4><<<grid, kSiluThreads, 0, stream>>>(o, i, rows, ni, stride);
+  else if (vec)
+    silu_and_mul_kernel<T, VEC, 1><<<grid, kSiluThreads, 0, stream>>>(o, i, rows, ni, stride);
   else
-    silu_and_mul_kernel<T, 1><<<grid, kSiluThreads, 0, stream>>>(static_cast<T *>(out), static_cast<const T *>(x),
-                                                                  rows, static_cast<int>(n), stride);
+    silu_and_mul_kernel<T, 1, 1><<<grid, kSiluThreads, 0, stream>>>(o, i, rows, ni, stride);
   return launch_status();
 }
 

@@ -163,57 +163,52 @@ __global__ void __launch_bounds__(32 * (1 + W), CTAS) qknr_bulk_kernel(const __g
 
   if (warp == 0) {
     // ------------------------------------------------------------------ producer
-    // Units go in batches of B = min(NS, 32). For each unit of a batch, lane 0 first issues the q/k/v copies, which
-    // do not depend on its position or slot; then, as the batch's positions arrive, its slot number and cos/sin
-    // row, with the arrive that sets the stage's byte count (copies may complete before it: the count may go
-    // negative in between). Lanes load the next batch's positions and slots while this batch is issued, so the
-    // index loads' latency is hidden after the first batch. B <= NS keeps every stage a batch waits for owned by an
-    // earlier, fully issued batch.
-    const int B = NS < 32 ? NS : 32;
+    // Units go in batches of 32, one position and slot per lane, loaded one batch ahead so their latency is hidden
+    // after the first batch. Per unit, lane 0 waits for the stage, issues the q/k/v copies (they do not depend on
+    // the position), then the cos/sin copy and the arrive that sets the stage's byte count (copies may complete
+    // before it: the count may go negative in between).
     const uint32_t v_bytes = store ? kb : 0;  // v is only read when the cache is written
     bool abort = false;
     int64_t pos_next = 0;
     int32_t slot_next = -1;
-    if (lane < B && lane < n_units) {
+    if (lane < n_units) {
       const int64_t t = (first + lane) / p.splits;
       pos_next = __ldg(p.positions + t);
       if (store) slot_next = __ldg(p.slots + t);
     }
-    for (int base = 0; base < n_units && !abort; base += B) {
+    for (int base = 0; base < n_units && !abort; base += 32) {
       const int64_t pos = pos_next;
       const int32_t slot = slot_next;
-      if (base + B + lane < n_units && lane < B) {
-        const int64_t t = (first + base + B + lane) / p.splits;
+      if (base + 32 + lane < n_units) {
+        const int64_t t = (first + base + 32 + lane) / p.splits;
         pos_next = __ldg(p.positions + t);
         if (store) slot_next = __ldg(p.slots + t);
       }
-      const int cnt = min(B, n_units - base);
-      if (lane == 0) {
-        for (int j = 0; j < cnt; ++j) {
-          const int it = base + j;
-          const int st = it % NS;
-          const uint32_t full = bar_base + 8 * st, empty = bar_base + 8 * (NS + st);
+      const int cnt = min(32, n_units - base);
+      for (int j = 0; j < cnt; ++j) {
+        const int it = base + j;
+        const int st = it % NS;
+        const uint32_t full = bar_base + 8 * st, empty = bar_base + 8 * (NS + st);
+        const uint32_t sb = stage_base + st * p.stage_bytes;
+        if (lane == 0) {
           if (!mbar_wait_bounded(empty, ((it / NS) & 1) ^ 1)) {
             set_status(p.status, NVB200_STATUS_WAIT_TIMEOUT);
             abort = true;
-            break;
-          }
-          const int64_t unit = first + it;
-          const int64_t t = unit / p.splits;
-          const int s = static_cast<int>(unit % p.splits);
-          const uint32_t sb = stage_base + st * p.stage_bytes;
-          if (p.qkv_row) {
-            bulk_g2s(sb, p.q + t * p.q_stride, qb + 2 * kb, full);
           } else {
-            bulk_g2s(sb, p.q + t * p.q_stride + static_cast<int64_t>(s) * nq * D, qb, full);
-            bulk_g2s(sb + qb, p.k + t * p.k_stride + static_cast<int64_t>(s) * p.g * D, kb, full);
-            if (v_bytes) bulk_g2s(sb + qb + kb, p.v + t * p.v_stride + static_cast<int64_t>(s) * p.g * D, kb, full);
+            const int64_t unit = first + it;
+            const int64_t t = unit / p.splits;
+            const int s = static_cast<int>(unit % p.splits);
+            if (p.qkv_row) {
+              bulk_g2s(sb, p.q + t * p.q_stride, qb + 2 * kb, full);
+            } else {
+              bulk_g2s(sb, p.q + t * p.q_stride + static_cast<int64_t>(s) * nq * D, qb, full);
+              bulk_g2s(sb + qb, p.k + t * p.k_stride + static_cast<int64_t>(s) * p.g * D, kb, full);
+              if (v_bytes) bulk_g2s(sb + qb + kb, p.v + t * p.v_stride + static_cast<int64_t>(s) * p.g * D, kb, full);
+            }
           }
         }
-      }
-      abort = __shfl_sync(0xffffffffu, abort, 0);
-      if (abort) break;
-      for (int j = 0; j < cnt; ++j) {
+        abort = __shfl_sync(0xffffffffu, abort, 0);
+        if (abort) break;
         int64_t pj = __shfl_sync(0xffffffffu, pos, j);
         int32_t sj = __shfl_sync(0xffffffffu, slot, j);
         if (lane == 0) {
@@ -225,12 +220,9 @@ __global__ void __launch_bounds__(32 * (1 + W), CTAS) qknr_bulk_kernel(const __g
             set_status(p.status, NVB200_STATUS_BAD_SLOT);
             sj = -1;
           }
-          const int it = base + j;
-          const int st = it % NS;
-          const uint32_t full = bar_base + 8 * st;
           meta[st] = sj;
           mbar_arrive_expect_tx(full, qb + kb + v_bytes + csb);
-          bulk_g2s(stage_base + st * p.stage_bytes + qb + 2 * kb, p.cos_sin + pj * p.cs_stride, csb, full);
+          bulk_g2s(sb + qb + 2 * kb, p.cos_sin + pj * p.cs_stride, csb, full);
         }
       }
     }
@@ -324,6 +316,110 @@ __global__ void __launch_bounds__(32 * (1 + W), CTAS) qknr_bulk_kernel(const __g
     __syncwarp();
   }
   // Stores still in flight may finish after the CTA exits; their shared-memory reads are done (waited above).
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Direct kernel for small batches (decode): no staging, so the latency is one position load and the cos/sin row
+// behind it, in parallel with the q/k/v loads. One warp handles 32/LPH heads of one token with the bulk consumer's
+// lane layout (8 + 8 elements per lane, 16-byte loads and stores); the warps of a CTA cover a token's q heads,
+// then its k heads, each k-head lane group also copying its v row to the cache. Same 16-byte alignment
+// requirements as the bulk kernel.
+
+constexpr int kDirectWarps = 4;
+constexpr int64_t kDirectMaxTokens = 64;
+
+template <int D>
+__global__ void __launch_bounds__(32 * kDirectWarps) qknr_direct_kernel(const __grid_constant__ QknrParams p) {
+  constexpr int HALF = D / 2;
+  constexpr int LPH = D / 16;
+  constexpr int HPI = 32 / LPH;
+  const int lane = threadIdx.x & 31;
+  const int j = lane % LPH;
+  const int64_t t = blockIdx.x;
+  const int h = (blockIdx.y * kDirectWarps + (threadIdx.x >> 5)) * HPI + lane / LPH;
+  const int total = p.hq + p.hkv;
+  if (h >= total) return;  // whole head groups drop out; the row reduction below stays within a head's lanes
+  const bool isq = h < p.hq;
+  const int hk = h - p.hq;
+  int64_t pos = __ldg(p.positions + t);
+  int32_t slot = -1;
+  if (!isq && p.k_cache != nullptr) slot = __ldg(p.slots + t);
+  const __nv_bfloat16 *x = isq ? p.q + t * p.q_stride + static_cast<int64_t>(h) * D
+                               : p.k + t * p.k_stride + static_cast<int64_t>(hk) * D;
+  const uint4 xa = __ldg(reinterpret_cast<const uint4 *>(x + 8 * j));
+  const uint4 xb = __ldg(reinterpret_cast<const uint4 *>(x + HALF + 8 * j));
+  uint32_t w1[4], w2[4];
+  load_w8((isq ? p.q_w : p.k_w) + 8 * j, w1);
+  load_w8((isq ? p.q_w : p.k_w) + HALF + 8 * j, w2);
+  uint4 va = make_uint4(0, 0, 0, 0), vb = va;
+  const bool kv_store = !isq && p.k_cache != nullptr;
+  if (kv_store) {
+    const __nv_bfloat16 *vr = p.v + t * p.v_stride + static_cast<int64_t>(hk) * D;
+    va = __ldg(reinterpret_cast<const uint4 *>(vr + 8 * j));
+    vb = __ldg(reinterpret_cast<const uint4 *>(vr + HALF + 8 * j));
+  }
+  if (pos < 0 || pos >= p.num_positions) {
+    if (j == 0) set_status(p.status, NVB200_STATUS_BAD_POSITION);
+    pos = 0;
+  }
+  const float *cs = p.cos_sin + pos * p.cs_stride;
+  float c[8], sn[8];
+  {
+    const float4 c0 = __ldg(reinterpret_cast<const float4 *>(cs + 8 * j));
+    const float4 c1 = __ldg(reinterpret_cast<const float4 *>(cs + 8 * j + 4));
+    const float4 s0 = __ldg(reinterpret_cast<const float4 *>(cs + HALF + 8 * j));
+    const float4 s1 = __ldg(reinterpret_cast<const float4 *>(cs + HALF + 8 * j + 4));
+    c[0] = c0.x, c[1] = c0.y, c[2] = c0.z, c[3] = c0.w, c[4] = c1.x, c[5] = c1.y, c[6] = c1.z, c[7] = c1.w;
+    sn[0] = s0.x, sn[1] = s0.y, sn[2] = s0.z, sn[3] = s0.w, sn[4] = s1.x, sn[5] = s1.y, sn[6] = s1.z, sn[7] = s1.w;
+  }
+  float x1[8], x2[8];
+  unpack8(xa, x1);
+  unpack8(xb, x2);
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) ss = fmaf(x1[i], x1[i], ss);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) ss = fmaf(x2[i], x2[i], ss);
+  // The lanes of one head are LPH consecutive lanes; heads past `total` left whole groups, so the xor partners of
+  // every live lane are live.
+  const unsigned group_mask = LPH == 32 ? 0xffffffffu : (((1u << LPH) - 1u) << (lane / LPH * LPH));
+#pragma unroll
+  for (int o = LPH / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(group_mask, ss, o);
+  const float rstd = rsqrtf(ss / static_cast<float>(D) + p.eps);
+  float y1[8], y2[8];
+  norm_rope8(x1, x2, rstd, w1, w2, c, sn, y1, y2);
+  const uint4 ya = pack8(y1), yb = pack8(y2);
+  if (isq) {
+    __nv_bfloat16 *o = p.q_out + (t * p.hq + h) * D;
+    *reinterpret_cast<uint4 *>(o + 8 * j) = ya;
+    *reinterpret_cast<uint4 *>(o + HALF + 8 * j) = yb;
+    return;
+  }
+  if (p.k_out) {
+    __nv_bfloat16 *o = p.k_out + (t * p.hkv + hk) * D;
+    *reinterpret_cast<uint4 *>(o + 8 * j) = ya;
+    *reinterpret_cast<uint4 *>(o + HALF + 8 * j) = yb;
+  }
+  if (kv_store) {
+    if (slot < -1 || slot >= p.num_slots) {
+      if (j == 0) set_status(p.status, NVB200_STATUS_BAD_SLOT);
+      slot = -1;
+    }
+    if (slot >= 0) {
+      const int64_t off = (static_cast<int64_t>(slot) * p.hkv + hk) * D;
+      *reinterpret_cast<uint4 *>(p.k_cache + off + 8 * j) = ya;
+      *reinterpret_cast<uint4 *>(p.k_cache + off + HALF + 8 * j) = yb;
+      *reinterpret_cast<uint4 *>(p.v_cache + off + 8 * j) = va;
+      *reinterpret_cast<uint4 *>(p.v_cache + off + HALF + 8 * j) = vb;
+    }
+  }
+}
+
+template <int D> int launch_direct(QknrParams &p, cudaStream_t stream) {
+  constexpr int heads_per_cta = kDirectWarps * (32 / (D / 16));
+  const dim3 grid(static_cast<unsigned>(p.num_tokens), (p.hq + p.hkv + heads_per_cta - 1) / heads_per_cta);
+  qknr_direct_kernel<D><<<grid, 32 * kDirectWarps, 0, stream>>>(p);
+  return launch_status();
 }
 
 // ---------------------------------------------------------------------------------------------------------------
@@ -496,6 +592,14 @@ int qk_norm_rope_kv_launch(const nvb200_qk_norm_rope_kv_args *a, cudaStream_t st
     if (T > 0x7fffffffLL) return NVB200_ERR_UNSUPPORTED;
     qknr_generic_kernel<<<grid, 32 * kGenericWarps, 0, stream>>>(p, D);
     return launch_status();
+  }
+
+  if (T <= kDirectMaxTokens) {
+    switch (D) {
+      case 64: return launch_direct<64>(p, stream);
+      case 128: return launch_direct<128>(p, stream);
+      default: return launch_direct<256>(p, stream);
+    }
   }
 
   // Heads per unit: as many as possible while the units still cover every SM once.
