@@ -133,13 +133,18 @@ NVB200_DEVICE uint64_t global_timer_ns() {
 constexpr uint64_t kWaitLimitNs = 1000000000ull;
 
 // Waits for the phase of `bar` with the given parity to complete. Returns false if it has not after
-// kWaitLimitNs: the caller then records NVB200_STATUS_WAIT_TIMEOUT and winds its CTA down.
+// kWaitLimitNs: the caller then records NVB200_STATUS_WAIT_TIMEOUT and winds its CTA down. The global timer is only
+// read after 1024 unsuccessful polls (each poll may suspend the thread for a while), so a wait that ends normally
+// never pays for a timer read.
 NVB200_DEVICE bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t start = global_timer_ns();
+  uint64_t start = 0;
   for (uint32_t spin = 1;; ++spin) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((spin & 255u) == 0 && global_timer_ns() - start > kWaitLimitNs) return false;
+    if ((spin & 1023u) == 0) {
+      const uint64_t now = global_timer_ns();
+      if (start == 0) start = now;
+      else if (now - start > kWaitLimitNs) return false;
+    }
   }
 }
 

@@ -215,11 +215,14 @@ __global__ void __launch_bounds__(kRowThreads) long_row_norm_kernel(const __grid
   }
 }
 
-constexpr int kFewRows = 512;  // below this many rows, rows of >= 64 vectors take a CTA each, one vector a thread
+// Up to this many rows, rows of 64..128 vectors (e.g. the 1024-element hidden of Qwen3-0.6B) take one CTA each with
+// one vector per thread (shorter serial chain per thread at decode sizes); measured on B200: better up to ~1024
+// rows, worse beyond, and worse for longer rows, which keep 4 vectors per thread.
+constexpr int kFewRows = 1024;
 
 template <typename T, int VEC, bool ADD> int launch_norm_vec(RowArgs &a, cudaStream_t stream) {
   const int nvec = (a.n + VEC - 1) / VEC;
-  if (a.rows <= kFewRows && nvec >= 64 && nvec <= kMaxBlockThreads) {
+  if (a.rows <= kFewRows && nvec >= 64 && nvec <= 32 * kVecPerThread) {
     // Decode-sized batches: spread each row over a CTA so every thread does one vector (short serial chain).
     const int threads = (nvec + 31) / 32 * 32;
     block_row_norm_kernel<T, VEC, ADD><<<static_cast<unsigned>(a.rows), threads, 0, stream>>>(a);
@@ -264,8 +267,8 @@ template <bool ADD> int dispatch_norm(RowArgs &a, bool vec_ok, int dtype, cudaSt
 int elem_size(int dtype) { return dtype == NVB200_F32 ? 4 : 2; }
 
 // ---------------------------------------------------------------------------------------------------------------
-// SiLU x Mul: thread (x, y) owns vector column x of rows y*R, y*R + 1, ... (R rows per step, all loads of a step
-// issued before any math), grid-stride over row groups; no division on the index path.
+// SiLU x Mul: thread (x, y) owns vector column x of rows y, y + gridDim.y, ...: two 16-byte loads and one store per
+// step, no division on the index path. (Taking 4 rows per step measured no faster at 8192 rows and slower below.)
 
 template <typename T> NVB200_DEVICE float silu_mul(float g, float u) {
   // torch's silu: x / (1 + exp(-x)) in fp32, rounded to T; then T(silu * up) (exact product for 16-bit T).
@@ -274,37 +277,22 @@ template <typename T> NVB200_DEVICE float silu_mul(float g, float u) {
 }
 
 constexpr int kSiluThreads = 128;
-constexpr int kSiluManyRows = 1024;  // from this many rows on, a thread takes 4 rows per step; below, 1
 
-template <typename T, int VEC, int ROWS>
+template <typename T, int VEC>
 __global__ void __launch_bounds__(kSiluThreads) silu_and_mul_kernel(T *out, const T *x, int64_t rows, int n,
                                                                      int64_t x_row_stride) {
   const int nv = n / VEC;
   const int cv = blockIdx.x * kSiluThreads + threadIdx.x;
   if (cv >= nv) return;
   const int col = cv * VEC;
-  for (int64_t r0 = static_cast<int64_t>(blockIdx.y) * ROWS; r0 < rows;
-       r0 += static_cast<int64_t>(gridDim.y) * ROWS) {
-    typename VecIO<T, VEC>::Raw gr[ROWS], ur[ROWS];
+  for (int64_t r = blockIdx.y; r < rows; r += gridDim.y) {
+    const T *src = x + r * x_row_stride + col;
+    float g[VEC], u[VEC], o[VEC];
+    VecIO<T, VEC>::load(src, g);
+    VecIO<T, VEC>::load(src + n, u);
 #pragma unroll
-    for (int i = 0; i < ROWS; ++i) {
-      if (r0 + i < rows) {
-        const T *src = x + (r0 + i) * x_row_stride + col;
-        gr[i] = VecIO<T, VEC>::load_raw(src);
-        ur[i] = VecIO<T, VEC>::load_raw(src + n);
-      }
-    }
-#pragma unroll
-    for (int i = 0; i < ROWS; ++i) {
-      if (r0 + i < rows) {
-        float g[VEC], u[VEC], o[VEC];
-        VecIO<T, VEC>::unpack(gr[i], g);
-        VecIO<T, VEC>::unpack(ur[i], u);
-#pragma unroll
-        for (int e = 0; e < VEC; ++e) o[e] = silu_mul<T>(g[e], u[e]);
-        VecIO<T, VEC>::store(out + (r0 + i) * n + col, o);
-      }
-    }
+    for (int e = 0; e < VEC; ++e) o[e] = silu_mul<T>(g[e], u[e]);
+    VecIO<T, VEC>::store(out + r * n + col, o);
   }
 }
 
@@ -315,21 +303,15 @@ template <typename T> int launch_silu(void *out, const void *x, int64_t rows, in
   const int64_t nv = vec ? n / VEC : n;
   const int64_t gx = (nv + kSiluThreads - 1) / kSiluThreads;
   if (gx > 0x7fffffffLL) return NVB200_ERR_UNSUPPORTED;
-  // Many rows: 4 rows per step (8 loads in flight per thread). Few rows (decode): one row per step, so that each
-  // thread's serial work stays short and more CTAs share the rows.
-  const int rows_per_step = rows >= kSiluManyRows ? 4 : 1;
-  const int64_t want_y = (rows + rows_per_step - 1) / rows_per_step;
   const int64_t cap_y = std::max<int64_t>(1, static_cast<int64_t>(sm_count()) * 16 / gx);  // ~16 CTAs per SM
-  const dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(std::min<int64_t>(std::min(want_y, cap_y), 65535)));
+  const dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(std::min<int64_t>(std::min(rows, cap_y), 65535)));
   T *o = static_cast<T *>(out);
   const T *i = static_cast<const T *>(x);
   const int ni = static_cast<int>(n);
-  if (vec && rows_per_step == 4)
-    silu_and_mul_kernel<T, VEC, 4><<<grid, kSiluThreads, 0, stream>>>(o, i, rows, ni, stride);
-  else if (vec)
-    silu_and_mul_kernel<T, VEC, 1><<<grid, kSiluThreads, 0, stream>>>(o, i, rows, ni, stride);
+  if (vec)
+    silu_and_mul_kernel<T, VEC><<<grid, kSiluThreads, 0, stream>>>(o, i, rows, ni, stride);
   else
-    silu_and_mul_kernel<T, 1, 1><<<grid, kSiluThreads, 0, stream>>>(o, i, rows, ni, stride);
+    silu_and_mul_kernel<T, 1><<<grid, kSiluThreads, 0, stream>>>(o, i, rows, ni, stride);
   return launch_status();
 }
 

@@ -326,7 +326,7 @@ __global__ void __launch_bounds__(32 * (1 + W), CTAS) qknr_bulk_kernel(const __g
 // requirements as the bulk kernel.
 
 constexpr int kDirectWarps = 4;
-constexpr int64_t kDirectMaxTokens = 64;
+constexpr int64_t kDirectMaxTokens = 512;
 
 template <int D>
 __global__ void __launch_bounds__(32 * kDirectWarps) qknr_direct_kernel(const __grid_constant__ QknrParams p) {
