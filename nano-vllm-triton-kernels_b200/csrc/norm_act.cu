@@ -87,6 +87,15 @@ struct RowArgs {
 };
 
 // y = T(T(v * rstd) * w): v * rstd rounded to fp32 then to T, times w in fp32 (exact for 16-bit T), rounded.
+// Element offset of row `row` of x: 2-D views (rows_per_group == 1) need no division; 3-D [T, H, n] views divide in
+// 32 bits (the host guarantees rows < 2^31), avoiding the slow 64-bit division routine on the load path.
+NVB200_DEVICE int64_t row_offset(const RowArgs &a, int64_t row) {
+  if (a.rows_per_group == 1) return row * a.x_group_stride;
+  const uint32_t r = static_cast<uint32_t>(row), h = static_cast<uint32_t>(a.rows_per_group);
+  const uint32_t g = r / h;
+  return static_cast<int64_t>(g) * a.x_group_stride + static_cast<int64_t>(r - g * h) * a.x_row_stride;
+}
+
 template <typename T> NVB200_DEVICE float norm_out(float v, float rstd, float w) {
   return __fmul_rn(round_to<T>(__fmul_rn(v, rstd)), w);
 }
@@ -149,7 +158,7 @@ __global__ void __launch_bounds__(kRowThreads) row_norm_kernel(const __grid_cons
   RawVec<T, VEC> wr[kVecPerThread];
   float ss = 0.f;
   if (live) {
-    const int64_t xoff = (row / a.rows_per_group) * a.x_group_stride + (row % a.rows_per_group) * a.x_row_stride;
+    const int64_t xoff = row_offset(a, row);
     ss = load_row<T, VEC, ADD>(x + xoff, ADD ? r + row * a.r_row_stride : nullptr, static_cast<const T *>(a.w), a.n,
                                li, L, v, wr);
   }
@@ -165,8 +174,7 @@ template <typename T, int VEC, bool ADD>
 __global__ void __launch_bounds__(kMaxBlockThreads) block_row_norm_kernel(const __grid_constant__ RowArgs a) {
   __shared__ float partial[kMaxBlockThreads / 32];
   const int64_t row = blockIdx.x;
-  const T *x = static_cast<const T *>(a.x) + (row / a.rows_per_group) * a.x_group_stride +
-               (row % a.rows_per_group) * a.x_row_stride;
+  const T *x = static_cast<const T *>(a.x) + row_offset(a, row);
   const T *r = ADD ? static_cast<const T *>(a.r) + row * a.r_row_stride : nullptr;
   float v[kVecPerThread][VEC];
   RawVec<T, VEC> wr[kVecPerThread];
@@ -186,8 +194,7 @@ template <typename T, bool ADD>
 __global__ void __launch_bounds__(kRowThreads) long_row_norm_kernel(const __grid_constant__ RowArgs a) {
   __shared__ float partial[kRowThreads / 32];
   const int64_t row = blockIdx.x;
-  const T *x = static_cast<const T *>(a.x) + (row / a.rows_per_group) * a.x_group_stride +
-               (row % a.rows_per_group) * a.x_row_stride;
+  const T *x = static_cast<const T *>(a.x) + row_offset(a, row);
   const T *r = ADD ? static_cast<const T *>(a.r) + row * a.r_row_stride : nullptr;
   const T *w = static_cast<const T *>(a.w);
   T *y = static_cast<T *>(a.y) + row * a.n;
@@ -327,6 +334,7 @@ extern "C" int nvb200_rms_norm(void *y, const void *x, const void *w, int64_t gr
   if (dtype != NVB200_BF16 && dtype != NVB200_F16 && dtype != NVB200_F32) return NVB200_ERR_ARG;
   const int64_t rows = groups * rows_per_group;
   if (rows == 0) return NVB200_OK;
+  if (rows_per_group > 1 && rows > 0x7fffffffLL) return NVB200_ERR_UNSUPPORTED;
   if (!y || !x || !w) return NVB200_ERR_ARG;
   if (int rc = check_device()) return rc;
   const int es = elem_size(dtype);
