@@ -41,6 +41,7 @@ struct TcParams {
   int bn;          // tile N (256 or 128)
   int tiles_m, tiles_n;
   int k_blocks;    // pipeline stages per tile: ceil(K / (BK * ksub))
+  int k_subs;      // 64-element (128-byte) K sub-tiles per tile: ceil(K / BK)
   int ksub;        // 64-element (128-byte) K sub-tiles per stage: one commit releases 4 * ksub MMAs' operands
   int stages;      // pipeline depth
   uint32_t idesc;  // tcgen05 instruction descriptor
@@ -199,9 +200,41 @@ NVB200_DEVICE uint64_t smem_desc(uint32_t addr, uint32_t lbo_bytes, uint32_t sbo
 }
 
 // K sub-tiles of stage kb that hold any of K (the last stage may end early); the rest are neither loaded nor used.
-NVB200_DEVICE int stage_subtiles(const TcParams &p, int kb, int BK) {
-  const int left = (p.K - kb * p.ksub * BK + BK - 1) / BK;
+NVB200_DEVICE int stage_subtiles(const TcParams &p, int kb) {
+  const int left = p.k_subs - kb * p.ksub;
   return left < p.ksub ? left : p.ksub;
+}
+
+// One K sub-tile (BK = 128 bytes of K) is 4 MMAs of UK = 32 bytes of K, for bf16 and tf32 alike.
+constexpr int kMmaPerSub = 4;
+
+// Shared-memory descriptors of stage 0's first A and B sub-tiles and the increments of their address field (16-byte
+// units) per MMA K step, per sub-tile and per stage. The MMA loop only adds these: shared-memory addresses stay
+// below 2^18 bytes, so the 14-bit address field never carries into the next field. Keeping the issue loop down to
+// a few integer adds matters: the issuing thread's work between two tcgen05.mma instructions shows up as tensor-pipe
+// idle time.
+struct OperandDescs {
+  uint64_t a0, b0;
+  uint32_t a_k, b_k;      // one MMA's K step
+  uint32_t a_sub, b_sub;  // one K sub-tile
+  uint32_t stage;         // one stage
+};
+
+NVB200_DEVICE OperandDescs operand_descs(const TcParams &p, uint32_t stage0, int sub_b, int stage_bytes) {
+  const int BK = 128 / p.elem_bytes, UK = 32 / p.elem_bytes;
+  const uint32_t b_base = stage0 + p.ksub * kTileBytesA;
+  // K-major: the K step moves 32 B inside the swizzle row; SBO = 8 rows * 128 B.
+  // MN-major: the K step moves UK rows of 128 B; LBO = next 128-byte MN block (BK rows), SBO = one swizzle atom of
+  // k rows (8 rows, or 4 rows for the 32-byte-atom swizzle).
+  OperandDescs d;
+  d.a0 = p.a_mn_major ? smem_desc(stage0, BK * 128, p.a_sbo, p.a_swz) : smem_desc(stage0, 16, 1024, 2);
+  d.b0 = p.b_mn_major ? smem_desc(b_base, BK * 128, p.b_sbo, p.b_swz) : smem_desc(b_base, 16, 1024, 2);
+  d.a_k = (p.a_mn_major ? UK * 128 : 32) >> 4;
+  d.b_k = (p.b_mn_major ? UK * 128 : 32) >> 4;
+  d.a_sub = kTileBytesA >> 4;
+  d.b_sub = static_cast<uint32_t>(sub_b) >> 4;
+  d.stage = static_cast<uint32_t>(stage_bytes) >> 4;
+  return d;
 }
 
 // GROUP_M-swizzled tile order (nanovllm/kernels/matmul.py:50-57).
@@ -347,21 +380,20 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     // ---------------------------------------------------------------- TMA producer
     if (lane == 0) {
-      int it = 0;
+      int st = 0;
+      uint32_t ph = 0;
       for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
         int pm, pn;
         tile_coords(tile, p.tiles_m, p.tiles_n, pm, pn);
         const int m0 = pm * BM, n0 = pn * p.bn;
-        for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
-          const int st = it % stages;
-          const uint32_t ph = (it / stages) & 1;
+        for (int kb = 0; kb < p.k_blocks; ++kb, st = st + 1 == stages ? 0 : st + 1, ph ^= st == 0) {
           if (!mbar_wait_bounded(bar_empty + 8 * st, ph ^ 1)) {
             set_status(p.status, NVB200_STATUS_WAIT_TIMEOUT);
             *abort_flag = 1;
             break;
           }
           const uint32_t full = bar_full + 8 * st;
-          const int nsub = stage_subtiles(p, kb, BK);
+          const int nsub = stage_subtiles(p, kb);
           mbar_arrive_expect_tx(full, nsub * (kTileBytesA + sub_b));
           for (int u = 0; u < nsub; ++u) {
             const uint32_t sa = stage0 + st * stage_bytes + u * kTileBytesA;
@@ -383,36 +415,29 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
-    int it = 0, local = 0;
+    const OperandDescs od = operand_descs(p, stage0, sub_b, stage_bytes);
+    int st = 0, local = 0;
+    uint32_t ph = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
       const int buf = local & 1;
       const uint32_t acc_ph = (local >> 1) & 1;
       bool ok = mbar_wait_bounded(bar_acc_empty + 8 * buf, acc_ph ^ 1);
       tc_fence_after();
       const uint32_t d_tmem = tmem_base + buf * p.bn;
-      for (int kb = 0; kb < p.k_blocks && ok; ++kb, ++it) {
-        const int st = it % stages;
-        const uint32_t ph = (it / stages) & 1;
+      for (int kb = 0; kb < p.k_blocks && ok; ++kb, st = st + 1 == stages ? 0 : st + 1, ph ^= st == 0) {
         if (!mbar_wait_bounded(bar_full + 8 * st, ph)) {
           ok = false;
           break;
         }
         tc_fence_after();
         if (lane == 0) {
-          const int nsub = stage_subtiles(p, kb, BK);
+          const int nsub = stage_subtiles(p, kb);
+          const uint64_t a_st = od.a0 + st * od.stage, b_st = od.b0 + st * od.stage;
           for (int u = 0; u < nsub; ++u) {
-            const uint32_t sa = stage0 + st * stage_bytes + u * kTileBytesA;
-            const uint32_t sb = stage0 + st * stage_bytes + p.ksub * kTileBytesA + u * sub_b;
-            for (int k = 0; k < BK / UK; ++k) {
-              // K-major: the K step moves 32 B inside the swizzle row; SBO = 8 rows * 128 B.
-              // MN-major: the K step moves UK rows of 128 B; LBO = next 128-byte MN block (BK rows), SBO = one
-              // swizzle atom of k rows (8 rows, or 4 rows for the 32-byte-atom swizzle).
-              const uint64_t ad = p.a_mn_major ? smem_desc(sa + k * UK * 128, BK * 128, p.a_sbo, p.a_swz)
-                                               : smem_desc(sa + k * 32, 16, 1024, 2);
-              const uint64_t bd = p.b_mn_major ? smem_desc(sb + k * UK * 128, BK * 128, p.b_sbo, p.b_swz)
-                                               : smem_desc(sb + k * 32, 16, 1024, 2);
-              tc_mma<TF32>(d_tmem, ad, bd, p.idesc, (kb > 0 || u > 0 || k > 0) ? 1u : 0u);
-            }
+#pragma unroll
+            for (int k = 0; k < kMmaPerSub; ++k)
+              tc_mma<TF32>(d_tmem, a_st + u * od.a_sub + k * od.a_k, b_st + u * od.b_sub + k * od.b_k, p.idesc,
+                           (kb > 0 || u > 0 || k > 0) ? 1u : 0u);
           }
           tc_commit(bar_empty + 8 * st);
         }
@@ -519,22 +544,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     // ---------------------------------------------------------------- TMA producer (both CTAs)
     if (lane == 0) {
-      int it = 0;
+      int st = 0;
+      uint32_t ph = 0;
       for (int tile = cluster; tile < num_tiles && !*abort_flag; tile += clusters) {
         int pm, pn;
         tile_coords(tile, p.tiles_m, p.tiles_n, pm, pn);
         const int m0 = pm * 2 * BM + static_cast<int>(rank) * BM;
         const int n0 = pn * p.bn + static_cast<int>(rank) * half_bn;
-        for (int kb = 0; kb < p.k_blocks; ++kb, ++it) {
-          const int st = it % stages;
-          const uint32_t ph = (it / stages) & 1;
+        for (int kb = 0; kb < p.k_blocks; ++kb, st = st + 1 == stages ? 0 : st + 1, ph ^= st == 0) {
           if (!mbar_wait_bounded(bar_empty + 8 * st, ph ^ 1)) {
             set_status(p.status, NVB200_STATUS_WAIT_TIMEOUT);
             *abort_flag = 1;
             break;
           }
           const uint32_t full = map_to_cta(bar_full + 8 * st, 0);
-          const int nsub = stage_subtiles(p, kb, BK);
+          const int nsub = stage_subtiles(p, kb);
           if (leader) mbar_arrive_expect_tx(bar_full + 8 * st, 2 * nsub * (kTileBytesA + sub_b));
           for (int u = 0; u < nsub; ++u) {
             const uint32_t sa = stage0 + st * stage_bytes + u * kTileBytesA;
@@ -558,31 +582,28 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer (leader only)
     if (leader) {
-      int it = 0, local = 0;
+      const OperandDescs od = operand_descs(p, stage0, sub_b, stage_bytes);
+      int st = 0, local = 0;
+      uint32_t ph = 0;
       for (int tile = cluster; tile < num_tiles; tile += clusters, ++local) {
         const int buf = local & 1;
         bool ok = mbar_wait_bounded(bar_acc_empty + 8 * buf, ((local >> 1) & 1) ^ 1);
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + buf * p.bn;
-        for (int kb = 0; kb < p.k_blocks && ok; ++kb, ++it) {
-          const int st = it % stages;
-          if (!mbar_wait_bounded(bar_full + 8 * st, (it / stages) & 1)) {
+        for (int kb = 0; kb < p.k_blocks && ok; ++kb, st = st + 1 == stages ? 0 : st + 1, ph ^= st == 0) {
+          if (!mbar_wait_bounded(bar_full + 8 * st, ph)) {
             ok = false;
             break;
           }
           tc_fence_after();
           if (lane == 0) {
-            const int nsub = stage_subtiles(p, kb, BK);
+            const int nsub = stage_subtiles(p, kb);
+            const uint64_t a_st = od.a0 + st * od.stage, b_st = od.b0 + st * od.stage;
             for (int u = 0; u < nsub; ++u) {
-              const uint32_t sa = stage0 + st * stage_bytes + u * kTileBytesA;
-              const uint32_t sb = stage0 + st * stage_bytes + p.ksub * kTileBytesA + u * sub_b;
-              for (int k = 0; k < BK / UK; ++k) {
-                const uint64_t ad = p.a_mn_major ? smem_desc(sa + k * UK * 128, BK * 128, p.a_sbo, p.a_swz)
-                                                 : smem_desc(sa + k * 32, 16, 1024, 2);
-                const uint64_t bd = p.b_mn_major ? smem_desc(sb + k * UK * 128, BK * 128, p.b_sbo, p.b_swz)
-                                                 : smem_desc(sb + k * 32, 16, 1024, 2);
-                tc_mma2<TF32>(d_tmem, ad, bd, p.idesc, (kb > 0 || u > 0 || k > 0) ? 1u : 0u);
-              }
+#pragma unroll
+              for (int k = 0; k < kMmaPerSub; ++k)
+                tc_mma2<TF32>(d_tmem, a_st + u * od.a_sub + k * od.a_k, b_st + u * od.b_sub + k * od.b_k, p.idesc,
+                              (kb > 0 || u > 0 || k > 0) ? 1u : 0u);
             }
             tc_commit_pair(bar_empty + 8 * st);
           }
@@ -753,6 +774,7 @@ int matmul_tc_launch(void *c, const void *a, const void *b, int64_t M, int64_t N
   // 58 % of the back-to-back MMA rate, 8 at 92 %, 16 at 98 %.)
   p.ksub = NVB200_MM_KSUB;
   p.k_blocks = static_cast<int>((K + BK * p.ksub - 1) / (BK * p.ksub));
+  p.k_subs = static_cast<int>((K + BK - 1) / BK);
   p.a_mn_major = a_mn;
   p.b_mn_major = b_mn;
   p.a_swz = p.b_swz = f32 ? 1u : 2u;
