@@ -78,6 +78,30 @@ def test_silu_and_mul(cuda, rows):
     assert ulps(out, om.silu_and_mul(cpu(x))) <= 1
 
 
+def _same_bits(a, b):
+    """Bit-for-bit equality of two bf16 tensors, any NaN matching any NaN."""
+    return bool(((a.view(torch.int16) == b.view(torch.int16)) | (torch.isnan(a) & torch.isnan(b))).all())
+
+
+def test_silu_every_bf16_gate(cuda):
+    # silu(g) rounded to bf16 depends only on the 16-bit gate value, so running all 65,536 bit patterns (zeros,
+    # subnormals, infinities and NaNs included) as gates covers every input the kernel can see. Up = 1 isolates the
+    # rounded silu; the second pass multiplies by up values that include subnormals, signed zeros and non-finite
+    # values.
+    gate = torch.arange(-32768, 32768, dtype=torch.int32, device=cuda).to(torch.int16).view(torch.bfloat16)
+    gate = gate.view(64, 1024)
+    ones = torch.ones_like(gate)
+    out = silu_and_mul(torch.cat([gate, ones], dim=1))
+    assert _same_bits(out, om.silu_and_mul(torch.cat([gate, ones], dim=1)))
+    g = torch.Generator(device=cuda).manual_seed(11)
+    up = torch.randn(64, 1024, device=cuda, generator=g).to(torch.bfloat16)
+    special = torch.tensor([0.0, -0.0, 1e-40, -1e-40, 9.2e-41, float("inf"), float("-inf"), float("nan"), 3e38,
+                            -3e38, 1.2e-38, 65504.0], device=cuda).to(torch.bfloat16)
+    up.view(-1)[: special.numel() * 512] = special.repeat(512)
+    x = torch.cat([gate, up], dim=1)
+    assert _same_bits(silu_and_mul(x), om.silu_and_mul(x))
+
+
 # ---------------------------------------------------------------------------------------------------------------
 # Config 2 (hidden 1024, gate_up [T, 6144] read as strided column views) at T in {1, 32, 2048, 8192}.
 
