@@ -94,22 +94,25 @@ NVB200_API int nvb200_qk_norm_rope_kv(const nvb200_qk_norm_rope_kv_args *args, n
  * Replaces: nanovllm/kernels/rms_norm.py:83-98 (rms_norm) and _rms_norm_kernel :34-54.
  * Row g * rows_per_group + r of x starts at x + g * group_stride + r * row_stride (a 2-D [rows, n] view is
  * groups = rows, rows_per_group = 1; a 3-D [T, H, n] view is groups = T, rows_per_group = H). Unit last stride.
- * y = (x.float() * rsqrt(mean(x.float()^2) + eps)).to(dtype) * w, the product in dtype. */
+ * y = (x.float() * rsqrt(mean(x.float()^2) + eps)).to(dtype) * w, the product in dtype.
+ * status (nullable, device int32): NVB200_STATUS_WAIT_TIMEOUT is OR-ed in if a pipeline wait gave up (long bf16
+ * rows in large batches run a bulk-copy pipeline whose waits are bounded). The two functions below take the same
+ * argument for the same purpose; their current kernels have no waits and never set it. */
 NVB200_API int nvb200_rms_norm(void *y, const void *x, const void *w, int64_t groups, int64_t rows_per_group,
                     int64_t group_stride, int64_t row_stride, int64_t n, float eps, int dtype,
-                    nvb200_stream_t stream);
+                    int32_t *status, nvb200_stream_t stream);
 
 /* s = x + residual in fp32; residual_out = s.to(dtype); y = RMSNorm of the unrounded s. y, residual_out
  * contiguous [rows, n]; x and residual have unit last stride and any row stride.
  * Replaces: nanovllm/kernels/rms_norm.py:101-111 (fused_add_rms_norm) and _fused_add_rms_norm_kernel :57-80. */
 NVB200_API int nvb200_fused_add_rms_norm(void *y, void *residual_out, const void *x, const void *residual, const void *w,
                               int64_t rows, int64_t n, int64_t x_row_stride, int64_t residual_row_stride,
-                              float eps, int dtype, nvb200_stream_t stream);
+                              float eps, int dtype, int32_t *status, nvb200_stream_t stream);
 
 /* out[r, :] = silu(x[r, :n].float()).to(dtype) * x[r, n:2n]; out contiguous [rows, n]; x unit last stride.
  * Replaces: nanovllm/kernels/swiglu.py:34-43 (silu_and_mul) and _silu_and_mul_kernel :19-31. */
 NVB200_API int nvb200_silu_and_mul(void *out, const void *x, int64_t rows, int64_t n, int64_t x_row_stride, int dtype,
-                        nvb200_stream_t stream);
+                        int32_t *status, nvb200_stream_t stream);
 
 /* C[M, N] = A[M, K] @ B[K, N] with fp32 accumulation, C in the inputs' dtype (bf16 or fp32).
  * Replaces: nanovllm/kernels/matmul.py:84-99 (matmul) and _matmul_kernel :33-81.

@@ -361,6 +361,179 @@ template <typename T> int launch_silu(void *out, const void *x, int64_t rows, in
   return launch_status();
 }
 
+// ---------------------------------------------------------------------------------------------------------------
+// Bulk-copy RMSNorm for long bf16 rows in large batches (the producer / consumer pipeline of the fused q/k kernel).
+// A unit is R consecutive rows. Warp 0 (one lane) copies each unit's rows HBM -> shared memory with cp.async.bulk
+// into a ring of stages (completion counted in mbarrier transaction bytes); consumer warp w owns stages w, w + W, ...
+// (so it observes every phase of their barriers), normalises the rows in place and writes them with cp.async.bulk
+// stores, then frees the stage once the stores have read it. The copies keep tens of KB per SM in flight without
+// registers, which the register kernels cannot for 8 KB rows (one 128-thread CTA per row, 64 B in flight per
+// thread). Measured on B200 at 8192 rows: 4096-element rows 28.7 us against 32.8 us for the register kernel;
+// 1024-element rows no faster, and Add+RMSNorm and SiLU x Mul slower (their register kernels keep more loads in
+// flight per thread, and SiLU's arithmetic wants more warps than a producer / consumer CTA has), so only RMSNorm
+// with rows of at least kStreamMinRowBytes takes this path.
+
+constexpr int kStreamWarps = 8;      // consumer warps per CTA
+constexpr int kStreamCtas = 2;       // CTAs per SM
+constexpr int kStreamMaxStages = 8;  // multiple of kStreamWarps
+constexpr int kStreamHeader = 256;   // full[kStreamMaxStages], empty[kStreamMaxStages]
+constexpr int kStreamUnitTarget = 12 * 1024;
+constexpr int kStreamBudget = (228 * 1024) / kStreamCtas - 1024 - kStreamHeader;
+constexpr int kStreamMinRowBytes = 8 * 1024;
+#ifndef NVB200_STREAM_MIN_ROWS
+#define NVB200_STREAM_MIN_ROWS 2048
+#endif
+constexpr int64_t kStreamMinRows = NVB200_STREAM_MIN_ROWS;  // below this the register kernels are as fast
+
+struct StreamArgs {
+  const __nv_bfloat16 *x, *w;
+  __nv_bfloat16 *y;
+  int64_t rows;
+  int64_t x_stride;  // elements between consecutive rows of x
+  int n;             // elements per row
+  int rows_per_unit;
+  int64_t units, chunk;  // units in total, units per CTA
+  int stages, consumers, stage_bytes;
+  float eps;
+  int32_t *status;
+};
+
+NVB200_DEVICE int stream_next_unit(int it, int NS, int W) {
+  const int st = it % NS;
+  return st + W < NS ? it + W : it - st + NS + st % W;
+}
+
+__global__ void __launch_bounds__(32 * (1 + kStreamWarps), kStreamCtas)
+    rms_stream_kernel(const __grid_constant__ StreamArgs a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int NS = a.stages;
+  const uint32_t bar_base = smem_addr(smem);  // full[0..NS), empty[0..NS)
+  const uint32_t stage_base = smem_addr(smem + kStreamHeader);
+  const int64_t first = static_cast<int64_t>(blockIdx.x) * a.chunk;
+  if (first >= a.units) return;
+  const int n_units = static_cast<int>(a.chunk < a.units - first ? a.chunk : a.units - first);
+  const int R = a.rows_per_unit;
+  const uint32_t rb = 2u * static_cast<uint32_t>(a.n);  // bytes of one row
+  const int64_t x_pitch = a.x_stride * 2;               // bytes between rows of x
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(bar_base + 8 * i, 1);
+      mbar_init(bar_base + 8 * (NS + i), 1);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ producer (lane 0)
+    if (lane != 0) return;
+    const uint8_t *xb = reinterpret_cast<const uint8_t *>(a.x);
+    const bool dense = x_pitch == static_cast<int64_t>(rb);
+    for (int it = 0; it < n_units; ++it) {
+      const int st = it % NS;
+      const uint32_t full = bar_base + 8 * st, empty = bar_base + 8 * (NS + st);
+      if (!mbar_wait_bounded(empty, ((it / NS) & 1) ^ 1)) {
+        set_status(a.status, NVB200_STATUS_WAIT_TIMEOUT);
+        return;
+      }
+      const int64_t r0 = (first + it) * R;
+      const int nr = static_cast<int>(R < a.rows - r0 ? R : a.rows - r0);
+      const uint32_t sb = stage_base + st * a.stage_bytes;
+      mbar_arrive_expect_tx(full, nr * rb);
+      if (dense) {
+        bulk_g2s(sb, xb + r0 * x_pitch, nr * rb, full);
+      } else {
+        for (int i = 0; i < nr; ++i) bulk_g2s(sb + i * rb, xb + (r0 + i) * x_pitch, rb, full);
+      }
+    }
+    return;
+  }
+
+  // -------------------------------------------------------------------- consumers
+  const int cw = warp - 1;
+  const int nw = a.consumers;
+  if (cw >= nw) return;
+  const int nv = a.n / 8;
+  for (int it = cw; it < n_units; it = stream_next_unit(it, NS, nw)) {
+    const int st = it % NS;
+    const uint32_t full = bar_base + 8 * st, empty = bar_base + 8 * (NS + st);
+    if (!mbar_wait_bounded(full, (it / NS) & 1)) {
+      if (lane == 0) set_status(a.status, NVB200_STATUS_WAIT_TIMEOUT);
+      break;
+    }
+    const int64_t r0 = (first + it) * R;
+    const int nr = static_cast<int>(R < a.rows - r0 ? R : a.rows - r0);
+    const uint32_t sb = stage_base + st * a.stage_bytes;
+    for (int i = 0; i < nr; ++i) {
+      const uint32_t xr = sb + i * rb;
+      float ss = 0.f;
+      for (int v = lane; v < nv; v += 32) {
+        float f[8];
+        unpack8(ld_shared_v4(xr + 16 * v), f);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) ss = fmaf(f[e], f[e], ss);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      const float rstd = rsqrtf(ss / static_cast<float>(a.n) + a.eps);
+      // y = T(T(x * rstd) * w): the bf16 x bf16 product is exact in fp32, so mul.rn.bf16x2 rounds it once.
+      for (int v = lane; v < nv; v += 32) {
+        float f[8];
+        unpack8(ld_shared_v4(xr + 16 * v), f);
+        const uint4 wv = __ldg(reinterpret_cast<const uint4 *>(a.w) + v);
+        const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+        uint32_t o[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          o[k] = bf16x2_mul(pack_bf16x2(__fmul_rn(f[2 * k], rstd), __fmul_rn(f[2 * k + 1], rstd)), ww[k]);
+        st_shared_v4(xr + 16 * v, make_uint4(o[0], o[1], o[2], o[3]));
+      }
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      bulk_s2g(a.y + r0 * a.n, sb, nr * rb);
+      bulk_commit();
+      bulk_wait_read<0>();  // the stores have read the stage: hand it back to the producer
+      mbar_arrive(empty);
+    }
+    __syncwarp();
+  }
+  // Stores still in flight may finish after the CTA exits; their shared-memory reads are done (waited above).
+}
+
+// Launches the bulk-copy RMSNorm when it applies (bf16, long rows of whole 16-byte vectors, 16-byte aligned rows,
+// a large batch); returns NVB200_ERR_UNSUPPORTED otherwise so the caller runs the register kernels.
+int launch_rms_stream(StreamArgs &a, cudaStream_t stream) {
+  const int rb = 2 * a.n;
+  if (a.rows < kStreamMinRows || a.n % 8 != 0 || rb < kStreamMinRowBytes || rb > kStreamBudget / 2)
+    return NVB200_ERR_UNSUPPORTED;
+  a.rows_per_unit = std::max(1, kStreamUnitTarget / rb);
+  a.stage_bytes = a.rows_per_unit * rb;
+  a.stages = std::min(kStreamMaxStages, kStreamBudget / a.stage_bytes);
+  a.consumers = std::min(kStreamWarps, a.stages);
+  a.stages -= a.stages % a.consumers;
+  a.units = (a.rows + a.rows_per_unit - 1) / a.rows_per_unit;
+  if (a.units > 0x7fffffffLL) return NVB200_ERR_UNSUPPORTED;
+  const int smem = kStreamHeader + a.stages * a.stage_bytes;
+  static int configured[64] = {0};  // per device: max dynamic shared memory raised once
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !configured[dev]) {
+    if (cudaFuncSetAttribute(rms_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kStreamHeader + kStreamBudget) != cudaSuccess)
+      return NVB200_ERR_CUDA;
+    configured[dev] = 1;
+  }
+  const int64_t grid = std::min<int64_t>(a.units, static_cast<int64_t>(sm_count()) * kStreamCtas);
+  a.chunk = (a.units + grid - 1) / grid;
+  const int64_t blocks = (a.units + a.chunk - 1) / a.chunk;
+  rms_stream_kernel<<<static_cast<unsigned>(blocks), 32 * (1 + kStreamWarps), smem, stream>>>(a);
+  return launch_status();
+}
+
 }  // namespace
 }  // namespace nvb200
 
@@ -368,7 +541,7 @@ using namespace nvb200;
 
 extern "C" int nvb200_rms_norm(void *y, const void *x, const void *w, int64_t groups, int64_t rows_per_group,
                                int64_t group_stride, int64_t row_stride, int64_t n, float eps, int dtype,
-                               nvb200_stream_t stream) {
+                               int32_t *status, nvb200_stream_t stream) {
   if (groups < 0 || rows_per_group <= 0 || n <= 0 || n > 0x7fffffffLL) return NVB200_ERR_ARG;
   if (dtype != NVB200_BF16 && dtype != NVB200_F16 && dtype != NVB200_F32) return NVB200_ERR_ARG;
   const int64_t rows = groups * rows_per_group;
@@ -382,12 +555,22 @@ extern "C" int nvb200_rms_norm(void *y, const void *x, const void *w, int64_t gr
   a.x_group_stride = group_stride, a.x_row_stride = row_stride, a.n = static_cast<int>(n), a.eps = eps;
   const bool vec_ok = aligned16(y) && aligned16(x) && aligned16(w) && (group_stride * es) % 16 == 0 &&
                       (row_stride * es) % 16 == 0;
-  return dispatch_norm<false>(a, vec_ok, dtype, reinterpret_cast<cudaStream_t>(stream));
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (dtype == NVB200_BF16 && vec_ok && rows_per_group == 1) {
+    StreamArgs sa{};
+    sa.x = static_cast<const __nv_bfloat16 *>(x), sa.w = static_cast<const __nv_bfloat16 *>(w);
+    sa.y = static_cast<__nv_bfloat16 *>(y), sa.rows = rows, sa.x_stride = group_stride, sa.n = static_cast<int>(n);
+    sa.eps = eps, sa.status = status;
+    const int rc = launch_rms_stream(sa, s);
+    if (rc != NVB200_ERR_UNSUPPORTED) return rc;
+  }
+  return dispatch_norm<false>(a, vec_ok, dtype, s);
 }
 
 extern "C" int nvb200_fused_add_rms_norm(void *y, void *residual_out, const void *x, const void *residual,
                                          const void *w, int64_t rows, int64_t n, int64_t x_row_stride,
-                                         int64_t residual_row_stride, float eps, int dtype, nvb200_stream_t stream) {
+                                         int64_t residual_row_stride, float eps, int dtype, int32_t *status,
+                                         nvb200_stream_t stream) {
   if (rows < 0 || n <= 0 || n > 0x7fffffffLL) return NVB200_ERR_ARG;
   if (dtype != NVB200_BF16 && dtype != NVB200_F16 && dtype != NVB200_F32) return NVB200_ERR_ARG;
   if (rows == 0) return NVB200_OK;
@@ -400,11 +583,12 @@ extern "C" int nvb200_fused_add_rms_norm(void *y, void *residual_out, const void
   a.n = static_cast<int>(n), a.eps = eps;
   const bool vec_ok = aligned16(y) && aligned16(residual_out) && aligned16(x) && aligned16(residual) &&
                       aligned16(w) && (x_row_stride * es) % 16 == 0 && (residual_row_stride * es) % 16 == 0;
-  return dispatch_norm<true>(a, vec_ok, dtype, reinterpret_cast<cudaStream_t>(stream));
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  return dispatch_norm<true>(a, vec_ok, dtype, s);
 }
 
 extern "C" int nvb200_silu_and_mul(void *out, const void *x, int64_t rows, int64_t n, int64_t x_row_stride,
-                                   int dtype, nvb200_stream_t stream) {
+                                   int dtype, int32_t *status, nvb200_stream_t stream) {
   if (rows < 0 || n <= 0 || n > 0x3fffffffLL) return NVB200_ERR_ARG;
   if (rows == 0) return NVB200_OK;
   if (!out || !x) return NVB200_ERR_ARG;

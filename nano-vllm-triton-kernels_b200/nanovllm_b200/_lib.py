@@ -52,11 +52,12 @@ def _declare(lib):
     lib.nvb200_status_string.restype = ctypes.c_char_p
     lib.nvb200_qk_norm_rope_kv.argtypes = [ctypes.POINTER(QkNormRopeKvArgs), _vp]
     lib.nvb200_qk_norm_rope_kv.restype = ctypes.c_int
-    lib.nvb200_rms_norm.argtypes = [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _f32, ctypes.c_int, _vp]
+    lib.nvb200_rms_norm.argtypes = [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _f32, ctypes.c_int, _vp, _vp]
     lib.nvb200_rms_norm.restype = ctypes.c_int
-    lib.nvb200_fused_add_rms_norm.argtypes = [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _f32, ctypes.c_int, _vp]
+    lib.nvb200_fused_add_rms_norm.argtypes = [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _f32, ctypes.c_int, _vp,
+                                              _vp]
     lib.nvb200_fused_add_rms_norm.restype = ctypes.c_int
-    lib.nvb200_silu_and_mul.argtypes = [_vp, _vp, _i64, _i64, _i64, ctypes.c_int, _vp]
+    lib.nvb200_silu_and_mul.argtypes = [_vp, _vp, _i64, _i64, _i64, ctypes.c_int, _vp, _vp]
     lib.nvb200_silu_and_mul.restype = ctypes.c_int
     lib.nvb200_matmul_workspace_size.argtypes = [_i64] * 7 + [ctypes.c_int]
     lib.nvb200_matmul_workspace_size.restype = _i64

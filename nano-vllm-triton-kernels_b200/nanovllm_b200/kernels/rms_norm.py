@@ -35,7 +35,8 @@ def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
     y = torch.empty(x.shape, dtype=x.dtype, device=x.device)
     if groups * rows_per_group:
         _lib.check(_lib.lib().nvb200_rms_norm(y.data_ptr(), x.data_ptr(), w.data_ptr(), groups, rows_per_group,
-                                              group_stride, row_stride, n, eps, code, _lib.stream_of(x)),
+                                              group_stride, row_stride, n, eps, code,
+                                              _lib.status_word(x.device).data_ptr(), _lib.stream_of(x)),
                    "rms_norm")
     return y
 
@@ -56,6 +57,7 @@ def fused_add_rms_norm(x: torch.Tensor, residual: torch.Tensor, w: torch.Tensor,
     if rows:
         _lib.check(_lib.lib().nvb200_fused_add_rms_norm(y.data_ptr(), s.data_ptr(), x.data_ptr(), residual.data_ptr(),
                                                         w.data_ptr(), rows, n, x.stride(0), residual.stride(0), eps,
-                                                        code, _lib.stream_of(x)),
+                                                        code, _lib.status_word(x.device).data_ptr(),
+                                                        _lib.stream_of(x)),
                    "fused_add_rms_norm")
     return y, s

@@ -20,6 +20,7 @@ def silu_and_mul(x: torch.Tensor) -> torch.Tensor:
     out = torch.empty(rows, n, dtype=x.dtype, device=x.device)
     if rows and n:
         _lib.check(_lib.lib().nvb200_silu_and_mul(out.data_ptr(), x.data_ptr(), rows, n, x.stride(0),
-                                                  _lib.DTYPE_CODE[x.dtype], _lib.stream_of(x)),
+                                                  _lib.DTYPE_CODE[x.dtype], _lib.status_word(x.device).data_ptr(),
+                                                  _lib.stream_of(x)),
                    "silu_and_mul")
     return out

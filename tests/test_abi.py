@@ -40,9 +40,9 @@ def test_no_gpu_means_error_not_crash():
     import torch
     if torch.cuda.is_available():
         pytest.skip("a GPU is present")
-    rc = _lib.lib().nvb200_rms_norm(None, None, None, 1, 1, 8, 0, 8, 1e-6, _lib.BF16, None)
+    rc = _lib.lib().nvb200_rms_norm(None, None, None, 1, 1, 8, 0, 8, 1e-6, _lib.BF16, None, None)
     assert rc == _lib.ERR_ARG  # null pointers are rejected before any CUDA call
-    rc = _lib.lib().nvb200_rms_norm(8, 8, 8, 1, 1, 8, 0, 8, 1e-6, _lib.BF16, None)
+    rc = _lib.lib().nvb200_rms_norm(8, 8, 8, 1, 1, 8, 0, 8, 1e-6, _lib.BF16, None, None)
     assert rc == _lib.ERR_NO_DEVICE
 
 

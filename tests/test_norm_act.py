@@ -103,6 +103,44 @@ def test_silu_every_bf16_gate(cuda):
 
 
 # ---------------------------------------------------------------------------------------------------------------
+# Large bf16 batches: long rows run the bulk-copy RMSNorm (units of one or more rows, a ragged last unit, dense or
+# strided rows), the rest the register kernels; the same properties as above must hold for both.
+
+@pytest.mark.parametrize("rows", [2048, 4099, 9001])
+@pytest.mark.parametrize("n", [128, 1024, 4096, 6144])
+@pytest.mark.parametrize("strided", [False, True])
+def test_row_engine_norms(cuda, rows, n, strided):
+    pad = 64 if strided else 0
+    xw = make(cuda, (rows, n + pad), rows + n)
+    rw = make(cuda, (rows, n + 2 * pad), rows + n + 1)
+    x, r = xw[:, pad:pad + n], rw[:, :n]
+    w = weight(cuda, n, rows)
+    assert ulps(rms_norm(x, w, EPS), om.rms_forward(x, w, EPS)) <= MAX_ULP
+    y, s = fused_add_rms_norm(x, r, w, EPS)
+    ry, rs = om.add_rms_forward(x, r, w, EPS)
+    assert ulps(y, ry) <= MAX_ULP and torch.equal(s, rs)
+    assert om.bf16_ulp_diff(cpu(y), cpu(ry)).float().mean() < 0.05  # almost all elements bitwise
+    assert _lib_status(cuda) == 0
+
+
+@pytest.mark.parametrize("rows", [2048, 4099, 9001])
+@pytest.mark.parametrize("n", [64, 1536, 3072, 8192])
+@pytest.mark.parametrize("strided", [False, True])
+def test_row_engine_silu(cuda, rows, n, strided):
+    buf = make(cuda, (rows, 2 * n + (128 if strided else 0)), rows * 3 + n)
+    x = buf[:, 64:64 + 2 * n] if strided else buf
+    out = silu_and_mul(x)
+    assert out.shape == (rows, n) and out.is_contiguous()
+    assert torch.equal(out, om.silu_and_mul(x))
+    assert _lib_status(cuda) == 0
+
+
+def _lib_status(dev):
+    from nanovllm_b200 import _lib
+    return _lib.status(dev, clear=True)
+
+
+# ---------------------------------------------------------------------------------------------------------------
 # Config 2 (hidden 1024, gate_up [T, 6144] read as strided column views) at T in {1, 32, 2048, 8192}.
 
 @pytest.mark.parametrize("T", [1, 32, 2048, 8192])
