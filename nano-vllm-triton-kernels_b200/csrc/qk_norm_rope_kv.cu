@@ -90,6 +90,7 @@ struct QknrParams {
                     // token, so one bulk copy moves the unit's q | k | v (v is then read for skipped slots too,
                     // as the reference's byte count assumes)
   int stage_bytes;  // bytes per stage (multiple of 128)
+  int tpu;          // tokens per unit of the multi-token kernel (1 for the others)
   float eps;
   int32_t *status;
 };
@@ -338,6 +339,212 @@ __global__ void __launch_bounds__(32 * (1 + W), CTAS) qknr_bulk_kernel(const __g
 }
 
 // ---------------------------------------------------------------------------------------------------------------
+// Multi-token bulk kernel: the same pipeline with a unit of B consecutive tokens, for shards whose tokens are small
+// (a tensor-parallel rank's 1-4 kv heads: 2-6.5 KB per token), where one token per unit would spend as much time
+// on per-unit barrier and issue work as on moving bytes. It needs q | k | v consecutive in one qkv_proj row per
+// token and consecutive rows (the layout of a rank's qkv_proj output), so the producer moves a unit's B rows with
+// one bulk copy (q | k per token when the cache is not written). Stage layout: B rows of qb + 2 kb bytes (the v
+// slot unused without a cache), then B cos/sin rows. Positions and slots are loaded 32 tokens at a time, one
+// batch ahead; lane i of the producer issues the cos/sin copy of the unit's token i.
+
+constexpr int kMultiMaxTpu = 16;                    // tokens per unit (a power of two)
+#ifndef NVB200_QKNR_MULTI_UNIT_BYTES
+#define NVB200_QKNR_MULTI_UNIT_BYTES (18 * 1024)
+#endif
+constexpr int64_t kMultiUnitBytes = NVB200_QKNR_MULTI_UNIT_BYTES;  // largest multi-token unit
+constexpr int kMultiHeader = 256 + 4 * kMaxStagesAny * kMultiMaxTpu;  // barriers + per-stage slot numbers
+constexpr int multi_stage_budget(int ctas) { return (228 * 1024) / ctas - 1024 - kMultiHeader; }
+
+template <int D, int W, int CTAS>
+__global__ void __launch_bounds__(32 * (1 + W), CTAS) qknr_multi_kernel(const __grid_constant__ QknrParams p) {
+  constexpr int HALF = D / 2;
+  constexpr int LPH = D / 16;    // lanes per head: each lane holds 8 + 8 elements
+  constexpr int HPI = 32 / LPH;  // heads per warp step
+  extern __shared__ __align__(128) uint8_t smem[];
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int NS = p.stages;
+  const int B = p.tpu;
+  const uint32_t bar_base = smem_addr(smem);  // full[0..NS), empty[0..NS)
+  int32_t *meta = reinterpret_cast<int32_t *>(smem + 256);  // slot of token i of stage st at st * kMultiMaxTpu + i
+  const uint32_t stage_base = smem_addr(smem + kMultiHeader);
+
+  const int64_t first = static_cast<int64_t>(blockIdx.x) * p.chunk;  // first unit of this CTA
+  if (first >= p.units) return;
+  const int n_units = static_cast<int>(p.chunk < p.units - first ? p.chunk : p.units - first);
+  const int64_t t_first = first * B;
+  const int64_t t_end = (first + n_units) * B < p.num_tokens ? (first + n_units) * B : p.num_tokens;
+
+  const int nq = p.hq;  // a unit holds every head of its tokens
+  const uint32_t qb = nq * D * 2, kb = p.hkv * D * 2, csb = D * 4;
+  const uint32_t row_stage = qb + 2 * kb;
+  const bool store = p.k_cache != nullptr;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(bar_base + 8 * i, 1);
+      mbar_init(bar_base + 8 * (NS + i), 1);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ producer
+    const int upb = 32 / B;  // units per batch of 32 tokens
+    bool abort = false;
+    int64_t pos_next = 0;
+    int32_t slot_next = -1;
+    if (t_first + lane < t_end) {
+      pos_next = __ldg(p.positions + t_first + lane);
+      if (store) slot_next = __ldg(p.slots + t_first + lane);
+    }
+    for (int base = 0; base < n_units && !abort; base += upb) {
+      const int64_t pos = pos_next;
+      const int32_t slot = slot_next;
+      const int64_t tn = t_first + static_cast<int64_t>(base + upb) * B + lane;
+      if (tn < t_end) {
+        pos_next = __ldg(p.positions + tn);
+        if (store) slot_next = __ldg(p.slots + tn);
+      }
+      const int cnt = min(upb, n_units - base);
+      for (int jj = 0; jj < cnt; ++jj) {
+        const int it = base + jj;
+        const int st = it % NS;
+        const uint32_t full = bar_base + 8 * st, empty = bar_base + 8 * (NS + st);
+        const uint32_t sb = stage_base + st * p.stage_bytes;
+        const int64_t t0 = t_first + static_cast<int64_t>(it) * B;
+        const int nt = static_cast<int>(B < t_end - t0 ? B : t_end - t0);
+        if (lane == 0) {
+          if (!mbar_wait_bounded(empty, ((it / NS) & 1) ^ 1)) {
+            set_status(p.status, NVB200_STATUS_WAIT_TIMEOUT);
+            abort = true;
+          } else if (store) {
+            bulk_g2s(sb, p.q + t0 * p.q_stride, nt * row_stage, full);
+          } else {
+            for (int i = 0; i < nt; ++i) bulk_g2s(sb + i * row_stage, p.q + (t0 + i) * p.q_stride, qb + kb, full);
+          }
+        }
+        abort = __shfl_sync(0xffffffffu, abort, 0);
+        if (abort) break;
+        const int src = jj * B + (lane < B ? lane : 0);
+        int64_t pj = __shfl_sync(0xffffffffu, pos, src);
+        int32_t sj = __shfl_sync(0xffffffffu, slot, src);
+        if (lane < nt) {
+          if (pj < 0 || pj >= p.num_positions) {
+            set_status(p.status, NVB200_STATUS_BAD_POSITION);
+            pj = 0;
+          }
+          if (sj < -1 || sj >= p.num_slots) {
+            set_status(p.status, NVB200_STATUS_BAD_SLOT);
+            sj = -1;
+          }
+          meta[st * kMultiMaxTpu + lane] = sj;
+        }
+        __syncwarp();  // the slot numbers are written before lane 0's arrive releases the stage
+        if (lane == 0) mbar_arrive_expect_tx(full, nt * ((store ? row_stage : qb + kb) + csb));
+        if (lane < nt) bulk_g2s(sb + B * row_stage + lane * csb, p.cos_sin + pj * p.cs_stride, csb, full);
+      }
+    }
+    return;
+  }
+
+  // -------------------------------------------------------------------- consumers
+  const int cw = warp - 1;
+  const int j = lane % LPH;   // 8-element column block inside each half
+  const int hl = lane / LPH;  // head within the warp step
+  uint32_t wq1[4], wq2[4], wk1[4], wk2[4];
+  load_w8(p.q_w + 8 * j, wq1);
+  load_w8(p.q_w + HALF + 8 * j, wq2);
+  load_w8(p.k_w + 8 * j, wk1);
+  load_w8(p.k_w + HALF + 8 * j, wk2);
+  const int total = nq + p.hkv;
+
+  // Warp cw owns stages cw, cw + W, ... (every waiter of a stage's full barrier sees each of its phases).
+  const int nw = p.consumers;
+  if (cw >= nw) return;
+  for (int it = cw; it < n_units; it = next_unit(it, NS, nw)) {
+    const int st = it % NS;
+    const uint32_t full = bar_base + 8 * st, empty = bar_base + 8 * (NS + st);
+    if (!mbar_wait_bounded(full, (it / NS) & 1)) {
+      if (lane == 0) set_status(p.status, NVB200_STATUS_WAIT_TIMEOUT);
+      break;
+    }
+    const uint32_t sb = stage_base + st * p.stage_bytes;
+    const int64_t t0 = t_first + static_cast<int64_t>(it) * B;
+    const int nt = static_cast<int>(B < t_end - t0 ? B : t_end - t0);
+    // The unit's (token, head) pairs in order, HPI per warp step: a token's heads need not fill a step (a rank with
+    // one kv head has 5 per token), so steps run across token boundaries. (ti, hi): this lane group's pair.
+    const int nflat = nt * total;
+    int ti = 0, hi = hl;
+    while (hi >= total) hi -= total, ++ti;
+    for (int f0 = 0; f0 < nflat; f0 += HPI) {
+      const bool active = f0 + hl < nflat;
+      const int i = active ? ti : 0;
+      const bool isq = hi < nq;
+      const uint32_t sq = sb + i * row_stage;
+      const uint32_t row = active ? (isq ? sq + hi * D * 2 : sq + qb + (hi - nq) * D * 2) : sq;
+      const uint32_t scs = sb + B * row_stage + i * csb;
+      float c[8], s[8];
+      {
+        const float4 c0 = ld_shared_f4(scs + 32 * j), c1 = ld_shared_f4(scs + 32 * j + 16);
+        const float4 s0 = ld_shared_f4(scs + 4 * HALF + 32 * j), s1 = ld_shared_f4(scs + 4 * HALF + 32 * j + 16);
+        c[0] = c0.x, c[1] = c0.y, c[2] = c0.z, c[3] = c0.w, c[4] = c1.x, c[5] = c1.y, c[6] = c1.z, c[7] = c1.w;
+        s[0] = s0.x, s[1] = s0.y, s[2] = s0.z, s[3] = s0.w, s[4] = s1.x, s[5] = s1.y, s[6] = s1.z, s[7] = s1.w;
+      }
+      const uint4 a = ld_shared_v4(row + 16 * j);
+      const uint4 b = ld_shared_v4(row + 2 * HALF + 16 * j);
+      float x1[8], x2[8];
+      unpack8(a, x1);
+      unpack8(b, x2);
+      float ss = 0.f;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ss = fmaf(x1[e], x1[e], ss);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ss = fmaf(x2[e], x2[e], ss);
+#pragma unroll
+      for (int o = LPH / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      const float rstd = rsqrtf(ss / static_cast<float>(D) + p.eps);
+      uint32_t w1[4], w2[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        w1[e] = isq ? wq1[e] : wk1[e];
+        w2[e] = isq ? wq2[e] : wk2[e];
+      }
+      float y1[8], y2[8];
+      norm_rope8(x1, x2, rstd, w1, w2, c, s, y1, y2);
+      if (active) {
+        st_shared_v4(row + 16 * j, pack8(y1));
+        st_shared_v4(row + 2 * HALF + 16 * j, pack8(y2));
+      }
+      hi += HPI;
+      while (hi >= total) hi -= total, ++ti;
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      for (int i = 0; i < nt; ++i) {
+        const int64_t t = t0 + i;
+        const uint32_t sq = sb + i * row_stage;
+        bulk_s2g(p.q_out + t * p.hq * D, sq, qb);
+        if (p.k_out) bulk_s2g(p.k_out + t * p.hkv * D, sq + qb, kb);
+        const int32_t slot = meta[st * kMultiMaxTpu + i];
+        if (slot >= 0) {
+          const int64_t off = static_cast<int64_t>(slot) * p.hkv * D;
+          bulk_s2g(p.k_cache + off, sq + qb, kb);
+          bulk_s2g(p.v_cache + off, sq + qb + kb, kb);
+        }
+      }
+      bulk_commit();
+      bulk_wait_read<0>();  // the stores have read the stage: hand it back to the producer
+      mbar_arrive(empty);
+    }
+    __syncwarp();
+  }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
 // Direct kernel for small batches (decode): no staging, so the latency is one position load and the cos/sin row
 // behind it, in parallel with the q/k/v loads. One warp handles 32/LPH heads of one token with the bulk consumer's
 // lane layout (8 + 8 elements per lane, 16-byte loads and stores); the warps of a CTA cover a token's q heads,
@@ -550,6 +757,36 @@ int launch_bulk(QknrParams &p, int sms, cudaStream_t stream) {
   return launch_status();
 }
 
+template <int D, int W, int CTAS, int MAX_STAGES>
+int launch_multi(QknrParams &p, int sms, cudaStream_t stream) {
+  constexpr int budget = multi_stage_budget(CTAS);
+  p.stages = std::min(MAX_STAGES, budget / p.stage_bytes);
+  if (p.stages < 2) return NVB200_ERR_UNSUPPORTED;
+  p.consumers = std::min(W, p.stages);
+  p.stages -= p.stages % p.consumers;
+  const int smem = kMultiHeader + p.stages * p.stage_bytes;
+  static int configured[64] = {0};  // per device: max dynamic shared memory raised once
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !configured[dev]) {
+    if (cudaFuncSetAttribute(qknr_multi_kernel<D, W, CTAS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kMultiHeader + budget) != cudaSuccess)
+      return NVB200_ERR_CUDA;
+    configured[dev] = 1;
+  }
+  const int64_t grid = std::min<int64_t>(p.units, static_cast<int64_t>(sms) * CTAS);
+  p.chunk = (p.units + grid - 1) / grid;
+  const int64_t blocks = (p.units + p.chunk - 1) / p.chunk;
+  qknr_multi_kernel<D, W, CTAS><<<static_cast<unsigned>(blocks), 32 * (1 + W), smem, stream>>>(p);
+  return launch_status();
+}
+
+template <int D> int launch_multi_shaped(QknrParams &p, int sms, cudaStream_t stream) {
+  if (p.stage_bytes >= NVB200_QKNR_SMALL_UNIT_BYTES)
+    return launch_multi<D, NVB200_QKNR_LARGE_CONSUMERS, NVB200_QKNR_LARGE_CTAS, NVB200_QKNR_LARGE_STAGES>(p, sms, stream);
+  return launch_multi<D, NVB200_QKNR_SMALL_CONSUMERS, NVB200_QKNR_SMALL_CTAS, NVB200_QKNR_SMALL_STAGES>(p, sms, stream);
+}
+
 template <int D> int launch_bulk_shaped(QknrParams &p, int sms, cudaStream_t stream) {
   if (p.stage_bytes >= NVB200_QKNR_SMALL_UNIT_BYTES)
     return launch_bulk<D, NVB200_QKNR_LARGE_CONSUMERS, NVB200_QKNR_LARGE_CTAS, NVB200_QKNR_LARGE_STAGES>(p, sms, stream);
@@ -621,8 +858,35 @@ int qk_norm_rope_kv_launch(const nvb200_qk_norm_rope_kv_args *a, cudaStream_t st
     }
   }
 
-  // Heads per unit: as many as possible while the units still cover every SM once.
   const int sms = sm_count();
+  // Small tokens in a rank's qkv_proj layout: units of B consecutive tokens (B a power of two, the unit at most
+  // kMultiUnitBytes), when that still gives every SM's CTAs work.
+  {
+    const int64_t row_stage = static_cast<int64_t>(hq + 2 * hkv) * D * 2;
+    const int64_t unit1 = row_stage + D * 4;
+    const bool rows_consecutive = a->k == p.q + static_cast<int64_t>(hq) * D &&
+                                  a->v == p.k + static_cast<int64_t>(hkv) * D &&
+                                  a->q_token_stride == static_cast<int64_t>(hq + 2 * hkv) * D &&
+                                  a->k_token_stride == a->q_token_stride && a->v_token_stride == a->q_token_stride;
+    int B = 1;
+    while (B < kMultiMaxTpu && 2 * B * unit1 <= kMultiUnitBytes) B *= 2;
+    // Measured on B200: 2 tokens per unit ran slower than 1 (6.5 KB tokens: 4.7 vs 5.4 TB/s), 4 and 8 faster.
+    if (B >= 4 && rows_consecutive && (T + B - 1) / B >= 2 * sms) {
+      p.tpu = B;
+      p.splits = 1;
+      p.g = hkv;
+      p.units = (T + B - 1) / B;
+      p.stage_bytes = static_cast<int>((B * unit1 + 127) / 128 * 128);
+      switch (D) {
+        case 64: return launch_multi_shaped<64>(p, sms, stream);
+        case 128: return launch_multi_shaped<128>(p, sms, stream);
+        default: return launch_multi_shaped<256>(p, sms, stream);
+      }
+    }
+  }
+  p.tpu = 1;
+
+  // Heads per unit: as many as possible while the units still cover every SM once.
   int splits = hkv;
   for (int d = 1; d <= hkv; ++d) {
     if (hkv % d == 0 && T * d >= sms) {
