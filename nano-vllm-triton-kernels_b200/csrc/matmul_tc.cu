@@ -743,12 +743,15 @@ int matmul_tc_launch(void *c, const void *a, const void *b, int64_t M, int64_t N
   if (!aligned16(a) || !aligned16(b)) return NVB200_ERR_UNSUPPORTED;
 
   const int sms = sm_count();
-  // CTA pairs (256-row tiles) when M fills at least two 128-row tiles and the pairs get enough tiles to keep
-  // every SM busy; single CTAs (128-row tiles) otherwise.
+  // CTA pairs (256-row tiles) when M fills at least two 128-row tiles and the pairs' tiles occupy at least half the
+  // SMs; single CTAs (128-row tiles) otherwise. Measured on B200: 4096 x 1024 x 3072 (64 pair tiles on 128 SMs)
+  // runs at 1168 TF/s as pairs against 1034 as 128 single-CTA tiles of 128 x 256.
   const int64_t tm1 = (M + BM - 1) / BM;
   const int64_t tm2 = (M + 2 * BM - 1) / (2 * BM);
-  const bool pair = tm1 >= 2 && tm2 * ((N + 255) / 256) * 2 >= sms;
+  const bool pair = tm1 >= 2 && tm2 * ((N + 255) / 256) * 4 >= sms;
   int bn = 256;
+  // 128-column tiles only where 256-column ones would leave SMs idle (an N = 128 MMA takes nearly as long as an
+  // N = 256 one, so they halve the rate per SM).
   if (!pair && tm1 * ((N + 255) / 256) < sms && tm1 * ((N + 127) / 128) > tm1 * ((N + 255) / 256)) bn = 128;
   const int box_n = pair ? bn / 2 : bn;  // B rows (K-major) or columns (MN-major) one CTA loads per stage
 
