@@ -354,7 +354,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int *abort_flag = reinterpret_cast<volatile int *>(hdr + 16 * kMaxStages2 + 36);
   const uint32_t stage0 = smem_addr(smem);
   const int BK = 128 / p.elem_bytes;
-  const int UK = 32 / p.elem_bytes;
   const int num_tiles = p.tiles_m * p.tiles_n;
 
   if (threadIdx.x == 0) {
@@ -517,7 +516,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   volatile int *abort_flag = reinterpret_cast<volatile int *>(hdr + 16 * kMaxStages2 + 36);
   const uint32_t stage0 = smem_addr(smem);
   const int BK = 128 / p.elem_bytes;
-  const int UK = 32 / p.elem_bytes;
   const int num_tiles = p.tiles_m * p.tiles_n;  // 256-row tiles
   const int cluster = blockIdx.x >> 1, clusters = gridDim.x >> 1;
 
@@ -722,6 +720,264 @@ template <typename Kernel> int configure_once(Kernel kernel, int smem, int slot)
   return NVB200_OK;
 }
 
+// ---------------------------------------------------------------------------------------------------------------
+// Skinny GEMM (M <= 64 rows, the decode-sized case): C^T = B^T A^T on the tensor cores, so the weight's N
+// dimension fills the MMA's 128 rows and M is the MMA's N (16..64), split over K across a thread-block cluster of S
+// CTAs whose fp32 partials are summed through distributed shared memory (no global scratch).
+//   * CTA (tile t, rank r) of a cluster multiplies the 128 x K-slice r of B^T (K-major: B = weight.t()) with the
+//     M_pad x K-slice of A, 64-element (128-byte) K blocks through a TMA ring; one elected thread issues
+//     tcgen05.mma (M = 128, N = M_pad) into TMEM. The producer starts loading as soon as its barriers exist.
+//   * S = 1: each thread holds row n of C^T (one TMEM lane) and writes C[:, n] (consecutive n per warp).
+//   * S > 1: CTA r owns rows [r 128/S, (r+1) 128/S) of C^T. Every CTA pushes each row of its partial into the
+//     owner's shared memory (st.shared::cluster, slot [source rank][m][row]); after one cluster barrier each owner
+//     sums its S slots locally and writes C. Nothing reads a peer's memory, so no second barrier is needed.
+// Every wait is bounded; on a timeout a CTA sets the status bit and still takes the cluster barrier, so its peers
+// never wait on it forever.
+
+constexpr int kSkinnyThreads = 128;  // 4 warps: warp 0 lane 0 loads, warp 1 lane 0 issues MMAs, all 4 drain TMEM
+constexpr int kSkinnyMaxStages = 8;
+constexpr int kSkinnyMaxM = 64;
+#ifndef NVB200_SKINNY_KPB
+#define NVB200_SKINNY_KPB 2
+#endif
+
+struct SkinnyParams {
+  void *c;
+  int64_t scm, scn;
+  int M, N, K;
+  int m_pad;        // M rounded up to 16 (the MMA's N)
+  int split;        // CTAs per cluster (K split)
+  int k_blocks;     // 128-byte K blocks in total
+  int kpb;          // K blocks per stage (1 or 2): one tcgen05.commit releases 4 kpb MMAs' operands
+  int stages;
+  uint32_t idesc;
+  int elem_bytes;
+  int c_is_f32;
+  int red_off;      // shared-memory offset of the partial slots [S][m_pad][128 / S] fp32 (S > 1)
+  int hdr_off;      // barriers and the TMEM slot
+  int32_t *status;
+};
+
+NVB200_DEVICE void store_c(const SkinnyParams &p, int m, int n, float v) {
+  const int64_t idx = m * p.scm + static_cast<int64_t>(n) * p.scn;
+  if (p.c_is_f32)
+    static_cast<float *>(p.c)[idx] = v;
+  else
+    static_cast<__nv_bfloat16 *>(p.c)[idx] = __float2bfloat16_rn(v);
+}
+
+// One stage of the skinny kernel: nsub consecutive K blocks from kb, each [B^T tile | A tile].
+NVB200_DEVICE void skinny_load_stage(const CUtensorMap &map_w, const CUtensorMap &map_x, uint32_t full, uint32_t sw,
+                                     int kb, int nsub, uint32_t sub_bytes, uint32_t tile_w, int BK, int n0) {
+  mbar_arrive_expect_tx(full, nsub * sub_bytes);
+  for (int u = 0; u < nsub; ++u) {
+    tma_load_2d(sw + u * sub_bytes, &map_w, (kb + u) * BK, n0, full);
+    tma_load_2d(sw + u * sub_bytes + tile_w, &map_x, (kb + u) * BK, 0, full);
+  }
+}
+
+template <bool TF32>
+__global__ void __launch_bounds__(kSkinnyThreads)
+    matmul_skinny_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x,
+                         const __grid_constant__ SkinnyParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const int S = p.split;
+  const int n0 = (blockIdx.x / S) * BM;  // first row of B^T (column of C) of this tile
+  const int BK = 128 / p.elem_bytes;
+  const uint32_t tile_w = BM * 128, tile_x = static_cast<uint32_t>(p.m_pad) * 128;
+  const uint32_t sub_bytes = tile_w + tile_x;  // one K block: [B^T tile | A tile]
+  const int kpb = p.kpb;
+  const uint32_t stage_bytes = kpb * sub_bytes;
+  const int stages = p.stages;
+  uint8_t *hdr = smem + p.hdr_off;
+  const uint32_t bar_full = smem_addr(hdr);
+  const uint32_t bar_empty = bar_full + 8 * kSkinnyMaxStages;
+  const uint32_t bar_acc = bar_empty + 8 * kSkinnyMaxStages;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(hdr + 16 * kSkinnyMaxStages + 8);
+  const uint32_t stage0 = smem_addr(smem);
+  const uint32_t tmem_cols = p.m_pad <= 32 ? 32 : 64;
+  // This CTA's K blocks: an even share of the tile's blocks.
+  const int kb_begin = static_cast<int>((static_cast<int64_t>(p.k_blocks) * rank) / S);
+  const int kb_end = static_cast<int>((static_cast<int64_t>(p.k_blocks) * (rank + 1)) / S);
+
+  // Thread 0 creates the barriers and, as the producer, fills the ring at once; the rest of the set-up (TMEM) runs
+  // while those loads are in flight.
+  int pst = 0, pkb = kb_begin;  // producer: next stage slot, first K block of the next stage
+  uint32_t pph = 0;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < stages; ++i) {
+      mbar_init(bar_full + 8 * i, 1);
+      mbar_init(bar_empty + 8 * i, 1);
+    }
+    mbar_init(bar_acc, 1);
+    fence_mbar_init();
+    for (int i = 0; pkb < kb_end && i < stages; ++i, pkb += kpb, pst = pst + 1 == stages ? 0 : pst + 1, pph ^= pst == 0)
+      skinny_load_stage(map_w, map_x, bar_full + 8 * pst, stage0 + pst * stage_bytes, pkb, min(kpb, kb_end - pkb),
+                        sub_bytes, tile_w, BK, n0);
+  }
+  if (warp == 1) tmem_alloc(smem_addr(tmem_slot), tmem_cols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  bool ok = true;
+
+  if (warp == 0 && lane == 0) {
+    // ---------------------------------------------------------------- TMA producer (the rest of the K blocks)
+    for (; pkb < kb_end; pkb += kpb, pst = pst + 1 == stages ? 0 : pst + 1, pph ^= pst == 0) {
+      if (!mbar_wait_bounded(bar_empty + 8 * pst, pph ^ 1)) {
+        set_status(p.status, NVB200_STATUS_WAIT_TIMEOUT);
+        break;
+      }
+      skinny_load_stage(map_w, map_x, bar_full + 8 * pst, stage0 + pst * stage_bytes, pkb, min(kpb, kb_end - pkb),
+                        sub_bytes, tile_w, BK, n0);
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    const uint64_t w0 = smem_desc(stage0, 16, 1024, 2), x0 = smem_desc(stage0 + tile_w, 16, 1024, 2);
+    const uint32_t step = stage_bytes >> 4, sub = sub_bytes >> 4;
+    int st = 0;
+    uint32_t ph = 0;
+    for (int kb = kb_begin; kb < kb_end; kb += kpb, st = st + 1 == stages ? 0 : st + 1, ph ^= st == 0) {
+      if (!mbar_wait_bounded(bar_full + 8 * st, ph)) {
+        if (lane == 0) set_status(p.status, NVB200_STATUS_WAIT_TIMEOUT);
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      if (lane == 0) {
+        const int nsub = min(kpb, kb_end - kb);
+        for (int u = 0; u < nsub; ++u) {
+          const uint64_t wd = w0 + st * step + u * sub, xd = x0 + st * step + u * sub;
+#pragma unroll
+          for (int k = 0; k < kMmaPerSub; ++k)
+            tc_mma<TF32>(tmem_base, wd + k * 2, xd + k * 2, p.idesc, (kb > kb_begin || u > 0 || k > 0) ? 1u : 0u);
+        }
+        tc_commit(bar_empty + 8 * st);
+      }
+      __syncwarp();
+    }
+    if (lane == 0) tc_commit(bar_acc);  // arrives once every MMA above has completed
+    __syncwarp();
+  }
+
+  // -------------------------------------------------------------------- epilogue
+  __syncwarp();
+  ok = mbar_wait_bounded(bar_acc, 0) && ok;
+  if (!ok && lane == 0) set_status(p.status, NVB200_STATUS_WAIT_TIMEOUT);
+  tc_fence_after();
+  const int nt = warp * 32 + lane;  // this thread's TMEM lane: row n0 + nt of C^T
+  const uint32_t taddr = tmem_base + (static_cast<uint32_t>(warp * 32) << 16);
+  if (S == 1) {
+    const int n = n0 + nt;
+    for (int c0 = 0; c0 < p.m_pad; c0 += 32) {
+      float v[32];
+      tmem_ld32(taddr + c0, v);
+      if (n < p.N) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (c0 + i < p.M) store_c(p, c0 + i, n, v[i]);
+      }
+    }
+    tc_fence_before();
+    __syncthreads();  // every TMEM read done before the columns are freed
+  } else {
+    // Push this CTA's partial of row nt to its owner: slot [rank][m][nt - owner * rows] of the owner's buffer.
+    const int rows = BM / S;
+    const int owner = nt / rows;
+    const uint32_t dst = map_to_cta(smem_addr(smem + p.red_off), owner) +
+                         static_cast<uint32_t>((static_cast<int>(rank) * p.m_pad * rows + (nt - owner * rows)) * 4);
+    for (int c0 = 0; c0 < p.m_pad; c0 += 32) {
+      float v[32];
+      tmem_ld32(taddr + c0, v);
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (c0 + i < p.m_pad)
+          asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(dst + (c0 + i) * rows * 4), "f"(v[i]) : "memory");
+    }
+    tc_fence_before();
+    cluster_sync();  // every partial is in its owner's memory (and every TMEM read done)
+    // Sum the S slots of this CTA's rows, 4 consecutive rows (columns n of C) per step.
+    const float *red = reinterpret_cast<const float *>(smem + p.red_off);
+    const int qpr = rows / 4;
+    for (int gi = threadIdx.x; gi < p.M * qpr; gi += kSkinnyThreads) {
+      const int m = gi / qpr, q = gi - m * qpr;
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int r = 0; r < S; ++r) {
+        const float4 x = *reinterpret_cast<const float4 *>(red + (r * p.m_pad + m) * rows + 4 * q);
+        acc[0] += x.x, acc[1] += x.y, acc[2] += x.z, acc[3] += x.w;
+      }
+      const int n = n0 + static_cast<int>(rank) * rows + 4 * q;
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        if (n + i < p.N) store_c(p, m, n + i, acc[i]);
+    }
+  }
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, tmem_cols);
+  }
+}
+
+// Launches the skinny kernel for M <= kSkinnyMaxM with K-major A and B (A row-major, B = weight.t()); returns
+// NVB200_ERR_UNSUPPORTED otherwise.
+int launch_skinny(void *c, const void *a, const void *b, int64_t M, int64_t N, int64_t K, int64_t sam, int64_t sbn,
+                  int64_t scm, int64_t scn, bool f32, int32_t *status, cudaStream_t stream) {
+  if (M > kSkinnyMaxM || M <= 0) return NVB200_ERR_UNSUPPORTED;
+  const int es = f32 ? 4 : 2;
+  const int BK = 128 / es;
+  SkinnyParams p{};
+  p.c = c, p.scm = scm, p.scn = scn;
+  p.M = static_cast<int>(M), p.N = static_cast<int>(N), p.K = static_cast<int>(K);
+  p.m_pad = static_cast<int>((M + 15) / 16 * 16);
+  p.k_blocks = static_cast<int>((K + BK - 1) / BK);
+  p.elem_bytes = es, p.c_is_f32 = f32, p.status = status;
+  const int tiles = static_cast<int>((N + BM - 1) / BM);
+  const int sms = sm_count();
+  int split = 1;
+  while (split < 8 && static_cast<int64_t>(tiles) * split * 2 <= sms && split * 2 <= p.k_blocks) split *= 2;
+  p.split = split;
+  CUtensorMap map_w, map_x;
+  if (!make_map(&map_w, b, f32, K, N, sbn, BK, BM) || !make_map(&map_x, a, f32, K, M, sam, BK, p.m_pad))
+    return NVB200_ERR_UNSUPPORTED;
+  const uint32_t fmt = f32 ? 2u : 1u;
+  p.idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | (static_cast<uint32_t>(p.m_pad >> 3) << 17) |
+            (static_cast<uint32_t>(BM >> 4) << 24);
+  const int blocks_per_cta = (p.k_blocks + split - 1) / split;
+  // Two K blocks per stage (8 MMAs per commit) for a K split with at least 4 blocks per CTA; without a split the
+  // smaller ring of three CTAs per SM keeps one block per stage.
+  p.kpb = split > 1 && blocks_per_cta >= 4 ? NVB200_SKINNY_KPB : 1;
+  const int stage_bytes = p.kpb * (BM * 128 + p.m_pad * 128);
+  // One CTA per SM with a K split (the grid is at most one wave); without one, the grid has many waves and three
+  // CTAs per SM overlap one's epilogue with the others' loads.
+  const int ring_budget = split > 1 ? 160 * 1024 : 72 * 1024;
+  p.stages = std::max(1, std::min({kSkinnyMaxStages, (blocks_per_cta + p.kpb - 1) / p.kpb, ring_budget / stage_bytes}));
+  p.red_off = p.stages * stage_bytes;
+  p.hdr_off = p.red_off + (split > 1 ? p.m_pad * BM * 4 : 0);
+  const int smem = 1024 + p.hdr_off + 256;
+  const int rc = f32 ? configure_once(matmul_skinny_kernel<true>, smem, 2) : configure_once(matmul_skinny_kernel<false>, smem, 3);
+  if (rc) return rc;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(tiles * split), 1, 1);
+  cfg.blockDim = dim3(kSkinnyThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(split);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = f32 ? cudaLaunchKernelEx(&cfg, matmul_skinny_kernel<true>, map_w, map_x, p)
+                            : cudaLaunchKernelEx(&cfg, matmul_skinny_kernel<false>, map_w, map_x, p);
+  return e == cudaSuccess ? NVB200_OK : NVB200_ERR_CUDA;
+}
+
 }  // namespace
 
 int matmul_tc_launch(void *c, const void *a, const void *b, int64_t M, int64_t N, int64_t K, int64_t sam,
@@ -741,6 +997,10 @@ int matmul_tc_launch(void *c, const void *a, const void *b, int64_t M, int64_t N
   else if (sbn == 1 && (sbk * es) % 16 == 0) b_mn = true;
   else return NVB200_ERR_UNSUPPORTED;
   if (!aligned16(a) || !aligned16(b)) return NVB200_ERR_UNSUPPORTED;
+  if (M <= kSkinnyMaxM && !a_mn && !b_mn) {
+    const int rc = launch_skinny(c, a, b, M, N, K, sam, sbn, scm, scn, f32, status, stream);
+    if (rc != NVB200_ERR_UNSUPPORTED) return rc;
+  }
 
   const int sms = sm_count();
   // CTA pairs (256-row tiles) when M fills at least two 128-row tiles and the pairs' tiles occupy at least half the

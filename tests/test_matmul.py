@@ -92,3 +92,38 @@ def test_strided_operands(cuda):
     c = matmul(a, b)
     rtol, atol = om.matmul_tolerance("bf16", "ieee", 96)
     torch.testing.assert_close(c.double(), om.matmul(a, b), rtol=rtol, atol=atol)
+
+
+# Decode-sized rows (M <= 64) with A row-major and B = weight.t() run the swap-AB kernel that splits K over a
+# cluster of up to 8 CTAs and sums their partials through distributed shared memory: every M padding (16, 32, 48,
+# 64 rows of the MMA), K splits of 1-8 with ragged shares and K tails, N tails.
+SKINNY = [(1, 4096, 1024), (7, 1000, 104), (16, 128, 64), (32, 4096, 1024), (32, 6144, 1024), (32, 1024, 3072),
+          (33, 4096, 4096), (48, 3000, 1000), (64, 256, 8192), (64, 151936 // 16, 1024)]
+
+
+@pytest.mark.parametrize("M,N,K", SKINNY)
+@pytest.mark.parametrize("dtype,prec", [("bf16", "ieee"), ("fp32", "tf32")])
+def test_skinny(cuda, M, N, K, dtype, prec):
+    g = torch.Generator(device=cuda).manual_seed(M * 7 + N + K)
+    s = 1 / math.sqrt(K)
+    a = (torch.randn(M, K, device=cuda, generator=g) * s).to(DTYPES[dtype])
+    b = (torch.randn(N, K, device=cuda, generator=g) * s).to(DTYPES[dtype]).t()
+    c = matmul(a, b, prec)
+    assert c.shape == (M, N)
+    ref = om.matmul(a, b) if dtype == "bf16" else om.matmul(om.tf32_round(a), om.tf32_round(b))
+    scale = ref.abs().max().item()
+    tol = dict(rtol=1.6e-2, atol=1e-2 * scale) if dtype == "bf16" else dict(rtol=1e-3, atol=1e-4 * scale)
+    torch.testing.assert_close(c.double(), ref, **tol)
+    from nanovllm_b200 import _lib
+    assert _lib.status(cuda, clear=True) == 0
+
+
+def test_skinny_row_view(cuda):
+    """A as every other row of a wider buffer (row pitch > K) with M = 32."""
+    g = torch.Generator(device=cuda).manual_seed(3)
+    A = torch.randn(64, 1024 + 64, device=cuda, generator=g).to(torch.bfloat16)
+    a = A[::2, 32:32 + 1024]
+    b = torch.randn(2048, 1024, device=cuda, generator=g).to(torch.bfloat16).t()
+    c = matmul(a, b)
+    rtol, atol = om.matmul_tolerance("bf16", "ieee", 1024)
+    torch.testing.assert_close(c.double(), om.matmul(a, b), rtol=rtol, atol=atol)
