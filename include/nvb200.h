@@ -119,14 +119,26 @@ NVB200_API int nvb200_silu_and_mul(void *out, const void *x, int64_t rows, int64
  * Any strides for A and B (B is typically weight.t(), strides (1, K)); C any strides.
  * dtype: NVB200_BF16 (tcgen05 kind::f16) or NVB200_F32 with tf32 = 1 (tcgen05 kind::tf32, inputs rounded to
  * tf32) or tf32 = 0 ("ieee": fp32 FMA on the CUDA cores).
- * workspace: device scratch of workspace_bytes (16-byte aligned) used when an operand's layout cannot be read
- * by TMA and must be packed first; nvb200_matmul_workspace_size() tells how much a call needs (0 for the
- * usual layouts), and a call given less returns NVB200_ERR_ARG. */
+ * workspace, workspace_bytes: reserved for kernels that need device scratch; nvb200_matmul_workspace_size()
+ * tells how much a call needs, and every current path needs none (it returns 0, and both may be 0 / NULL). */
 NVB200_API int64_t nvb200_matmul_workspace_size(int64_t M, int64_t N, int64_t K, int64_t sam, int64_t sak, int64_t sbk,
                                      int64_t sbn, int dtype);
 NVB200_API int nvb200_matmul(void *c, const void *a, const void *b, int64_t M, int64_t N, int64_t K, int64_t sam,
                   int64_t sak, int64_t sbk, int64_t sbn, int64_t scm, int64_t scn, int dtype, int tf32,
                   void *workspace, int64_t workspace_bytes, int32_t *status, nvb200_stream_t stream);
+
+/* out[M, N] = silu(G).to(bf16) * U, where [G | U] = A[M, K] @ B[K, 2N] in bf16 (G the first N columns): the gate_up
+ * projection and SiLU x Mul of a SwiGLU MLP in one kernel, without writing the [M, 2N] intermediate. Bitwise equal
+ * to nvb200_matmul into a bf16 [M, 2N] followed by nvb200_silu_and_mul.
+ * Replaces: nanovllm/kernels/matmul.py:84-99 (matmul, whose module notes plan this SiLU*up epilogue at :3-4)
+ * followed by nanovllm/kernels/swiglu.py:34-43 (silu_and_mul), as layers/activation.py:15-22 applies it to
+ * MergedColumnParallelLinear's output (models/qwen3.py:133-137).
+ * bf16 only; A and B each with one unit stride (TMA-readable, 16-byte aligned), out row-major with a 16-byte row
+ * pitch scm. Returns NVB200_ERR_UNSUPPORTED for layouts it does not take (K = 0 included), in which case the
+ * caller runs the two steps separately. */
+NVB200_API int nvb200_matmul_silu_and_mul(void *out, const void *a, const void *b, int64_t M, int64_t N, int64_t K,
+                               int64_t sam, int64_t sak, int64_t sbk, int64_t sbn, int64_t scm, int32_t *status,
+                               nvb200_stream_t stream);
 
 #ifdef __cplusplus
 }

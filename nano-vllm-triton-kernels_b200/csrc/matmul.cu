@@ -15,7 +15,9 @@
 
 namespace nvb200 {
 
-// Implemented in matmul_tc.cu. Returns NVB200_ERR_UNSUPPORTED when the layout is not TMA-readable.
+// Implemented in matmul_tc.cu. Return NVB200_ERR_UNSUPPORTED when the layout is not TMA-readable.
+int matmul_swiglu_launch(void *c, const void *a, const void *b, int64_t M, int64_t N, int64_t K, int64_t sam,
+                         int64_t sak, int64_t sbk, int64_t sbn, int64_t scm, int32_t *status, cudaStream_t stream);
 int matmul_tc_launch(void *c, const void *a, const void *b, int64_t M, int64_t N, int64_t K, int64_t sam,
                      int64_t sak, int64_t sbk, int64_t sbn, int64_t scm, int64_t scn, int dtype, int32_t *status,
                      cudaStream_t stream);
@@ -177,4 +179,15 @@ extern "C" int nvb200_matmul(void *c, const void *a, const void *b, int64_t M, i
     if (rc != NVB200_ERR_UNSUPPORTED) return rc;
   }
   return matmul_simt_launch(c, a, b, M, N, K, sam, sak, sbk, sbn, scm, scn, dtype, tf32 != 0, s);
+}
+
+extern "C" int nvb200_matmul_silu_and_mul(void *c, const void *a, const void *b, int64_t M, int64_t N, int64_t K,
+                                          int64_t sam, int64_t sak, int64_t sbk, int64_t sbn, int64_t scm,
+                                          int32_t *status, nvb200_stream_t stream) {
+  if (M < 0 || N < 0 || K < 0) return NVB200_ERR_ARG;
+  if (M == 0 || N == 0) return NVB200_OK;
+  if (K == 0) return NVB200_ERR_UNSUPPORTED;  // silu(0) * 0: left to the caller's unfused path
+  if (!c || !a || !b) return NVB200_ERR_ARG;
+  if (int rc = check_device()) return rc;
+  return matmul_swiglu_launch(c, a, b, M, N, K, sam, sak, sbk, sbn, scm, status, reinterpret_cast<cudaStream_t>(stream));
 }

@@ -2,15 +2,17 @@
 //
 // Behaviour follows nanovllm/kernels/matmul.py:33-81 (tiles in GROUP_M-swizzled order, K tail zero-filled, masked
 // M/N edges); the machinery is Blackwell's:
-//   * Persistent kernel, one CTA per SM, 128 x BN output tiles (BN = 256, or 128 when that gives more tiles per SM).
+//   * Persistent kernels with 128 x BN output tiles on one CTA (BN = 256, or 128 when that gives more tiles per SM)
+//     or 256 x 256 tiles on a CTA pair (cta_group::2, below), and a skinny kernel for M <= 64 (further below).
 //   * Warp 0 (one elected lane) moves A and B tiles HBM -> shared memory with TMA (cp.async.bulk.tensor, 128-byte
-//     swizzle) into a 4-stage ring; completion is counted on mbarriers.
+//     swizzle) into a ring of stages of two 64-wide K sub-tiles; completion is counted on mbarriers.
 //   * Warp 1 (one elected lane) issues tcgen05.mma (kind::f16 for bf16, kind::tf32 for fp32) from the shared-memory
 //     descriptors into a TMEM accumulator, and tcgen05.commit releases each stage when its MMAs are done. Two TMEM
 //     accumulators (2 x BN columns) let the epilogue of one tile overlap the MMAs of the next.
-//   * Warps 2-5 (the epilogue) read the accumulator with tcgen05.ld (each warp its 32-lane quarter), round to C's
-//     dtype, stage 32 x 32 chunks in swizzled shared memory and write them with TMA stores (a thread holds one row,
-//     so direct stores would scatter every warp instruction over 32 rows).
+//   * Warps 2-9 (the epilogue; two per 32-lane TMEM quarter, each draining half of the columns) read the
+//     accumulator with tcgen05.ld, round to C's dtype, stage 32 x 32 chunks in swizzled shared memory and write
+//     them with TMA stores (a thread holds one row, so direct stores would scatter every warp instruction over
+//     32 rows). The gate_up variant pairs gate and up columns in one tile and applies SiLU x Mul there instead.
 // Operand layouts: A and B may each be K-major (the contiguous dim is K: A row-major, B = weight.t()) or MN-major
 // (B row-major [K, N], A column-major); the instruction descriptor's major bits select it, so no transpose pass.
 // Any layout TMA cannot describe (a non-unit inner stride, or a row pitch that is not a multiple of 16 bytes) is
@@ -25,7 +27,9 @@ namespace nvb200 {
 namespace {
 
 constexpr int BM = 128;
-constexpr int kEpilogueWarps = 4;
+// Epilogue warps: two per TMEM lane quarter (a warp may only read the quarter warp_id % 4), each draining half of a
+// tile's columns. Four warps kept up with the MMAs of the plain GEMM but not with the SiLU x Mul epilogue at short K.
+constexpr int kEpilogueWarps = 8;
 constexpr int kThreads = 32 * (2 + kEpilogueWarps);
 constexpr int kGroupM = 8;
 constexpr int kTileBytesA = BM * 128;  // one 128-byte swizzle row per M row (BK * elem = 128 B)
@@ -51,7 +55,9 @@ struct TcParams {
   int elem_bytes;  // 2 (bf16) or 4 (fp32/tf32)
   int c_is_f32;
   int c_tma;          // 1: C is written by TMA stores from shared-memory staging (row-major C, 16-byte pitch)
+  int swiglu;         // 1: gate_up GEMM with the SiLU x Mul epilogue (B holds 2 * N columns: gate | up)
   uint32_t epi_off;   // byte offset of the epilogue staging buffers in shared memory
+  int epi_bufs;       // staging tiles per epilogue warp: 2 for bf16 C (double-buffered), 1 for fp32 C
   uint32_t hdr_off;   // byte offset of the barriers / TMEM slot
   int32_t *status;
 };
@@ -237,6 +243,14 @@ NVB200_DEVICE OperandDescs operand_descs(const TcParams &p, uint32_t stage0, int
   return d;
 }
 
+// Column of B that tile column c (0..BN) of output tile pn reads. Plain GEMM: pn * BN + c. Gate_up GEMM with the
+// SiLU x Mul epilogue: a 256-column tile pairs the 128 gate columns [pn * 128, +128) with the matching up columns
+// [N + pn * 128, +128), N being the output width (B holds gate | up, 2 N columns).
+NVB200_DEVICE int b_col(const TcParams &p, int pn, int c) {
+  if (!p.swiglu) return pn * p.bn + c;
+  return c < 128 ? pn * 128 + c : p.N + pn * 128 + (c - 128);
+}
+
 // GROUP_M-swizzled tile order (nanovllm/kernels/matmul.py:50-57).
 NVB200_DEVICE void tile_coords(int tile, int tiles_m, int tiles_n, int &pm, int &pn) {
   const int in_group = kGroupM * tiles_n;
@@ -301,8 +315,11 @@ NVB200_DEVICE void store_tile_tma(const TcParams &p, const CUtensorMap *map_c, u
     float v[32];
     tmem_ld32(taddr + c0, v);
     if (row0 >= p.M || col_base + c0 >= p.N) continue;
-    const uint32_t buf = stage + (chunks & 1) * 32 * row_bytes;
-    if (chunks >= 2 && lane == 0) bulk_wait_read<1>();
+    const uint32_t buf = stage + (p.epi_bufs == 2 ? (chunks & 1) * 32 * row_bytes : 0);
+    if (lane == 0) {
+      if (p.epi_bufs == 2 && chunks >= 2) bulk_wait_read<1>();
+      if (p.epi_bufs == 1 && chunks >= 1) bulk_wait_read<0>();
+    }
     __syncwarp();
     const uint32_t row_addr = buf + lane * row_bytes;
     if (p.c_is_f32) {
@@ -319,6 +336,40 @@ NVB200_DEVICE void store_tile_tma(const TcParams &p, const CUtensorMap *map_c, u
                             v[8 * j + 4], v[8 * j + 5], v[8 * j + 6], v[8 * j + 7]};
         st_shared_v4(row_addr + ((j ^ ((lane >> 1) & 3)) << 4), pack8(f));
       }
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_2d(map_c, col_base + c0, row0, buf);
+      bulk_commit();
+    }
+    ++chunks;
+  }
+}
+
+// Epilogue of the gate_up GEMM: per 32 output columns, the gate accumulators (TMEM columns c0..) and the up
+// accumulators (columns 128 + c0..) are rounded to bf16 (what the plain GEMM would write) and combined by the
+// SiLU x Mul kernel's own routine, so the result equals silu_and_mul(matmul(a, b)) bit for bit; staging and TMA
+// stores as store_tile_tma (bf16 C).
+NVB200_DEVICE void store_tile_tma_swiglu(const TcParams &p, const CUtensorMap *map_c, uint32_t taddr, int row0,
+                                         int col_base, int c_begin, int c_end, uint32_t stage, int &chunks) {
+  const int lane = threadIdx.x & 31;
+  for (int c0 = c_begin; c0 < c_end; c0 += 32) {
+    float g[32], u[32];
+    tmem_ld32(taddr + c0, g);
+    tmem_ld32(taddr + 128 + c0, u);
+    if (row0 >= p.M || col_base + c0 >= p.N) continue;
+    const uint32_t buf = stage + (chunks & 1) * 32 * 64;
+    if (chunks >= 2 && lane == 0) bulk_wait_read<1>();
+    __syncwarp();
+    const uint32_t row_addr = buf + lane * 64;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float gf[8] = {g[8 * j], g[8 * j + 1], g[8 * j + 2], g[8 * j + 3],
+                           g[8 * j + 4], g[8 * j + 5], g[8 * j + 6], g[8 * j + 7]};
+      const float uf[8] = {u[8 * j], u[8 * j + 1], u[8 * j + 2], u[8 * j + 3],
+                           u[8 * j + 4], u[8 * j + 5], u[8 * j + 6], u[8 * j + 7]};
+      st_shared_v4(row_addr + ((j ^ ((lane >> 1) & 3)) << 4), silu_mul8_bf16(pack8(gf), pack8(uf)));
     }
     fence_proxy_async_smem();
     __syncwarp();
@@ -404,7 +455,10 @@ __global__ void __launch_bounds__(kThreads, 1)
               tma_load_2d(sa, &map_a, k0, m0, full);
             }
             if (p.b_mn_major) {  // B stored [K][N]: boxes of 128 B along N, BK rows
-              for (int j = 0; j < p.bn / BK; ++j) tma_load_2d(sb + j * BK * 128, &map_b, n0 + j * BK, k0, full);
+              for (int j = 0; j < p.bn / BK; ++j) tma_load_2d(sb + j * BK * 128, &map_b, b_col(p, pn, j * BK), k0, full);
+            } else if (p.swiglu) {  // two boxes of 128 rows: gate, then up
+              tma_load_2d(sb, &map_b, k0, b_col(p, pn, 0), full);
+              tma_load_2d(sb + 128 * 128, &map_b, k0, b_col(p, pn, 128), full);
             } else {
               tma_load_2d(sb, &map_b, k0, n0, full);
             }
@@ -452,8 +506,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ---------------------------------------------------------------- epilogue: TMEM -> registers -> C
-    const int q = warp & 3;  // TMEM lane quarter this warp may read
-    const uint32_t epi_stage = smem_addr(smem) + p.epi_off + (warp - 2) * 64 * (p.c_is_f32 ? 128 : 64);
+    const int q = warp & 3;         // TMEM lane quarter this warp may read
+    const int half = (warp - 2) >> 2;  // which half of the tile's columns it drains
+    const uint32_t epi_stage = smem_addr(smem) + p.epi_off + (warp - 2) * p.epi_bufs * 32 * (p.c_is_f32 ? 128 : 64);
     int chunks = 0;
     int local = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
@@ -467,10 +522,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_after();
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * p.bn;
-      if (p.c_tma)
-        store_tile_tma(p, &map_c, taddr, pm * BM + q * 32, pn * p.bn, p.bn, epi_stage, chunks);
+      const int hc = p.bn / 2;  // accumulator columns per half
+      if (p.swiglu)
+        store_tile_tma_swiglu(p, &map_c, taddr, pm * BM + q * 32, pn * 128, half * 64, half * 64 + 64, epi_stage,
+                              chunks);
+      else if (p.c_tma)
+        store_tile_tma(p, &map_c, taddr + half * hc, pm * BM + q * 32, pn * p.bn + half * hc, hc, epi_stage, chunks);
       else
-        store_tile_rows(p, taddr, pm * BM + q * 32 + lane, pn * p.bn, p.bn);
+        store_tile_rows(p, taddr + half * hc, pm * BM + q * 32 + lane, pn * p.bn + half * hc, hc);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar_acc_empty + 8 * buf);
@@ -548,7 +607,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         int pm, pn;
         tile_coords(tile, p.tiles_m, p.tiles_n, pm, pn);
         const int m0 = pm * 2 * BM + static_cast<int>(rank) * BM;
-        const int n0 = pn * p.bn + static_cast<int>(rank) * half_bn;
+        const int n0 = b_col(p, pn, static_cast<int>(rank) * half_bn);  // this CTA's half of the B tile
         for (int kb = 0; kb < p.k_blocks; ++kb, st = st + 1 == stages ? 0 : st + 1, ph ^= st == 0) {
           if (!mbar_wait_bounded(bar_empty + 8 * st, ph ^ 1)) {
             set_status(p.status, NVB200_STATUS_WAIT_TIMEOUT);
@@ -618,9 +677,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     }
   } else {
     // ---------------------------------------------------------------- epilogue (both CTAs, own TMEM lanes)
-    const int q = warp & 3;
+    const int q = warp & 3;            // TMEM lane quarter this warp may read
+    const int half = (warp - 2) >> 2;  // which half of the tile's columns it drains
     const uint32_t leader_acc_empty = map_to_cta(bar_acc_empty, 0);
-    const uint32_t epi_stage = smem_addr(smem) + p.epi_off + (warp - 2) * 64 * (p.c_is_f32 ? 128 : 64);
+    const uint32_t epi_stage = smem_addr(smem) + p.epi_off + (warp - 2) * p.epi_bufs * 32 * (p.c_is_f32 ? 128 : 64);
     int chunks = 0;
     int local = 0;
     for (int tile = cluster; tile < num_tiles; tile += clusters, ++local) {
@@ -635,10 +695,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * p.bn;
       const int row0 = pm * 2 * BM + static_cast<int>(rank) * BM + q * 32;
-      if (p.c_tma)
-        store_tile_tma(p, &map_c, taddr, row0, pn * p.bn, p.bn, epi_stage, chunks);
+      const int hc = p.bn / 2;  // accumulator columns per half
+      if (p.swiglu)
+        store_tile_tma_swiglu(p, &map_c, taddr, row0, pn * 128, half * 64, half * 64 + 64, epi_stage, chunks);
+      else if (p.c_tma)
+        store_tile_tma(p, &map_c, taddr + half * hc, row0, pn * p.bn + half * hc, hc, epi_stage, chunks);
       else
-        store_tile_rows(p, taddr, row0 + lane, pn * p.bn, p.bn);
+        store_tile_rows(p, taddr + half * hc, row0 + lane, pn * p.bn + half * hc, hc);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(leader_acc_empty + 8 * buf);
@@ -980,10 +1043,15 @@ int launch_skinny(void *c, const void *a, const void *b, int64_t M, int64_t N, i
 
 }  // namespace
 
-int matmul_tc_launch(void *c, const void *a, const void *b, int64_t M, int64_t N, int64_t K, int64_t sam,
-                     int64_t sak, int64_t sbk, int64_t sbn, int64_t scm, int64_t scn, int dtype, int32_t *status,
-                     cudaStream_t stream) {
-  if (K <= 0 || M > 0x7fffffffLL || N > 0x7fffffffLL || K > 0x7fffffffLL) return NVB200_ERR_UNSUPPORTED;
+namespace {
+
+// Shared launcher. swiglu: N is the output width, B holds 2 N columns (gate | up) and the epilogue is SiLU x Mul
+// (bf16 only, C row-major with a 16-byte row pitch).
+int tc_launch(void *c, const void *a, const void *b, int64_t M, int64_t N, int64_t K, int64_t sam, int64_t sak,
+              int64_t sbk, int64_t sbn, int64_t scm, int64_t scn, int dtype, bool swiglu, int32_t *status,
+              cudaStream_t stream) {
+  if (K <= 0 || M > 0x7fffffffLL || N > 0x3fffffffLL || K > 0x7fffffffLL) return NVB200_ERR_UNSUPPORTED;
+  if (swiglu && dtype != NVB200_BF16) return NVB200_ERR_UNSUPPORTED;
   const bool f32 = dtype == NVB200_F32;
   const int es = f32 ? 4 : 2;
   const int BK = 128 / es;
@@ -997,7 +1065,7 @@ int matmul_tc_launch(void *c, const void *a, const void *b, int64_t M, int64_t N
   else if (sbn == 1 && (sbk * es) % 16 == 0) b_mn = true;
   else return NVB200_ERR_UNSUPPORTED;
   if (!aligned16(a) || !aligned16(b)) return NVB200_ERR_UNSUPPORTED;
-  if (M <= kSkinnyMaxM && !a_mn && !b_mn) {
+  if (M <= kSkinnyMaxM && !a_mn && !b_mn && !swiglu) {
     const int rc = launch_skinny(c, a, b, M, N, K, sam, sbn, scm, scn, f32, status, stream);
     if (rc != NVB200_ERR_UNSUPPORTED) return rc;
   }
@@ -1008,18 +1076,22 @@ int matmul_tc_launch(void *c, const void *a, const void *b, int64_t M, int64_t N
   // runs at 1168 TF/s as pairs against 1034 as 128 single-CTA tiles of 128 x 256.
   const int64_t tm1 = (M + BM - 1) / BM;
   const int64_t tm2 = (M + 2 * BM - 1) / (2 * BM);
-  const bool pair = tm1 >= 2 && tm2 * ((N + 255) / 256) * 4 >= sms;
+  const int64_t out_cols = swiglu ? 128 : 256;  // output columns of a 256-column tile
+  const bool pair = tm1 >= 2 && tm2 * ((N + out_cols - 1) / out_cols) * 4 >= sms;
   int bn = 256;
   // 128-column tiles only where 256-column ones would leave SMs idle (an N = 128 MMA takes nearly as long as an
   // N = 256 one, so they halve the rate per SM).
-  if (!pair && tm1 * ((N + 255) / 256) < sms && tm1 * ((N + 127) / 128) > tm1 * ((N + 255) / 256)) bn = 128;
-  const int box_n = pair ? bn / 2 : bn;  // B rows (K-major) or columns (MN-major) one CTA loads per stage
+  if (!swiglu && !pair && tm1 * ((N + 255) / 256) < sms && tm1 * ((N + 127) / 128) > tm1 * ((N + 255) / 256)) bn = 128;
+  // B rows (K-major) or columns (MN-major) one TMA box holds: half a tile per CTA of a pair, and the gate / up
+  // halves of a gate_up tile are separate boxes.
+  const int box_n = pair || swiglu ? bn / 2 : bn;
+  const int64_t b_cols = swiglu ? 2 * N : N;
 
   // 32-bit MN-major operands use the 32-byte-atom swizzle (4-row atoms); everything else the 16-byte one.
   CUtensorMap map_a, map_b;
   const bool ok_a = a_mn ? make_map(&map_a, a, f32, M, K, sak, BK, BK, f32) : make_map(&map_a, a, f32, K, M, sam, BK, BM);
-  const bool ok_b = b_mn ? make_map(&map_b, b, f32, N, K, sbk, BK, BK, f32)
-                         : make_map(&map_b, b, f32, K, N, sbn, BK, box_n);
+  const bool ok_b = b_mn ? make_map(&map_b, b, f32, b_cols, K, sbk, BK, BK, f32)
+                         : make_map(&map_b, b, f32, K, b_cols, sbn, BK, box_n);
   if (!ok_a || !ok_b) return NVB200_ERR_UNSUPPORTED;
 
   TcParams p{};
@@ -1031,7 +1103,8 @@ int matmul_tc_launch(void *c, const void *a, const void *b, int64_t M, int64_t N
   p.K = static_cast<int>(K);
   p.bn = bn;
   p.tiles_m = static_cast<int>(pair ? tm2 : tm1);
-  p.tiles_n = static_cast<int>((N + bn - 1) / bn);
+  p.tiles_n = static_cast<int>(swiglu ? (N + 127) / 128 : (N + bn - 1) / bn);  // output columns per tile: 128 or bn
+  p.swiglu = swiglu;
   // Two 64-wide K sub-tiles per stage: one tcgen05.commit then releases 8 MMAs' operands. (Each commit and
   // stage handoff idles the tensor pipe for some hundreds of cycles; measured on B200, 4 MMAs per commit ran at
   // 58 % of the back-to-back MMA rate, 8 at 92 %, 16 at 98 %.)
@@ -1048,8 +1121,10 @@ int matmul_tc_launch(void *c, const void *a, const void *b, int64_t M, int64_t N
   // C through shared memory and TMA stores when C is row-major with a 16-byte pitch; direct stores otherwise.
   CUtensorMap map_c;
   p.c_tma = scn == 1 && (scm * es) % 16 == 0 && aligned16(c) && make_map_c(&map_c, c, f32, M, N, scm);
+  if (swiglu && !p.c_tma) return NVB200_ERR_UNSUPPORTED;
   if (!p.c_tma) map_c = map_a;  // unused
-  const int epi_bytes = p.c_tma ? kEpilogueWarps * 2 * 32 * 32 * es : 0;
+  p.epi_bufs = f32 ? 1 : 2;
+  const int epi_bytes = p.c_tma ? kEpilogueWarps * p.epi_bufs * 32 * 32 * es : 0;
   // Instruction descriptor: D fp32 (bits 4-5 = 1), A/B format (bits 7-9, 10-12: 1 = bf16, 2 = tf32), major bits
   // 15/16 (1 = MN-major), N >> 3 at bit 17, M >> 4 at bit 24 (M = 256 for a CTA pair).
   const uint32_t fmt = f32 ? 2u : 1u;
@@ -1091,6 +1166,19 @@ int matmul_tc_launch(void *c, const void *a, const void *b, int64_t M, int64_t N
   else
     matmul_tc_kernel<false><<<grid, kThreads, smem, stream>>>(map_a, map_b, map_c, p);
   return launch_status();
+}
+
+}  // namespace
+
+int matmul_tc_launch(void *c, const void *a, const void *b, int64_t M, int64_t N, int64_t K, int64_t sam,
+                     int64_t sak, int64_t sbk, int64_t sbn, int64_t scm, int64_t scn, int dtype, int32_t *status,
+                     cudaStream_t stream) {
+  return tc_launch(c, a, b, M, N, K, sam, sak, sbk, sbn, scm, scn, dtype, false, status, stream);
+}
+
+int matmul_swiglu_launch(void *c, const void *a, const void *b, int64_t M, int64_t N, int64_t K, int64_t sam,
+                         int64_t sak, int64_t sbk, int64_t sbn, int64_t scm, int32_t *status, cudaStream_t stream) {
+  return tc_launch(c, a, b, M, N, K, sam, sak, sbk, sbn, scm, 1, NVB200_BF16, true, status, stream);
 }
 
 }  // namespace nvb200

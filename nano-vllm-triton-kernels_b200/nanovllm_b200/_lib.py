@@ -21,7 +21,7 @@ STATUS_BAD_POSITION, STATUS_BAD_SLOT, STATUS_WAIT_TIMEOUT = 1, 2, 4
 
 # Every extern "C" function of include/nvb200.h; tests check that the library exports each one.
 EXPORTS = ("nvb200_status_string", "nvb200_qk_norm_rope_kv", "nvb200_rms_norm", "nvb200_fused_add_rms_norm",
-           "nvb200_silu_and_mul", "nvb200_matmul_workspace_size", "nvb200_matmul")
+           "nvb200_silu_and_mul", "nvb200_matmul_workspace_size", "nvb200_matmul", "nvb200_matmul_silu_and_mul")
 
 _vp, _i64, _i32, _f32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32, ctypes.c_float
 
@@ -63,6 +63,8 @@ def _declare(lib):
     lib.nvb200_matmul_workspace_size.restype = _i64
     lib.nvb200_matmul.argtypes = [_vp, _vp, _vp] + [_i64] * 9 + [ctypes.c_int, ctypes.c_int, _vp, _i64, _vp, _vp]
     lib.nvb200_matmul.restype = ctypes.c_int
+    lib.nvb200_matmul_silu_and_mul.argtypes = [_vp, _vp, _vp] + [_i64] * 8 + [_vp, _vp]
+    lib.nvb200_matmul_silu_and_mul.restype = ctypes.c_int
 
 
 def lib():

@@ -33,3 +33,26 @@ def matmul(a: torch.Tensor, b: torch.Tensor, input_precision: str = "ieee") -> t
                                             _lib.status_word(a.device).data_ptr(), _lib.stream_of(a)),
                    "matmul")
     return c
+
+
+def matmul_silu_and_mul(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """silu_and_mul(matmul(a, b)) for bf16 a [M, K] and b [K, 2 N] ([gate | up] columns, e.g. a merged gate_up
+    weight.t()), -> [M, N] bf16, in one kernel (`nvb200_matmul_silu_and_mul`) that never writes the [M, 2 N]
+    intermediate. Bitwise equal to the two-step form, which it runs instead for layouts the fused kernel does not
+    take (and for K = 0)."""
+    if not (a.ndim == 2 and b.ndim == 2 and a.shape[1] == b.shape[0] and b.shape[1] % 2 == 0):
+        raise AssertionError((a.shape, b.shape))
+    if not (a.dtype == b.dtype == torch.bfloat16):
+        raise AssertionError((a.dtype, b.dtype))
+    M, K = a.shape
+    N = b.shape[1] // 2
+    out = torch.empty((M, N), device=a.device, dtype=a.dtype)
+    if M and N:
+        rc = _lib.lib().nvb200_matmul_silu_and_mul(out.data_ptr(), a.data_ptr(), b.data_ptr(), M, N, K, a.stride(0),
+                                                   a.stride(1), b.stride(0), b.stride(1), out.stride(0),
+                                                   _lib.status_word(a.device).data_ptr(), _lib.stream_of(a))
+        if rc == _lib.ERR_UNSUPPORTED:
+            from nanovllm_b200.kernels.swiglu import silu_and_mul
+            return silu_and_mul(matmul(a, b))
+        _lib.check(rc, "matmul_silu_and_mul")
+    return out

@@ -127,3 +127,36 @@ def test_skinny_row_view(cuda):
     c = matmul(a, b)
     rtol, atol = om.matmul_tolerance("bf16", "ieee", 1024)
     torch.testing.assert_close(c.double(), om.matmul(a, b), rtol=rtol, atol=atol)
+
+
+# gate_up GEMM with the SiLU x Mul epilogue: B = [gate | up] columns, out = silu(gate) * up without the [M, 2N]
+# intermediate. Against the two-step form through this library (the same tensor-core accumulation, so bitwise
+# where both run the tiled kernels, M > 64; the skinny kernel sums in another order) and against the oracle (fp64 product rounded to bf16, then the torch
+# SiLU x Mul) within bf16 tolerance.
+GATE_UP = [(100, 3072, 1024), (300, 1000, 104), (2048, 3072, 1024), (4096, 3072, 1024), (1000, 128, 256),
+           (257, 200, 512), (32, 3072, 1024), (7, 384, 64)]
+
+
+@pytest.mark.parametrize("M,N,K", GATE_UP)
+@pytest.mark.parametrize("b_transposed", [True, False])
+def test_matmul_silu_and_mul(cuda, M, N, K, b_transposed):
+    from nanovllm_b200.kernels.matmul import matmul_silu_and_mul
+    from nanovllm_b200.kernels.swiglu import silu_and_mul
+    g = torch.Generator(device=cuda).manual_seed(M + N + K)
+    a = (torch.randn(M, K, device=cuda, generator=g) / math.sqrt(K)).to(torch.bfloat16)
+    if b_transposed:
+        b = torch.randn(2 * N, K, device=cuda, generator=g).to(torch.bfloat16).t()
+    else:
+        b = torch.randn(K, 2 * N, device=cuda, generator=g).to(torch.bfloat16)
+    out = matmul_silu_and_mul(a, b)
+    assert out.shape == (M, N) and out.dtype == torch.bfloat16
+    two_step = silu_and_mul(matmul(a, b))
+    ref = om.silu_and_mul(om.matmul(a, b).to(torch.bfloat16)).double()
+    scale = ref.abs().max().item()
+    if M > 64:
+        assert torch.equal(out, two_step)
+    else:  # the two-step GEMM is the skinny kernel here: another fp32 summation order
+        torch.testing.assert_close(out.double(), two_step.double(), rtol=1.6e-2, atol=1e-2 * scale)
+    torch.testing.assert_close(out.double(), ref, rtol=1.6e-2, atol=1e-2 * scale)
+    from nanovllm_b200 import _lib
+    assert _lib.status(cuda, clear=True) == 0
