@@ -18,7 +18,9 @@ inputs (qkv, positions, slots) copied from pinned host memory and q_out copied b
 it, tests/test_oracle.py), run on the host cores in bf16.
 
 Other workloads (not the driver's headline): fused06b (config 1 shape at T = 8192), norm (config 2: rms_norm,
-add_rms_norm, silu_and_mul at T = 8192), matmul (config 4, bf16 M = K = N = 4096).
+add_rms_norm, silu_and_mul at T = 8192), matmul (config 4, bf16 M = K = N = 4096), gateup (the gate_up GEMM with
+the SiLU x Mul epilogue at the Qwen3-8B MLP shape, M = 4096), decode (config 5: the reference's decode step per
+backend).
 """
 import argparse
 import datetime
@@ -46,7 +48,7 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", default="fused8b", choices=["fused8b", "fused06b", "norm", "matmul", "decode"])
+    ap.add_argument("--workload", default="fused8b", choices=["fused8b", "fused06b", "norm", "matmul", "gateup", "decode"])
     ap.add_argument("--decode-worker", default=None, help=argparse.SUPPRESS)
     ap.add_argument("--decode-backends", default="b200,compile,triton_fused")
     ap.add_argument("--decode-batch", type=int, default=32)
@@ -316,6 +318,39 @@ def matmul_workload(args, rank, world, dev):
                         "parallelism": f"column-parallel x{world}", "l2": "flushed between timed steps"})
 
 
+def gateup_workload(args, rank, world, dev):
+    """Qwen3-8B MLP gate_up projection with the SiLU x Mul epilogue: A [4096, 4096] @ [gate | up] weight.t()
+    ([4096, 2 x 12288]) -> [4096, 12288], one kernel (nvb200_matmul_silu_and_mul). Column-parallel shards split the
+    intermediate size (each rank its gate and up columns), as MergedColumnParallelLinear does."""
+    from nanovllm_b200.kernels.matmul import matmul_silu_and_mul
+    M, K, inter = 4096, 4096, 12288
+    n_local = inter // world if args.scaling == "strong" else inter
+    g = torch.Generator(device=dev).manual_seed(11)
+    a = (torch.randn(M, K, device=dev, generator=g) / K ** 0.5).to(torch.bfloat16)
+    w = torch.randn(2 * n_local, K, device=dev, generator=g).to(torch.bfloat16)
+    b = w.t()
+    units = 2 * M * 2 * n_local * K
+
+    def launch():
+        matmul_silu_and_mul(a, b)
+
+    xc = {}
+
+    def cpu(tokens=M):
+        if not xc:
+            xc.update(a=a.cpu(), b=b.cpu())
+        gu = xc["a"][:tokens] @ xc["b"]  # torch CPU bf16, then the reference's SiLU x Mul
+        torch.nn.functional.silu(gu[:, :n_local]) * gu[:, n_local:]
+        return 2 * tokens * 2 * n_local * K
+
+    return dict(launch=launch, units=units, e2e=None, cpu=cpu, unit="TFLOP/s", scale=1e12, bound="tensor",
+                metric="gate_up GEMM + SiLU x Mul bf16 TFLOP/s (Qwen3-8B MLP, M=4096)", dtype="bf16",
+                launches_per_step=1, traffic_key="gateup",
+                config={"workload": "gateup", "M": M, "K": K, "intermediate": n_local,
+                        "b_layout": "[gate | up] weight.t() (K-major)", "parallelism": f"column-parallel x{world}",
+                        "l2": "flushed between timed steps"})
+
+
 def make_workload(args, rank, world, dev):
     if args.workload == "fused8b":
         return fused_workload(args, rank, world, dev, 32, 8, 32768, 1024, "fused8b")
@@ -323,21 +358,32 @@ def make_workload(args, rank, world, dev):
         return fused_workload(args, rank, world, dev, 16, 8, 4096, 64, "fused06b")
     if args.workload == "norm":
         return norm_workload(args, rank, world, dev)
+    if args.workload == "gateup":
+        return gateup_workload(args, rank, world, dev)
     return matmul_workload(args, rank, world, dev)
 
 
 # ---------------------------------------------------------------------------------------------------------------
 
-def time_cpu(fn, budget_s=10.0, max_reps=30):
-    """Median seconds of fn() on the host cores after one warm-up, repeated until ~budget_s."""
-    fn()
-    times = []
+def time_cpu(fn, full, budget_s=10.0, max_reps=30):
+    """Host-core timing of fn(rows) (which returns the units it processed): the full step when a run fits in a quarter
+    of budget_s, else a prefix of rows sized to it (estimated from a 1/64 probe run after a first warm-up call).
+    Median over runs after one warm-up,
+    repeated until ~budget_s. Returns (units / second, runs, rows per run)."""
+    probe = max(1, full // 64)
+    fn(probe)  # one-time set-up (host copies of the inputs) outside the estimate
+    t0 = time.perf_counter()
+    fn(probe)
+    est_full = (time.perf_counter() - t0) * full / probe
+    rows = full if est_full <= budget_s / 4 else max(1, int(full * (budget_s / 4) / est_full))
+    fn(rows)
+    times, units = [], 0
     start = time.perf_counter()
     while len(times) < max_reps and (len(times) < 3 or time.perf_counter() - start < budget_s):
         t0 = time.perf_counter()
-        fn()
+        units = fn(rows)
         times.append(time.perf_counter() - t0)
-    return statistics.median(times), len(times)
+    return units / statistics.median(times), len(times), rows
 
 
 def run_reference_arm(args, rank, world):
@@ -568,11 +614,13 @@ def main():
         line["e2e"] = e2e
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         torch.set_num_threads(os.cpu_count() or 1)
+        full = wl["config"].get("tokens_per_step", wl["config"].get("M"))
         with torch.inference_mode():
-            secs, reps = time_cpu(wl["cpu"])
-        line["cpu_baseline"] = {"value": wl["units"] / secs / wl["scale"], "unit": wl["unit"],
+            rate, reps, rows = time_cpu(wl["cpu"], full)
+        what = "the full step" if rows == full else f"the first {rows} of the step's {full} rows/tokens"
+        line["cpu_baseline"] = {"value": rate / wl["scale"], "unit": wl["unit"],
                                 "cores": torch.get_num_threads(), "kind": "port",
-                                "sample": f"the full step on the host (torch CPU bf16 restatement of the reference), "
+                                "sample": f"{what} on the host (torch CPU bf16 restatement of the reference), "
                                           f"median of {reps} runs"}
     if rank == 0:
         print(json.dumps(line), flush=True)
