@@ -10,6 +10,7 @@
 //   fp32 with tf32 = 0 ("ieee"), or any other layout        -> this file's SIMT kernel: exact fp32 FMA for ieee;
 //                                                              for tf32 it rounds the operands to tf32 first
 #include <algorithm>
+#include <cstring>
 
 #include "common.cuh"
 
@@ -18,6 +19,10 @@ namespace nvb200 {
 // Implemented in matmul_tc.cu. Return NVB200_ERR_UNSUPPORTED when the layout is not TMA-readable.
 int matmul_swiglu_launch(void *c, const void *a, const void *b, int64_t M, int64_t N, int64_t K, int64_t sam,
                          int64_t sak, int64_t sbk, int64_t sbn, int64_t scm, int32_t *status, cudaStream_t stream);
+int64_t allreduce_buffer_bytes(int64_t max_n);
+int matmul_allreduce_launch(void *c, const void *a, const void *b, int64_t M, int64_t N, int64_t K, int64_t sam,
+                            int64_t sak, int64_t sbk, int64_t sbn, int64_t scm, const nvb200_allreduce_group *g,
+                            int32_t *status, cudaStream_t stream);
 int matmul_tc_launch(void *c, const void *a, const void *b, int64_t M, int64_t N, int64_t K, int64_t sam,
                      int64_t sak, int64_t sbk, int64_t sbn, int64_t scm, int64_t scn, int dtype, int32_t *status,
                      cudaStream_t stream);
@@ -190,4 +195,51 @@ extern "C" int nvb200_matmul_silu_and_mul(void *c, const void *a, const void *b,
   if (!c || !a || !b) return NVB200_ERR_ARG;
   if (int rc = check_device()) return rc;
   return matmul_swiglu_launch(c, a, b, M, N, K, sam, sak, sbk, sbn, scm, status, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int64_t nvb200_allreduce_buffer_bytes(int64_t max_n) {
+  return max_n > 0 ? allreduce_buffer_bytes(max_n) : 0;
+}
+
+extern "C" int nvb200_allreduce_buffer_create(int64_t max_n, void **buffer, void *ipc_handle) {
+  if (max_n <= 0 || max_n > 0x3fffffffLL || buffer == nullptr || ipc_handle == nullptr) return NVB200_ERR_ARG;
+  if (int rc = check_device()) return rc;
+  const int64_t bytes = allreduce_buffer_bytes(max_n);
+  void *p = nullptr;
+  if (cudaMalloc(&p, static_cast<size_t>(bytes)) != cudaSuccess) return NVB200_ERR_CUDA;
+  cudaIpcMemHandle_t h;
+  if (cudaMemset(p, 0, static_cast<size_t>(bytes)) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess ||
+      cudaIpcGetMemHandle(&h, p) != cudaSuccess) {
+    cudaFree(p);
+    return NVB200_ERR_CUDA;
+  }
+  static_assert(sizeof(h) == 64, "CUDA IPC handles are 64 bytes");
+  memcpy(ipc_handle, &h, sizeof(h));
+  *buffer = p;
+  return NVB200_OK;
+}
+
+extern "C" int nvb200_allreduce_buffer_open(const void *ipc_handle, void **buffer) {
+  if (ipc_handle == nullptr || buffer == nullptr) return NVB200_ERR_ARG;
+  if (int rc = check_device()) return rc;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, ipc_handle, sizeof(h));
+  return cudaIpcOpenMemHandle(buffer, h, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess ? NVB200_OK : NVB200_ERR_CUDA;
+}
+
+extern "C" int nvb200_allreduce_buffer_close(void *buffer, int owned) {
+  if (buffer == nullptr) return NVB200_OK;
+  const cudaError_t e = owned ? cudaFree(buffer) : cudaIpcCloseMemHandle(buffer);
+  return e == cudaSuccess ? NVB200_OK : NVB200_ERR_CUDA;
+}
+
+extern "C" int nvb200_matmul_allreduce(void *out, const void *a, const void *b, int64_t M, int64_t N, int64_t K,
+                                       int64_t sam, int64_t sak, int64_t sbk, int64_t sbn, int64_t scm,
+                                       const nvb200_allreduce_group *group, int32_t *status, nvb200_stream_t stream) {
+  if (M < 0 || N < 0 || K < 0 || group == nullptr) return NVB200_ERR_ARG;
+  if (M == 0 || N == 0) return NVB200_OK;
+  if (!out || !a || !b) return NVB200_ERR_ARG;
+  if (int rc = check_device()) return rc;
+  return matmul_allreduce_launch(out, a, b, M, N, K, sam, sak, sbk, sbn, scm, group, status,
+                                 reinterpret_cast<cudaStream_t>(stream));
 }

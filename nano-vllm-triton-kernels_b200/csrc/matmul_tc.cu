@@ -800,6 +800,8 @@ template <typename Kernel> int configure_once(Kernel kernel, int smem, int slot)
 constexpr int kSkinnyThreads = 128;  // 4 warps: warp 0 lane 0 loads, warp 1 lane 0 issues MMAs, all 4 drain TMEM
 constexpr int kSkinnyMaxStages = 8;
 constexpr int kSkinnyMaxM = 64;
+constexpr int kArMaxRanks = 8;
+constexpr int kArMaxGrid = 256;  // CTAs of a fused all-reduce call at most (all resident)
 #ifndef NVB200_SKINNY_KPB
 #define NVB200_SKINNY_KPB 2
 #endif
@@ -816,10 +818,24 @@ struct SkinnyParams {
   uint32_t idesc;
   int elem_bytes;
   int c_is_f32;
-  int red_off;      // shared-memory offset of the partial slots [S][m_pad][128 / S] fp32 (S > 1)
+  int red_off;      // shared-memory offset of the partial slots [S][m_pad][128 / S] fp32 (S > 1, or all-reduce)
   int hdr_off;      // barriers and the TMEM slot
   int32_t *status;
+  // Row-parallel all-reduce across GPUs (ar_world > 1): every rank's exchange buffer, mapped in this process.
+  int ar_world, ar_rank;
+  uint32_t ar_epoch;
+  int64_t ar_max_n;
+  uint8_t *ar_base[kArMaxRanks];
 };
+
+// Exchange buffer of one rank: two parities of [source rank][kSkinnyMaxM][max_n] 8-byte words, each an fp32
+// partial in the low half and the epoch of the call that wrote it in the high half (written with one 8-byte store,
+// so a reader that sees the epoch sees the value: no fences or separate flags). Calls alternate parities, so a rank
+// that runs ahead never overwrites a word a peer may still be waiting for.
+NVB200_DEVICE uint64_t *ar_slot(const SkinnyParams &p, int owner, int source) {
+  const int64_t parity = p.ar_epoch & 1;
+  return reinterpret_cast<uint64_t *>(p.ar_base[owner]) + ((parity * kArMaxRanks + source) * kSkinnyMaxM) * p.ar_max_n;
+}
 
 NVB200_DEVICE void store_c(const SkinnyParams &p, int m, int n, float v) {
   const int64_t idx = m * p.scm + static_cast<int64_t>(n) * p.scn;
@@ -935,22 +951,28 @@ __global__ void __launch_bounds__(kSkinnyThreads)
   tc_fence_after();
   const int nt = warp * 32 + lane;  // this thread's TMEM lane: row n0 + nt of C^T
   const uint32_t taddr = tmem_base + (static_cast<uint32_t>(warp * 32) << 16);
+  const int rows = BM / S;                          // rows of C^T this CTA finishes (its cluster slice)
+  const int o0 = static_cast<int>(rank) * rows;      // first of them
+  float *part = reinterpret_cast<float *>(smem + p.red_off);  // all-reduce: this CTA's partial, [m][rows]
   if (S == 1) {
     const int n = n0 + nt;
     for (int c0 = 0; c0 < p.m_pad; c0 += 32) {
       float v[32];
       tmem_ld32(taddr + c0, v);
-      if (n < p.N) {
+      if (p.ar_world > 1) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (c0 + i < p.m_pad) part[(c0 + i) * BM + nt] = v[i];
+      } else if (n < p.N) {
 #pragma unroll
         for (int i = 0; i < 32; ++i)
           if (c0 + i < p.M) store_c(p, c0 + i, n, v[i]);
       }
     }
     tc_fence_before();
-    __syncthreads();  // every TMEM read done before the columns are freed
+    __syncthreads();  // every TMEM read done before the columns are freed (and the partial complete)
   } else {
     // Push this CTA's partial of row nt to its owner: slot [rank][m][nt - owner * rows] of the owner's buffer.
-    const int rows = BM / S;
     const int owner = nt / rows;
     const uint32_t dst = map_to_cta(smem_addr(smem + p.red_off), owner) +
                          static_cast<uint32_t>((static_cast<int>(rank) * p.m_pad * rows + (nt - owner * rows)) * 4);
@@ -964,8 +986,9 @@ __global__ void __launch_bounds__(kSkinnyThreads)
     }
     tc_fence_before();
     cluster_sync();  // every partial is in its owner's memory (and every TMEM read done)
-    // Sum the S slots of this CTA's rows, 4 consecutive rows (columns n of C) per step.
-    const float *red = reinterpret_cast<const float *>(smem + p.red_off);
+    // Sum the S slots of this CTA's rows, 4 consecutive rows (columns n of C) per step. With an all-reduce to
+    // follow, the sum goes back into slot 0 (the same thread read it) as this GPU's partial.
+    float *red = reinterpret_cast<float *>(smem + p.red_off);
     const int qpr = rows / 4;
     for (int gi = threadIdx.x; gi < p.M * qpr; gi += kSkinnyThreads) {
       const int m = gi / qpr, q = gi - m * qpr;
@@ -974,10 +997,81 @@ __global__ void __launch_bounds__(kSkinnyThreads)
         const float4 x = *reinterpret_cast<const float4 *>(red + (r * p.m_pad + m) * rows + 4 * q);
         acc[0] += x.x, acc[1] += x.y, acc[2] += x.z, acc[3] += x.w;
       }
-      const int n = n0 + static_cast<int>(rank) * rows + 4 * q;
+      const int n = n0 + o0 + 4 * q;
+      if (p.ar_world > 1) {
+        *reinterpret_cast<float4 *>(red + m * rows + 4 * q) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+      } else {
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
-        if (n + i < p.N) store_c(p, m, n + i, acc[i]);
+        for (int i = 0; i < 4; ++i)
+          if (n + i < p.N) store_c(p, m, n + i, acc[i]);
+      }
+    }
+    if (p.ar_world > 1) __syncthreads();
+  }
+
+  if (p.ar_world > 1) {
+    // ------------------------------------------------------------------ all-reduce over the GPUs (NVLink)
+    // 1. This GPU's partial of the CTA's slice goes to every other rank's exchange buffer, tagged with the epoch.
+    const int W = p.ar_world, me = p.ar_rank;
+    const int qpr = rows / 4;
+    const uint64_t tag = static_cast<uint64_t>(p.ar_epoch) << 32;
+    for (int dst_rank = 0; dst_rank < W; ++dst_rank) {
+      if (dst_rank == me) continue;
+      uint64_t *slot = ar_slot(p, dst_rank, me);
+      for (int gi = threadIdx.x; gi < p.M * qpr; gi += kSkinnyThreads) {
+        const int m = gi / qpr, q = gi - m * qpr;
+        const int n = n0 + o0 + 4 * q;
+        if (n >= p.N) continue;
+        const float4 v = *reinterpret_cast<const float4 *>(part + m * rows + 4 * q);
+        uint64_t *dst = slot + m * p.ar_max_n + n;
+        asm volatile("st.relaxed.sys.global.v2.u64 [%0], {%1, %2};" ::"l"(dst), "l"(tag | __float_as_uint(v.x)),
+                     "l"(tag | __float_as_uint(v.y))
+                     : "memory");
+        asm volatile("st.relaxed.sys.global.v2.u64 [%0], {%1, %2};" ::"l"(dst + 2), "l"(tag | __float_as_uint(v.z)),
+                     "l"(tag | __float_as_uint(v.w))
+                     : "memory");
+      }
+    }
+    // 2. Sum the W partials in rank order (the same order, hence the same bits, on every GPU): this GPU's from shared
+    // memory, the others' from its exchange buffer once their words carry this call's epoch (bounded wait: after
+    // 1 s without a peer the status bit is set and the thread stops waiting).
+    bool expired = false;
+    uint64_t start = 0;
+    for (int gi = threadIdx.x; gi < p.M * qpr; gi += kSkinnyThreads) {
+      const int m = gi / qpr, q = gi - m * qpr;
+      const int n = n0 + o0 + 4 * q;
+      if (n >= p.N) continue;
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int src = 0; src < W; ++src) {
+        float x[4];
+        if (src == me) {
+          const float4 v = *reinterpret_cast<const float4 *>(part + m * rows + 4 * q);
+          x[0] = v.x, x[1] = v.y, x[2] = v.z, x[3] = v.w;
+        } else {
+          const uint64_t *w = ar_slot(p, me, src) + m * p.ar_max_n + n;
+          uint64_t a0, a1, a2, a3;
+          for (uint32_t spin = 1;; ++spin) {
+            asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(a0), "=l"(a1) : "l"(w) : "memory");
+            asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(a2), "=l"(a3) : "l"(w + 2) : "memory");
+            if (((a0 & a1 & a2 & a3) >> 32) == p.ar_epoch && ((a0 | a1 | a2 | a3) >> 32) == p.ar_epoch) break;
+            if (expired) break;
+            if ((spin & 1023u) == 0) {
+              const uint64_t now = global_timer_ns();
+              if (start == 0) start = now;
+              else if (now - start > kWaitLimitNs) {
+                set_status(p.status, NVB200_STATUS_WAIT_TIMEOUT);
+                expired = true;
+              }
+            }
+          }
+          x[0] = __uint_as_float(static_cast<uint32_t>(a0)), x[1] = __uint_as_float(static_cast<uint32_t>(a1));
+          x[2] = __uint_as_float(static_cast<uint32_t>(a2)), x[3] = __uint_as_float(static_cast<uint32_t>(a3));
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[i] += x[i];
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) store_c(p, m, n + i, acc[i]);
     }
   }
   if (warp == 1) {
@@ -989,7 +1083,8 @@ __global__ void __launch_bounds__(kSkinnyThreads)
 // Launches the skinny kernel for M <= kSkinnyMaxM with K-major A and B (A row-major, B = weight.t()); returns
 // NVB200_ERR_UNSUPPORTED otherwise.
 int launch_skinny(void *c, const void *a, const void *b, int64_t M, int64_t N, int64_t K, int64_t sam, int64_t sbn,
-                  int64_t scm, int64_t scn, bool f32, int32_t *status, cudaStream_t stream) {
+                  int64_t scm, int64_t scn, bool f32, int32_t *status, cudaStream_t stream,
+                  const nvb200_allreduce_group *ar = nullptr) {
   if (M > kSkinnyMaxM || M <= 0) return NVB200_ERR_UNSUPPORTED;
   const int es = f32 ? 4 : 2;
   const int BK = 128 / es;
@@ -1004,6 +1099,17 @@ int launch_skinny(void *c, const void *a, const void *b, int64_t M, int64_t N, i
   int split = 1;
   while (split < 8 && static_cast<int64_t>(tiles) * split * 2 <= sms && split * 2 <= p.k_blocks) split *= 2;
   p.split = split;
+  if (ar != nullptr) {
+    // Every CTA waits for its peers' CTAs of the same slice, so all of them must be resident at once.
+    if (ar->world < 2 || ar->world > kArMaxRanks || ar->rank < 0 || ar->rank >= ar->world || N % 4 != 0 ||
+        N > ar->max_n || static_cast<int64_t>(tiles) * split > std::min(sms, kArMaxGrid))
+      return NVB200_ERR_UNSUPPORTED;
+    p.ar_world = ar->world, p.ar_rank = ar->rank, p.ar_epoch = ar->epoch, p.ar_max_n = ar->max_n;
+    for (int r = 0; r < ar->world; ++r) {
+      if (ar->buffers[r] == nullptr) return NVB200_ERR_ARG;
+      p.ar_base[r] = static_cast<uint8_t *>(ar->buffers[r]);
+    }
+  }
   CUtensorMap map_w, map_x;
   if (!make_map(&map_w, b, f32, K, N, sbn, BK, BM) || !make_map(&map_x, a, f32, K, M, sam, BK, p.m_pad))
     return NVB200_ERR_UNSUPPORTED;
@@ -1020,7 +1126,7 @@ int launch_skinny(void *c, const void *a, const void *b, int64_t M, int64_t N, i
   const int ring_budget = split > 1 ? 160 * 1024 : 72 * 1024;
   p.stages = std::max(1, std::min({kSkinnyMaxStages, (blocks_per_cta + p.kpb - 1) / p.kpb, ring_budget / stage_bytes}));
   p.red_off = p.stages * stage_bytes;
-  p.hdr_off = p.red_off + (split > 1 ? p.m_pad * BM * 4 : 0);
+  p.hdr_off = p.red_off + (split > 1 || p.ar_world > 1 ? p.m_pad * BM * 4 : 0);
   const int smem = 1024 + p.hdr_off + 256;
   const int rc = f32 ? configure_once(matmul_skinny_kernel<true>, smem, 2) : configure_once(matmul_skinny_kernel<false>, smem, 3);
   if (rc) return rc;
@@ -1179,6 +1285,19 @@ int matmul_tc_launch(void *c, const void *a, const void *b, int64_t M, int64_t N
 int matmul_swiglu_launch(void *c, const void *a, const void *b, int64_t M, int64_t N, int64_t K, int64_t sam,
                          int64_t sak, int64_t sbk, int64_t sbn, int64_t scm, int32_t *status, cudaStream_t stream) {
   return tc_launch(c, a, b, M, N, K, sam, sak, sbk, sbn, scm, 1, NVB200_BF16, true, status, stream);
+}
+
+int64_t allreduce_buffer_bytes(int64_t max_n) {
+  return 2LL * kArMaxRanks * kSkinnyMaxM * max_n * 8;
+}
+
+int matmul_allreduce_launch(void *c, const void *a, const void *b, int64_t M, int64_t N, int64_t K, int64_t sam,
+                            int64_t sak, int64_t sbk, int64_t sbn, int64_t scm, const nvb200_allreduce_group *g,
+                            int32_t *status, cudaStream_t stream) {
+  if (K <= 0 || M > kSkinnyMaxM || N > 0x3fffffffLL || K > 0x7fffffffLL) return NVB200_ERR_UNSUPPORTED;
+  if (sak != 1 || sbk != 1 || (sam * 2) % 16 != 0 || (sbn * 2) % 16 != 0 || !aligned16(a) || !aligned16(b))
+    return NVB200_ERR_UNSUPPORTED;
+  return launch_skinny(c, a, b, M, N, K, sam, sbn, scm, 1, false, status, stream, g);
 }
 
 }  // namespace nvb200

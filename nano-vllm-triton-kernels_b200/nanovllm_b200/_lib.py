@@ -21,7 +21,9 @@ STATUS_BAD_POSITION, STATUS_BAD_SLOT, STATUS_WAIT_TIMEOUT = 1, 2, 4
 
 # Every extern "C" function of include/nvb200.h; tests check that the library exports each one.
 EXPORTS = ("nvb200_status_string", "nvb200_qk_norm_rope_kv", "nvb200_rms_norm", "nvb200_fused_add_rms_norm",
-           "nvb200_silu_and_mul", "nvb200_matmul_workspace_size", "nvb200_matmul", "nvb200_matmul_silu_and_mul")
+           "nvb200_silu_and_mul", "nvb200_matmul_workspace_size", "nvb200_matmul", "nvb200_matmul_silu_and_mul",
+           "nvb200_allreduce_buffer_bytes", "nvb200_allreduce_buffer_create", "nvb200_allreduce_buffer_open",
+           "nvb200_allreduce_buffer_close", "nvb200_matmul_allreduce")
 
 _vp, _i64, _i32, _f32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32, ctypes.c_float
 
@@ -37,6 +39,12 @@ class QkNormRopeKvArgs(ctypes.Structure):
         ("num_tokens", _i64), ("num_q_heads", _i32), ("num_kv_heads", _i32), ("head_dim", _i32),
         ("eps", _f32), ("status", _vp),
     ]
+
+
+class AllreduceGroup(ctypes.Structure):
+    """nvb200_allreduce_group (field order and types as in nvb200.h)."""
+    _fields_ = [("world", ctypes.c_int), ("rank", ctypes.c_int), ("epoch", ctypes.c_uint32), ("max_n", _i64),
+                ("buffers", _vp * 8)]
 
 
 class KernelError(RuntimeError):
@@ -65,6 +73,16 @@ def _declare(lib):
     lib.nvb200_matmul.restype = ctypes.c_int
     lib.nvb200_matmul_silu_and_mul.argtypes = [_vp, _vp, _vp] + [_i64] * 8 + [_vp, _vp]
     lib.nvb200_matmul_silu_and_mul.restype = ctypes.c_int
+    lib.nvb200_allreduce_buffer_bytes.argtypes = [_i64]
+    lib.nvb200_allreduce_buffer_bytes.restype = _i64
+    lib.nvb200_allreduce_buffer_create.argtypes = [_i64, ctypes.POINTER(_vp), _vp]
+    lib.nvb200_allreduce_buffer_create.restype = ctypes.c_int
+    lib.nvb200_allreduce_buffer_open.argtypes = [_vp, ctypes.POINTER(_vp)]
+    lib.nvb200_allreduce_buffer_open.restype = ctypes.c_int
+    lib.nvb200_allreduce_buffer_close.argtypes = [_vp, ctypes.c_int]
+    lib.nvb200_allreduce_buffer_close.restype = ctypes.c_int
+    lib.nvb200_matmul_allreduce.argtypes = [_vp, _vp, _vp] + [_i64] * 8 + [ctypes.POINTER(AllreduceGroup), _vp, _vp]
+    lib.nvb200_matmul_allreduce.restype = ctypes.c_int
 
 
 def lib():

@@ -9,6 +9,8 @@
   products (nanovllm/layers/linear.py:131-156): the one exchange on this path, done with
   torch.distributed.all_reduce (NCCL over NVLink on B200; gloo on CPU in the tests).
 """
+import ctypes
+
 import torch
 import torch.distributed as dist
 
@@ -76,3 +78,83 @@ def row_parallel_matmul(a_shard: torch.Tensor, b_shard: torch.Tensor, matmul=Non
     if dist.is_initialized() and dist.get_world_size(group) > 1:
         dist.all_reduce(c, group=group)
     return c
+
+
+class RowParallelAllReduce:
+    """Row-parallel matmul fused with its all-reduce over NVLink (nvb200_matmul_allreduce): every rank calls it with
+    its K shard A_r [M, K_r], B_r [K_r, N] and receives sum_r A_r @ B_r (bf16, summed in fp32 in rank order, so all
+    ranks hold the same bits), in one kernel per rank that pushes its partial into every rank's exchange buffer and
+    waits for theirs. Replaces F.linear followed by dist.all_reduce (nanovllm/layers/linear.py:131-156) for
+    decode-sized batches (M <= 64); other shapes, and groups of one rank, run the matmul and an NCCL all-reduce.
+
+    Construction is collective over `group` (the exchange buffers' CUDA IPC handles are all-gathered), and so is
+    every call: all ranks make the same calls in the same order. Buffers live until close()."""
+
+    def __init__(self, max_n: int, group=None, device=None):
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        self.max_n = int(max_n)
+        self.epoch = 0
+        self.own = None
+        self.peers = []
+        if self.world < 2:
+            return
+        if self.world > 8:
+            raise ValueError("at most 8 ranks")
+        from nanovllm_b200 import _lib
+        lib = _lib.lib()
+        with torch.cuda.device(self.device):
+            buf, handle = ctypes.c_void_p(), (ctypes.c_char * 64)()
+            _lib.check(lib.nvb200_allreduce_buffer_create(self.max_n, ctypes.byref(buf), handle), "allreduce buffer")
+            self.own = buf.value
+            handles = [None] * self.world
+            dist.all_gather_object(handles, bytes(handle), group=group)
+            self.group_args = _lib.AllreduceGroup(world=self.world, rank=self.rank, epoch=0, max_n=self.max_n)
+            for r, h in enumerate(handles):
+                if r == self.rank:
+                    self.group_args.buffers[r] = self.own
+                    continue
+                peer = ctypes.c_void_p()
+                _lib.check(lib.nvb200_allreduce_buffer_open((ctypes.c_char * 64).from_buffer_copy(h),
+                                                            ctypes.byref(peer)), "allreduce buffer open")
+                self.peers.append(peer.value)
+                self.group_args.buffers[r] = peer.value
+
+    def __call__(self, a_shard: torch.Tensor, b_shard: torch.Tensor) -> torch.Tensor:
+        from nanovllm_b200 import _lib
+        from nanovllm_b200.kernels.matmul import matmul
+        if self.world < 2:
+            return matmul(a_shard, b_shard)
+        if not (a_shard.ndim == 2 and b_shard.ndim == 2 and a_shard.shape[1] == b_shard.shape[0]):
+            raise AssertionError((a_shard.shape, b_shard.shape))
+        M, K = a_shard.shape
+        N = b_shard.shape[1]
+        out = torch.empty((M, N), device=a_shard.device, dtype=a_shard.dtype)
+        if a_shard.dtype == b_shard.dtype == torch.bfloat16 and M and N and K:
+            self.epoch += 1
+            self.group_args.epoch = self.epoch
+            rc = _lib.lib().nvb200_matmul_allreduce(
+                out.data_ptr(), a_shard.data_ptr(), b_shard.data_ptr(), M, N, K, a_shard.stride(0), a_shard.stride(1),
+                b_shard.stride(0), b_shard.stride(1), out.stride(0), ctypes.byref(self.group_args),
+                _lib.status_word(a_shard.device).data_ptr(), _lib.stream_of(a_shard))
+            if rc != _lib.ERR_UNSUPPORTED:
+                _lib.check(rc, "matmul_allreduce")
+                return out
+            self.epoch -= 1  # nothing was launched: the epoch is not used (every rank takes the same branch)
+        c = matmul(a_shard, b_shard)
+        dist.all_reduce(c, group=self.group)
+        return c
+
+    def close(self) -> None:
+        """Unmaps the peers' buffers and frees this rank's (after a device synchronisation)."""
+        if self.own is None:
+            return
+        from nanovllm_b200 import _lib
+        torch.cuda.synchronize(self.device)
+        lib = _lib.lib()
+        for p in self.peers:
+            lib.nvb200_allreduce_buffer_close(p, 0)
+        lib.nvb200_allreduce_buffer_close(self.own, 1)
+        self.own, self.peers = None, []

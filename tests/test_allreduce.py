@@ -1,0 +1,72 @@
+"""Row-parallel matmul fused with its all-reduce over NVLink (nvb200_matmul_allreduce via
+nanovllm_b200.parallel.RowParallelAllReduce) on two GPUs, one process each (NCCL group for the set-up): against
+the fp64 product of the full operands within bf16 tolerance, against the reference's path (matmul, then an NCCL
+all-reduce of the bf16 partials), and identical on both ranks; three calls per shape so both halves of the
+exchange buffers and increasing epochs are used. Needs two GPUs (skipped otherwise)."""
+import math
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+WORLD = 2
+# (M, N, K total): decode o_proj / down_proj of Qwen3-0.6B and -8B shards, M = 1 and odd M, ragged K shards.
+SHAPES = [(32, 1024, 2048), (32, 1024, 6144), (1, 4096, 1024), (7, 1000, 512), (64, 2048, 1024), (32, 4096, 24576)]
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, port, out_dir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=WORLD, device_id=torch.device("cuda", rank))
+    from nanovllm_b200 import _lib
+    from nanovllm_b200.kernels.matmul import matmul
+    from nanovllm_b200.parallel import RowParallelAllReduce
+    results = []
+    ar = RowParallelAllReduce(max_n=4096)
+    try:
+        for (M, N, K) in SHAPES:
+            g = torch.Generator(device="cuda").manual_seed(M * 31 + N + K)
+            a = (torch.randn(M, K, device="cuda", generator=g) / math.sqrt(K)).to(torch.bfloat16)
+            w = torch.randn(N, K, device="cuda", generator=g).to(torch.bfloat16)
+            k0, k1 = rank * K // WORLD, (rank + 1) * K // WORLD
+            a_r, b_r = a[:, k0:k1].contiguous(), w[:, k0:k1].t()
+            for it in range(3):
+                out = ar(a_r, b_r)
+                ref_nccl = matmul(a_r, b_r)
+                dist.all_reduce(ref_nccl)
+                gathered = [torch.empty_like(out) for _ in range(WORLD)]
+                dist.all_gather(gathered, out)
+                results.append(dict(shape=(M, N, K), it=it, out=out.cpu(), nccl=ref_nccl.cpu(),
+                                    same=all(torch.equal(gathered[0], x) for x in gathered),
+                                    ref=(a.double() @ w.double().t()).cpu(), status=_lib.status(clear=True)))
+        torch.cuda.synchronize()
+    finally:
+        ar.close()
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        torch.save(results, os.path.join(out_dir, "out.pt"))
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < WORLD, reason="needs two GPUs")
+def test_row_parallel_allreduce(tmp_path):
+    mp.start_processes(_worker, args=(_free_port(), str(tmp_path)), nprocs=WORLD, start_method="spawn")
+    results = torch.load(tmp_path / "out.pt")
+    assert len(results) == 3 * len(SHAPES)
+    for r in results:
+        assert r["status"] == 0, r["shape"]
+        assert r["same"], r["shape"]  # every rank holds the same bits
+        scale = r["ref"].abs().max().item()
+        torch.testing.assert_close(r["out"].double(), r["ref"], rtol=1.6e-2, atol=1e-2 * scale)
+        torch.testing.assert_close(r["out"].double(), r["nccl"].double(), rtol=1.6e-2, atol=1e-2 * scale)
