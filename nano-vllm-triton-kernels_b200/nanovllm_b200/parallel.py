@@ -6,8 +6,9 @@
   positions, slot_mapping and the cos/sin table are replicated.
 * Column-parallel matmul (qkv_proj, gate_up_proj) N-shards B: no collective.
 * Row-parallel matmul (o_proj, down_proj) K-shards A's columns and B's rows and all-reduces the [M, N] partial
-  products (nanovllm/layers/linear.py:131-156): the one exchange on this path, done with
-  torch.distributed.all_reduce (NCCL over NVLink on B200; gloo on CPU in the tests).
+  products (nanovllm/layers/linear.py:131-156): the one exchange on this path. row_parallel_matmul does it with
+  torch.distributed.all_reduce (NCCL over NVLink; gloo on CPU in the tests); RowParallelAllReduce does the GEMM and
+  the exchange in one kernel per rank over NVLink for decode-sized batches.
 """
 import ctypes
 
