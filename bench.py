@@ -19,7 +19,8 @@ it, tests/test_oracle.py), run on the host cores in bf16.
 
 Other workloads (not the driver's headline): fused06b (config 1 shape at T = 8192), norm (config 2: rms_norm,
 add_rms_norm, silu_and_mul at T = 8192), matmul (config 4, bf16 M = K = N = 4096), gateup (the gate_up GEMM with
-the SiLU x Mul epilogue at the Qwen3-8B MLP shape, M = 4096), decode (config 5: the reference's decode step per
+the SiLU x Mul epilogue at the Qwen3-8B MLP shape, M = 4096), rowpar (decode-sized row-parallel GEMM fused with
+its NVLink all-reduce, Qwen3-8B down_proj split over the ranks), decode (config 5: the reference's decode step per
 backend).
 """
 import argparse
@@ -48,7 +49,7 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", default="fused8b", choices=["fused8b", "fused06b", "norm", "matmul", "gateup", "decode"])
+    ap.add_argument("--workload", default="fused8b", choices=["fused8b", "fused06b", "norm", "matmul", "gateup", "rowpar", "decode"])
     ap.add_argument("--decode-worker", default=None, help=argparse.SUPPRESS)
     ap.add_argument("--decode-backends", default="b200,compile,triton_fused")
     ap.add_argument("--decode-batch", type=int, default=32)
@@ -351,6 +352,43 @@ def gateup_workload(args, rank, world, dev):
                         "l2": "flushed between timed steps"})
 
 
+def rowpar_workload(args, rank, world, dev):
+    """Decode-step row-parallel projection with its all-reduce: Qwen3-8B down_proj (K = 12288 split over the ranks,
+    N = 4096) for a batch of 32 tokens, one fused GEMM + NVLink all-reduce per rank (RowParallelAllReduce; one GPU:
+    the plain GEMM). Strong scaling: the layer is fixed, each rank holds K / N of it."""
+    from nanovllm_b200.parallel import RowParallelAllReduce
+    M, N, K = 32, 4096, 12288
+    k_local = K // world
+    g = torch.Generator(device=dev).manual_seed(13 + rank)
+    a = (torch.randn(M, k_local, device=dev, generator=g) / K ** 0.5).to(torch.bfloat16)
+    w = torch.randn(N, k_local, device=dev, generator=g).to(torch.bfloat16)
+    b = w.t()
+    if world > 1:
+        op = RowParallelAllReduce(max_n=N)  # collective set-up: every rank builds it
+    else:
+        from nanovllm_b200.kernels.matmul import matmul
+        op = matmul
+
+    def launch():
+        op(a, b)
+
+    xc = {}
+
+    def cpu(tokens=M):
+        if not xc:
+            xc.update(a=a.cpu(), b=b.cpu())
+        xc["a"][:tokens] @ xc["b"]  # this rank's partial on the host; the exchange is not timed on the CPU
+        return 2 * tokens * N * k_local
+
+    return dict(launch=launch, units=2 * M * N * k_local, e2e=None, cpu=cpu, unit="TFLOP/s", scale=1e12,
+                bound="tensor", scaling="strong",
+                metric="row-parallel down_proj GEMM + all-reduce bf16 TFLOP/s (Qwen3-8B, 32 tokens)", dtype="bf16",
+                launches_per_step=1, traffic_key="rowpar",
+                config={"workload": "rowpar", "M": M, "N": N, "K": K, "K_per_rank": k_local,
+                        "parallelism": f"row-parallel x{world}, fused NVLink all-reduce",
+                        "l2": "flushed between timed steps"})
+
+
 def make_workload(args, rank, world, dev):
     if args.workload == "fused8b":
         return fused_workload(args, rank, world, dev, 32, 8, 32768, 1024, "fused8b")
@@ -360,6 +398,8 @@ def make_workload(args, rank, world, dev):
         return norm_workload(args, rank, world, dev)
     if args.workload == "gateup":
         return gateup_workload(args, rank, world, dev)
+    if args.workload == "rowpar":
+        return rowpar_workload(args, rank, world, dev)
     return matmul_workload(args, rank, world, dev)
 
 
@@ -415,7 +455,7 @@ def run_reference_arm(args, rank, world):
               f"torch CPU bf16 eager restatement of the reference")
     line = {"metric": wl["metric"], "value": value, "unit": wl["unit"], "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": 1e3 * total / args.steps, "higher_is_better": True,
-            "scaling": args.scaling, "vs_baseline": None, "dtype": wl["dtype"], "data": "synthetic",
+            "scaling": wl.get("scaling", args.scaling), "vs_baseline": None, "dtype": wl["dtype"], "data": "synthetic",
             "config": wl["config"], "impl": "reference",
             "cpu_baseline": {"value": value, "unit": wl["unit"], "cores": torch.get_num_threads(), "kind": "port",
                              "sample": sample},
@@ -602,7 +642,7 @@ def main():
     traffic = load_traffic(wl["traffic_key"])
     line = {"metric": wl["metric"], "value": value, "unit": wl["unit"], "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": 1e3 * total_s / args.steps, "higher_is_better": True,
-            "scaling": args.scaling, "vs_baseline": None, "dtype": wl["dtype"],
+            "scaling": wl.get("scaling", args.scaling), "vs_baseline": None, "dtype": wl["dtype"],
             "data": "synthetic (seeded, BASELINE config shapes and distributions)", "config": wl["config"],
             "roofline": {"bound": wl["bound"], "achieved": achieved, "peak": peak, "unit": roof_unit,
                          "frac": achieved / peak, "peak_source": f"{peak_kind} (MEASURED_PEAKS.json)"
