@@ -143,23 +143,22 @@ NVB200_API int nvb200_matmul_silu_and_mul(void *out, const void *a, const void *
 /* Row-parallel GEMM fused with its all-reduce over NVLink (decode-sized rows), for tensor parallelism: rank r
  * holds A_r [M, K_r] and B_r [K_r, N] (its K shard); every rank receives out[M, N] = sum over ranks of A_r @ B_r in
  * bf16, summed in fp32 in rank order (so every rank gets the same bits). One kernel per rank computes its partial
- * with the tensor cores, pushes it into every rank's exchange buffer over NVLink, raises per-slice flags there
- * (system-scope release stores of the call's epoch) and, after a bounded wait for all ranks' flags, sums.
+ * with the tensor cores, pushes it into every rank's exchange buffer over NVLink and sums the ranks' partials in
+ * rank order as they arrive (each partial travels as 8-byte words tagged with the call's epoch: no flags or fences).
  * Replaces: nanovllm/layers/linear.py:131-156 (RowParallelLinear.forward: F.linear, then dist.all_reduce).
  * Exchange buffers: one per rank, nvb200_allreduce_buffer_bytes(max_n) bytes, created by
  * nvb200_allreduce_buffer_create (cudaMalloc'd and zeroed: a set-up call, not a per-step one) and shared through
  * its CUDA IPC handle (64 bytes); each rank opens its peers' handles with nvb200_allreduce_buffer_open. The group
- * lists every rank's buffer as mapped in the calling process (buffers[rank] = its own). epoch: 1, 2, 3, ... per
- * call, the same on every rank, never repeating for one set of buffers (calls alternate halves of the buffers by
- * its parity). All ranks must make the same sequence of calls with the same shapes; the kernels of one call must
- * run concurrently on all ranks (one process per GPU).
+ * lists every rank's buffer as mapped in the calling process (buffers[rank] = its own). The call number (epoch) is
+ * kept in each rank's buffer and advanced by the kernel, so calls may be captured in a CUDA graph and replayed.
+ * All ranks must make the same sequence of calls with the same shapes on one set of buffers; the kernels of one
+ * call must run concurrently on all ranks (one process per GPU).
  * Takes bf16, M <= 64, N a multiple of 4 and <= max_n, A row-major and B K-major (an nn.Linear weight.t()), and a
  * grid that fits on the GPU at once; returns NVB200_ERR_UNSUPPORTED otherwise (the caller then runs a GEMM and an
  * all-reduce). A peer that does not arrive within 1 s sets NVB200_STATUS_WAIT_TIMEOUT in *status. */
 typedef struct {
   int world;            /* ranks, 2..8 */
   int rank;             /* this rank */
-  uint32_t epoch;       /* call number, from 1 */
   int64_t max_n;        /* the max_n the buffers were created with */
   void *buffers[8];     /* every rank's exchange buffer, as mapped in this process */
 } nvb200_allreduce_group;

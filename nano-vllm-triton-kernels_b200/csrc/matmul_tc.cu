@@ -823,18 +823,29 @@ struct SkinnyParams {
   int32_t *status;
   // Row-parallel all-reduce across GPUs (ar_world > 1): every rank's exchange buffer, mapped in this process.
   int ar_world, ar_rank;
-  uint32_t ar_epoch;
   int64_t ar_max_n;
   uint8_t *ar_base[kArMaxRanks];
 };
 
-// Exchange buffer of one rank: two parities of [source rank][kSkinnyMaxM][max_n] 8-byte words, each an fp32
-// partial in the low half and the epoch of the call that wrote it in the high half (written with one 8-byte store,
-// so a reader that sees the epoch sees the value: no fences or separate flags). Calls alternate parities, so a rank
-// that runs ahead never overwrites a word a peer may still be waiting for.
-NVB200_DEVICE uint64_t *ar_slot(const SkinnyParams &p, int owner, int source) {
-  const int64_t parity = p.ar_epoch & 1;
-  return reinterpret_cast<uint64_t *>(p.ar_base[owner]) + ((parity * kArMaxRanks + source) * kSkinnyMaxM) * p.ar_max_n;
+// Exchange buffer of one rank: a 256-byte header (the number of calls completed on this rank, and the count of
+// CTAs of the current call that are done), then two parities of [source rank][kSkinnyMaxM][max_n] 8-byte words,
+// each an fp32 partial in the low half and the epoch (call number) of the call that wrote it in the high half
+// (written with one 8-byte store, so a reader that sees the epoch sees the value: no fences or separate flags).
+// Calls alternate parities, so a rank that runs ahead never overwrites a word a peer may still be waiting for.
+// The epoch lives in device memory and the kernel advances it, so a call captured in a CUDA graph gets a new epoch
+// on every replay; every rank makes the same calls, so the counters of all ranks advance together.
+constexpr int kArHeaderBytes = 256;
+struct ArHeader {
+  uint32_t completed;  // calls completed on this rank: this call's epoch is completed + 1
+  uint32_t arrived;    // CTAs of the current call that are done
+};
+NVB200_DEVICE ArHeader *ar_header(const SkinnyParams &p, int owner) {
+  return reinterpret_cast<ArHeader *>(p.ar_base[owner]);
+}
+NVB200_DEVICE uint64_t *ar_slot(const SkinnyParams &p, uint32_t epoch, int owner, int source) {
+  const int64_t parity = epoch & 1;
+  return reinterpret_cast<uint64_t *>(p.ar_base[owner] + kArHeaderBytes) +
+         ((parity * kArMaxRanks + source) * kSkinnyMaxM) * p.ar_max_n;
 }
 
 NVB200_DEVICE void store_c(const SkinnyParams &p, int m, int n, float v) {
@@ -1014,10 +1025,15 @@ __global__ void __launch_bounds__(kSkinnyThreads)
     // 1. This GPU's partial of the CTA's slice goes to every other rank's exchange buffer, tagged with the epoch.
     const int W = p.ar_world, me = p.ar_rank;
     const int qpr = rows / 4;
-    const uint64_t tag = static_cast<uint64_t>(p.ar_epoch) << 32;
+    // This call's epoch. The header's count only advances once every CTA of the call is done (below), and every CTA
+    // reads it before it is done, so all CTAs read the same value.
+    uint32_t epoch;
+    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(epoch) : "l"(&ar_header(p, me)->completed) : "memory");
+    epoch += 1;
+    const uint64_t tag = static_cast<uint64_t>(epoch) << 32;
     for (int dst_rank = 0; dst_rank < W; ++dst_rank) {
       if (dst_rank == me) continue;
-      uint64_t *slot = ar_slot(p, dst_rank, me);
+      uint64_t *slot = ar_slot(p, epoch, dst_rank, me);
       for (int gi = threadIdx.x; gi < p.M * qpr; gi += kSkinnyThreads) {
         const int m = gi / qpr, q = gi - m * qpr;
         const int n = n0 + o0 + 4 * q;
@@ -1048,12 +1064,12 @@ __global__ void __launch_bounds__(kSkinnyThreads)
           const float4 v = *reinterpret_cast<const float4 *>(part + m * rows + 4 * q);
           x[0] = v.x, x[1] = v.y, x[2] = v.z, x[3] = v.w;
         } else {
-          const uint64_t *w = ar_slot(p, me, src) + m * p.ar_max_n + n;
+          const uint64_t *w = ar_slot(p, epoch, me, src) + m * p.ar_max_n + n;
           uint64_t a0, a1, a2, a3;
           for (uint32_t spin = 1;; ++spin) {
             asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(a0), "=l"(a1) : "l"(w) : "memory");
             asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(a2), "=l"(a3) : "l"(w + 2) : "memory");
-            if (((a0 & a1 & a2 & a3) >> 32) == p.ar_epoch && ((a0 | a1 | a2 | a3) >> 32) == p.ar_epoch) break;
+            if (((a0 & a1 & a2 & a3) >> 32) == epoch && ((a0 | a1 | a2 | a3) >> 32) == epoch) break;
             if (expired) break;
             if ((spin & 1023u) == 0) {
               const uint64_t now = global_timer_ns();
@@ -1072,6 +1088,16 @@ __global__ void __launch_bounds__(kSkinnyThreads)
       }
 #pragma unroll
       for (int i = 0; i < 4; ++i) store_c(p, m, n + i, acc[i]);
+    }
+    // 3. The last CTA of the call to finish advances this rank's epoch (and resets the count for the next call).
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      ArHeader *h = ar_header(p, me);
+      if (atomicAdd(&h->arrived, 1u) == gridDim.x - 1) {
+        h->arrived = 0;
+        __threadfence();
+        h->completed = epoch;
+      }
     }
   }
   if (warp == 1) {
@@ -1104,7 +1130,7 @@ int launch_skinny(void *c, const void *a, const void *b, int64_t M, int64_t N, i
     if (ar->world < 2 || ar->world > kArMaxRanks || ar->rank < 0 || ar->rank >= ar->world || N % 4 != 0 ||
         N > ar->max_n || static_cast<int64_t>(tiles) * split > std::min(sms, kArMaxGrid))
       return NVB200_ERR_UNSUPPORTED;
-    p.ar_world = ar->world, p.ar_rank = ar->rank, p.ar_epoch = ar->epoch, p.ar_max_n = ar->max_n;
+    p.ar_world = ar->world, p.ar_rank = ar->rank, p.ar_max_n = ar->max_n;
     for (int r = 0; r < ar->world; ++r) {
       if (ar->buffers[r] == nullptr) return NVB200_ERR_ARG;
       p.ar_base[r] = static_cast<uint8_t *>(ar->buffers[r]);
@@ -1288,7 +1314,7 @@ int matmul_swiglu_launch(void *c, const void *a, const void *b, int64_t M, int64
 }
 
 int64_t allreduce_buffer_bytes(int64_t max_n) {
-  return 2LL * kArMaxRanks * kSkinnyMaxM * max_n * 8;
+  return kArHeaderBytes + 2LL * kArMaxRanks * kSkinnyMaxM * max_n * 8;
 }
 
 int matmul_allreduce_launch(void *c, const void *a, const void *b, int64_t M, int64_t N, int64_t K, int64_t sam,

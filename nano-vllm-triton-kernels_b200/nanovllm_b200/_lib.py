@@ -43,8 +43,7 @@ class QkNormRopeKvArgs(ctypes.Structure):
 
 class AllreduceGroup(ctypes.Structure):
     """nvb200_allreduce_group (field order and types as in nvb200.h)."""
-    _fields_ = [("world", ctypes.c_int), ("rank", ctypes.c_int), ("epoch", ctypes.c_uint32), ("max_n", _i64),
-                ("buffers", _vp * 8)]
+    _fields_ = [("world", ctypes.c_int), ("rank", ctypes.c_int), ("max_n", _i64), ("buffers", _vp * 8)]
 
 
 class KernelError(RuntimeError):

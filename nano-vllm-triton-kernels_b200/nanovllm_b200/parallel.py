@@ -89,7 +89,8 @@ class RowParallelAllReduce:
     decode-sized batches (M <= 64); other shapes, and groups of one rank, run the matmul and an NCCL all-reduce.
 
     Construction is collective over `group` (the exchange buffers' CUDA IPC handles are all-gathered), and so is
-    every call: all ranks make the same calls in the same order. Buffers live until close()."""
+    every call: all ranks make the same calls in the same order. The kernel keeps its call count in the buffers,
+    so calls may be captured in a CUDA graph and replayed. Buffers live until close()."""
 
     def __init__(self, max_n: int, group=None, device=None):
         self.group = group
@@ -97,7 +98,6 @@ class RowParallelAllReduce:
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
         self.max_n = int(max_n)
-        self.epoch = 0
         self.own = None
         self.peers = []
         if self.world < 2:
@@ -112,7 +112,7 @@ class RowParallelAllReduce:
             self.own = buf.value
             handles = [None] * self.world
             dist.all_gather_object(handles, bytes(handle), group=group)
-            self.group_args = _lib.AllreduceGroup(world=self.world, rank=self.rank, epoch=0, max_n=self.max_n)
+            self.group_args = _lib.AllreduceGroup(world=self.world, rank=self.rank, max_n=self.max_n)
             for r, h in enumerate(handles):
                 if r == self.rank:
                     self.group_args.buffers[r] = self.own
@@ -134,16 +134,13 @@ class RowParallelAllReduce:
         N = b_shard.shape[1]
         out = torch.empty((M, N), device=a_shard.device, dtype=a_shard.dtype)
         if a_shard.dtype == b_shard.dtype == torch.bfloat16 and M and N and K:
-            self.epoch += 1
-            self.group_args.epoch = self.epoch
             rc = _lib.lib().nvb200_matmul_allreduce(
                 out.data_ptr(), a_shard.data_ptr(), b_shard.data_ptr(), M, N, K, a_shard.stride(0), a_shard.stride(1),
                 b_shard.stride(0), b_shard.stride(1), out.stride(0), ctypes.byref(self.group_args),
                 _lib.status_word(a_shard.device).data_ptr(), _lib.stream_of(a_shard))
-            if rc != _lib.ERR_UNSUPPORTED:
+            if rc != _lib.ERR_UNSUPPORTED:  # (every rank takes the same branch: same shapes on every rank)
                 _lib.check(rc, "matmul_allreduce")
                 return out
-            self.epoch -= 1  # nothing was launched: the epoch is not used (every rank takes the same branch)
         c = matmul(a_shard, b_shard)
         dist.all_reduce(c, group=self.group)
         return c

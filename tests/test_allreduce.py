@@ -2,7 +2,8 @@
 nanovllm_b200.parallel.RowParallelAllReduce) on two GPUs, one process each (NCCL group for the set-up): against
 the fp64 product of the full operands within bf16 tolerance, against the reference's path (matmul, then an NCCL
 all-reduce of the bf16 partials), and identical on both ranks; three calls per shape so both halves of the
-exchange buffers and increasing epochs are used. Needs two GPUs (skipped otherwise)."""
+exchange buffers and increasing epochs are used; and three replays of a CUDA graph that captured one call, with
+new inputs each time. Needs two GPUs (skipped otherwise)."""
 import math
 import os
 import socket
@@ -50,7 +51,30 @@ def _worker(rank, port, out_dir):
                 results.append(dict(shape=(M, N, K), it=it, out=out.cpu(), nccl=ref_nccl.cpu(),
                                     same=all(torch.equal(gathered[0], x) for x in gathered),
                                     ref=(a.double() @ w.double().t()).cpu(), status=_lib.status(clear=True)))
+        # Captured in a CUDA graph and replayed with new inputs: each replay is a new call (the kernel advances its
+        # epoch in device memory), checked against the NCCL path.
+        M, N, K = 32, 1024, 2048
+        k0, k1 = rank * K // WORLD, (rank + 1) * K // WORLD
+        a_in = torch.zeros(M, k1 - k0, device="cuda", dtype=torch.bfloat16)
+        w_in = torch.zeros(N, k1 - k0, device="cuda", dtype=torch.bfloat16)
+        ar(a_in, w_in.t())
         torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            g_out = ar(a_in, w_in.t())
+        for it in range(3):
+            g = torch.Generator(device="cuda").manual_seed(1000 + it)
+            a = (torch.randn(M, K, device="cuda", generator=g) / math.sqrt(K)).to(torch.bfloat16)
+            w = torch.randn(N, K, device="cuda", generator=g).to(torch.bfloat16)
+            a_in.copy_(a[:, k0:k1])
+            w_in.copy_(w[:, k0:k1])
+            graph.replay()
+            ref_nccl = matmul(a_in, w_in.t())
+            dist.all_reduce(ref_nccl)
+            results.append(dict(shape=("graph", M, N, K), it=it, out=g_out.clone().cpu(), nccl=ref_nccl.cpu(),
+                                same=True, ref=(a.double() @ w.double().t()).cpu(), status=_lib.status(clear=True)))
+        torch.cuda.synchronize()
+        del graph
     finally:
         ar.close()
         dist.barrier()
@@ -63,7 +87,7 @@ def _worker(rank, port, out_dir):
 def test_row_parallel_allreduce(tmp_path):
     mp.start_processes(_worker, args=(_free_port(), str(tmp_path)), nprocs=WORLD, start_method="spawn")
     results = torch.load(tmp_path / "out.pt")
-    assert len(results) == 3 * len(SHAPES)
+    assert len(results) == 3 * len(SHAPES) + 3
     for r in results:
         assert r["status"] == 0, r["shape"]
         assert r["same"], r["shape"]  # every rank holds the same bits
