@@ -54,6 +54,7 @@ def parse_args():
     ap.add_argument("--decode-backends", default="b200,compile,triton_fused")
     ap.add_argument("--decode-batch", type=int, default=32)
     ap.add_argument("--decode-ctx", type=int, default=1024)
+    ap.add_argument("--decode-tp", type=int, default=1, help="tensor-parallel ranks of the decode step (one GPU each)")
     ap.add_argument("--tokens", type=int, default=8192, help="tokens per step at N = 1")
     ap.add_argument("--scaling", choices=["weak", "strong"], default="weak")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -479,7 +480,10 @@ QWEN3_06B = {"architectures": ["Qwen3ForCausalLM"], "model_type": "qwen3", "hidd
              "hidden_act": "silu", "attention_bias": False}
 
 
-def decode_worker(backend: str, bs: int, ctx: int) -> dict:
+def decode_worker(backend: str, bs: int, ctx: int, tp: int = 1) -> dict:
+    """One rank of the decode-step measurement (tp > 1: launched once per GPU by torch.distributed.run; the
+    reference's ModelRunner then forms its own NCCL group, and every rank replays its graph in step with the others,
+    as the reference's worker processes would)."""
     import tempfile
     ref = os.path.join(ROOT, "baseline", "_ref")
     sys.path.insert(0, ref)
@@ -487,6 +491,24 @@ def decode_worker(backend: str, bs: int, ctx: int) -> dict:
     nanovllm_b200.install()
     import nanovllm.engine.model_runner as mr
     from nanovllm.config import Config
+    rank = int(os.environ.get("RANK", "0"))
+    if tp > 1:
+        import torch.distributed as tdist
+        from multiprocessing.shared_memory import SharedMemory
+        init = tdist.init_process_group
+
+        def init_127(backend_name, init_method=None, **kw):
+            # The runner's own rendezvous (tcp://localhost:2333) would wait forever under torch.distributed.run:
+            # there, a tcp:// store connects to the launcher's store as a client, and nothing serves port 2333. Use
+            # the launcher's rendezvous (env://, MASTER_ADDR = 127.0.0.1) instead.
+            return init(backend_name, "env://", **kw)
+        mr.dist.init_process_group = init_127
+        mr.ModelRunner.loop = lambda self: None  # ranks > 0 return from __init__ instead of serving rank 0's calls
+        if rank == 0:
+            try:  # a segment left by an interrupted run would make the runner's create fail
+                SharedMemory(name="nanovllm").unlink()
+            except FileNotFoundError:
+                pass
 
     def random_weights(model, path):  # no checkpoint: random-init every parameter (norm weights around 1)
         g = torch.Generator(device="cuda").manual_seed(0)
@@ -501,8 +523,8 @@ def decode_worker(backend: str, bs: int, ctx: int) -> dict:
     with open(os.path.join(d, "config.json"), "w") as f:
         json.dump(QWEN3_06B, f)
     cfg = Config(d, kernel_backend=backend, max_num_seqs=bs, max_model_len=2048, max_num_batched_tokens=4096,
-                 gpu_memory_utilization=0.5)
-    runner = mr.ModelRunner(cfg, 0, [])
+                 gpu_memory_utilization=0.5, tensor_parallel_size=tp)
+    runner = mr.ModelRunner(cfg, rank, [])
     blocks_per_seq = (ctx + 1 + 255) // 256
     assert cfg.num_kvcache_blocks >= bs * blocks_per_seq
     with torch.inference_mode():  # the runner's graph buffers are inference tensors
@@ -520,19 +542,41 @@ def decode_worker(backend: str, bs: int, ctx: int) -> dict:
         gv["context_lens"][:bs] = ctx + 1
         graph = runner.graphs[("target", 1, bs)]
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        if tp > 1:
+            mr.dist.barrier()
         for _ in range(10):
             graph.replay()
         per_run = []
         for _ in range(3):
+            if tp > 1:
+                torch.cuda.synchronize()
+                mr.dist.barrier()
             start.record()
             for _ in range(50):
                 graph.replay()
             end.record()
             end.synchronize()
-            per_run.append(start.elapsed_time(end) / 50)
+            t = start.elapsed_time(end) / 50
+            if tp > 1:  # the slowest rank's time
+                tt = torch.tensor([t], device="cuda")
+                mr.dist.all_reduce(tt, op=mr.dist.ReduceOp.MAX)
+                t = float(tt.item())
+            per_run.append(t)
         out = gv["outputs"]["target"][:bs].float()
         res = {"backend": backend, "graph_replay_us": 1e3 * sorted(per_run)[1], "runs_us": [1e3 * x for x in per_run],
-               "finite": bool(torch.isfinite(out).all()), "kv_blocks": cfg.num_kvcache_blocks}
+               "finite": bool(torch.isfinite(out).all()), "kv_blocks": cfg.num_kvcache_blocks, "tp": tp}
+    if tp > 1:
+        torch.cuda.synchronize()
+        del graph
+        runner.graphs.clear()  # graphs holding NCCL calls go before the process group
+        mr.dist.barrier()
+        if rank == 0:
+            runner.shm.close()
+            runner.shm.unlink()
+        else:
+            runner.shm.close()
+        mr.dist.destroy_process_group()
+        return res if rank == 0 else None
     try:
         runner.exit()
     except Exception:
@@ -544,7 +588,10 @@ def run_decode(args) -> None:
     results = {}
     for backend in args.decode_backends.split(","):
         cmd = [sys.executable, os.path.abspath(__file__), "--decode-worker", backend, "--decode-batch",
-               str(args.decode_batch), "--decode-ctx", str(args.decode_ctx)]
+               str(args.decode_batch), "--decode-ctx", str(args.decode_ctx), "--decode-tp", str(args.decode_tp)]
+        if args.decode_tp > 1:
+            cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={args.decode_tp}",
+                   "--master-addr", "127.0.0.1", "--master-port", "29581", *cmd[1:]]
         out = subprocess.run(cmd, capture_output=True, text=True)
         lines = [ln for ln in out.stdout.splitlines() if ln.startswith("{")]
         if out.returncode == 0 and lines:
@@ -553,11 +600,12 @@ def run_decode(args) -> None:
             results[backend] = {"backend": backend, "error": (out.stderr or out.stdout)[-800:]}
     ours = results.get("b200", {})
     line = {"metric": "decode-step graph replay us (Qwen3-0.6B arch, batch 32, ctx 1024)",
-            "value": ours.get("graph_replay_us"), "unit": "us", "n_gpus": 1, "steps": 150, "warmup": 10,
+            "value": ours.get("graph_replay_us"), "unit": "us", "n_gpus": args.decode_tp, "steps": 150, "warmup": 10,
             "ms_per_step": (ours.get("graph_replay_us") or 0) / 1e3, "higher_is_better": False, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (random-init weights, N(0,1) KV cache)",
             "config": {"workload": "decode", "model": "Qwen3-0.6B architecture", "batch": args.decode_batch,
-                       "context": args.decode_ctx, "parallelism": "tp1", "graph": "whole-step CUDA graph"},
+                       "context": args.decode_ctx, "parallelism": f"tp{args.decode_tp}",
+                       "graph": "whole-step CUDA graph"},
             "backends": results}
     print(json.dumps(line), flush=True)
 
@@ -565,7 +613,9 @@ def run_decode(args) -> None:
 def main():
     args = parse_args()
     if args.decode_worker:
-        print(json.dumps(decode_worker(args.decode_worker, args.decode_batch, args.decode_ctx)), flush=True)
+        res = decode_worker(args.decode_worker, args.decode_batch, args.decode_ctx, args.decode_tp)
+        if res is not None:
+            print(json.dumps(res), flush=True)
         return
     if args.workload == "decode":
         run_decode(args)

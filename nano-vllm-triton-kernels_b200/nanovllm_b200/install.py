@@ -11,7 +11,12 @@ The reference selects its kernels with the module-global string `nanovllm.kernel
    `nanovllm.kernels.backend == "b200"`; every other backend keeps the reference's own kernels;
 3. makes `Qwen3Attention` (nanovllm/models/qwen3.py:73-75) take the fused path for "b200" as for "triton_fused",
    so q/k norm, RoPE and the KV write run as one kernel inside Attention.forward (layers/attention.py:64-76);
-4. makes the tensor-parallel worker processes (spawned, nanovllm/engine/llm_engine.py:24-30) run install() too.
+4. makes the tensor-parallel worker processes (spawned, nanovllm/engine/llm_engine.py:24-30) run install() too;
+5. under tensor parallelism, makes RowParallelLinear (o_proj, down_proj; nanovllm/layers/linear.py:131-156) run
+   decode-sized batches (at most 64 rows, bf16, no bias) as one fused GEMM + NVLink all-reduce kernel per rank
+   (nanovllm_b200.parallel.RowParallelAllReduce) instead of F.linear and an NCCL all-reduce. Its exchange buffers
+   are set up collectively on the first call, which is the warm-up prefill (never a CUDA-graph capture), so the
+   decode graphs capture only the kernel.
 
 Call it once, before constructing `LLM(..., kernel_backend="b200")`.
 """
@@ -99,4 +104,45 @@ def install() -> None:
 
     # 4. Spawned tensor-parallel workers register the backend before building their ModelRunner.
     engine_mod.ModelRunner = _model_runner
+
+    # 5. Row-parallel layers of a b200 model: fused GEMM + all-reduce for decode-sized batches.
+    import nanovllm.layers.linear as linear_mod
+    row_init, row_forward = linear_mod.RowParallelLinear.__init__, linear_mod.RowParallelLinear.forward
+
+    @functools.wraps(row_init)
+    def row_parallel_init(self, *args, **kwargs):
+        row_init(self, *args, **kwargs)
+        self._b200_fused = kernels_mod.backend == BACKEND and self.tp_size > 1
+
+    @functools.wraps(row_forward)
+    def row_parallel_forward(self, x):
+        if not getattr(self, "_b200_fused", False):
+            return row_forward(self, x)
+        op = _row_parallel_op(self.weight.shape[0], x.device)
+        if (op is None or self.bias is not None or x.dim() != 2 or x.shape[0] > 64 or x.dtype != self.weight.dtype
+                or self.weight.shape[0] > op.max_n):
+            return row_forward(self, x)
+        return op(x, self.weight.t())
+    linear_mod.RowParallelLinear.__init__ = row_parallel_init
+    linear_mod.RowParallelLinear.forward = row_parallel_forward
     _installed = True
+
+
+_row_op = None
+
+
+def _row_parallel_op(n_out, device):
+    """The process's RowParallelAllReduce, created (collectively: every rank runs the same layers) by the first
+    row-parallel call outside a CUDA-graph capture; None while it does not exist and a capture is running."""
+    global _row_op
+    if _row_op is None:
+        import torch
+        if torch.cuda.is_current_stream_capturing():
+            return None
+        from nanovllm_b200.parallel import RowParallelAllReduce
+        _row_op = RowParallelAllReduce(max_n=n_out, device=device)
+        # One call at once (every rank reaches this point together), so that the kernel's one-time set-up (its
+        # shared-memory attribute) is done before any graph capture.
+        x = torch.zeros(1, 64, dtype=torch.bfloat16, device=device)
+        _row_op(x, torch.zeros(n_out, 64, dtype=torch.bfloat16, device=device).t())
+    return _row_op
