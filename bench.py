@@ -20,7 +20,9 @@ it, tests/test_oracle.py), run on the host cores in bf16.
 Other workloads (not the driver's headline): fused06b (config 1 shape at T = 8192), norm (config 2: rms_norm,
 add_rms_norm, silu_and_mul at T = 8192), matmul (config 4, bf16 M = K = N = 4096), gateup (the gate_up GEMM with
 the SiLU x Mul epilogue at the Qwen3-8B MLP shape, M = 4096), rowpar (decode-sized row-parallel GEMM fused with
-its NVLink all-reduce, Qwen3-8B down_proj split over the ranks), decode (config 5: the reference's decode step per
+its NVLink all-reduce, Qwen3-8B down_proj split over the ranks), attn (paged decode attention at the config-5
+decode shape: 32 sequences x 1024 keys, Qwen3-0.6B heads, pages of 256; flash-attn's kernel timed beside it),
+storekv (the plain KV-cache write at T = 8192, Qwen3-0.6B heads), decode (config 5: the reference's decode step per
 backend).
 """
 import argparse
@@ -49,7 +51,8 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", default="fused8b", choices=["fused8b", "fused06b", "norm", "matmul", "gateup", "rowpar", "decode"])
+    ap.add_argument("--workload", default="fused8b", choices=["fused8b", "fused06b", "norm", "matmul", "gateup", "rowpar", "attn",
+                                                            "storekv", "decode"])
     ap.add_argument("--decode-worker", default=None, help=argparse.SUPPRESS)
     ap.add_argument("--decode-backends", default="b200,compile,triton_fused")
     ap.add_argument("--decode-batch", type=int, default=32)
@@ -390,6 +393,121 @@ def rowpar_workload(args, rank, world, dev):
                         "l2": "flushed between timed steps"})
 
 
+def attn_workload(args, rank, world, dev):
+    """Decode attention of the config-5 decode step (the flash_attn_with_kvcache call of the reference's
+    Attention.forward): 32 sequences, one query each, 1024 keys per sequence in pages of 256 (randomly placed
+    blocks), Qwen3-0.6B heads (16 q / 8 kv, head_dim 128), bf16 cache N(0,1). Sharded by KV head like the fused op
+    (weak scaling multiplies the sequences by N). Four copies of the cache rotate between steps, so no step finds the
+    previous one's keys in L2 even without the flush."""
+    from nanovllm_b200.kernels.attention import flash_attn_with_kvcache
+    from oracle import reference_math as om
+    B = 32 * (world if args.scaling == "weak" else 1)
+    hq, hkv, d, bs, ctx = 16 // world, 8 // world, 128, 256, 1024
+    pages = ctx // bs
+    nb = B * pages + 8
+    g = torch.Generator(device=dev).manual_seed(17 + rank)
+    copies = 4
+    caches = [(torch.randn(nb, bs, hkv, d, device=dev, generator=g).to(torch.bfloat16),
+               torch.randn(nb, bs, hkv, d, device=dev, generator=g).to(torch.bfloat16)) for _ in range(copies)]
+    q = torch.randn(B, 1, hq, d, device=dev, generator=g).to(torch.bfloat16)
+    table = torch.randperm(nb, device=dev, generator=g)[:B * pages].view(B, pages).to(torch.int32)
+    seqlens = torch.full((B,), ctx, dtype=torch.int32, device=dev)
+    scale = d ** -0.5
+    units = om.paged_decode_attention_bytes([ctx] * B, 1, hq, hkv, d, bs)
+    step = [0]
+
+    def launch():
+        kc, vc = caches[step[0] % copies]
+        step[0] += 1
+        flash_attn_with_kvcache(q, kc, vc, cache_seqlens=seqlens, block_table=table, softmax_scale=scale, causal=True)
+
+    def library():
+        import flash_attn
+        kc, vc = caches[step[0] % copies]
+        step[0] += 1
+        flash_attn.flash_attn_with_kvcache(q, kc, vc, cache_seqlens=seqlens, block_table=table, softmax_scale=scale,
+                                           causal=True)
+
+    host = {}
+
+    def e2e():
+        if not host:
+            host.update(q=q.cpu().pin_memory(), lens=seqlens.cpu().pin_memory(), table=table.cpu().pin_memory(),
+                        out=torch.empty(B, 1, hq, d, dtype=torch.bfloat16).pin_memory(), dq=torch.empty_like(q),
+                        dlens=torch.empty_like(seqlens), dtable=torch.empty_like(table))
+        host["dq"].copy_(host["q"], non_blocking=True)
+        host["dlens"].copy_(host["lens"], non_blocking=True)
+        host["dtable"].copy_(host["table"], non_blocking=True)
+        kc, vc = caches[step[0] % copies]
+        step[0] += 1
+        out = flash_attn_with_kvcache(host["dq"], kc, vc, cache_seqlens=host["dlens"], block_table=host["dtable"],
+                                      softmax_scale=scale, causal=True)
+        host["out"].copy_(out, non_blocking=True)
+        return q.numel() * 2 + seqlens.numel() * 4 + table.numel() * 4, out.numel() * 2
+
+    xc = {}
+
+    def cpu(tokens=B):
+        if not xc:
+            xc.update(q=q.cpu(), k=caches[0][0].cpu(), v=caches[0][1].cpu(), t=table.cpu(), l=seqlens.cpu())
+        om.paged_decode_attention(xc["q"][:tokens], xc["k"], xc["v"], xc["l"][:tokens], xc["t"][:tokens], scale, True)
+        return om.paged_decode_attention_bytes([ctx] * tokens, 1, hq, hkv, d, bs)
+
+    return dict(launch=launch, units=units, e2e=e2e, cpu=cpu, unit="GB/s", scale=1e9, bound="hbm",
+                metric="paged decode attention GB/s (32 seqs x 1024 keys, Qwen3-0.6B heads)", dtype="bf16",
+                launches_per_step=1, traffic_key="attn", library=("flash_attn.flash_attn_with_kvcache", library),
+                e2e_path="nanovllm_b200.kernels.attention.flash_attn_with_kvcache (public API) with pinned host q, "
+                         "lengths and block table",
+                config={"workload": "attn", "tokens_per_step": B, "sequences": B, "keys_per_sequence": ctx,
+                        "q_heads_per_gpu": hq, "kv_heads_per_gpu": hkv, "head_dim": d, "block_size": bs,
+                        "queries_per_sequence": 1, "causal": True,
+                        "parallelism": f"tp{world} (KV-head sharding, no collective)",
+                        "l2": f"flushed between timed steps; {copies} cache copies rotate",
+                        "bytes_formula": "sum_b L_b*Hkv*D*2*2 + 2*B*Hq*D*2 + 4*B + 4*sum_b ceil(L_b/256)"})
+
+
+def storekv_workload(args, rank, world, dev):
+    """The plain KV-cache write (store_kvcache, the attention layer's non-fused route) at T = 8192 tokens with the
+    Qwen3-0.6B layout: k and v are strided views of the qkv projection output [T, 4096], the cache is
+    [64, 256, 8, 128] per rank slice, 5 % of the slots are -1."""
+    from nanovllm_b200.kernels.attention import store_kvcache
+    from oracle import reference_math as om
+    T = args.tokens * (world if args.scaling == "weak" else 1)
+    hq, hkv, d = 16 // world, 8 // world, 128
+    blocks = max(64, (T + 255) // 256 + 1)
+    g = torch.Generator(device=dev).manual_seed(23 + rank)
+    qkv = torch.randn(T, (hq + 2 * hkv) * d, device=dev, generator=g).to(torch.bfloat16)
+    k = qkv[:, hq * d:(hq + hkv) * d].view(T, hkv, d)
+    v = qkv[:, (hq + hkv) * d:].view(T, hkv, d)
+    kc = torch.zeros(blocks, 256, hkv, d, dtype=torch.bfloat16, device=dev)
+    vc = torch.zeros_like(kc)
+    g2 = torch.Generator(device=dev).manual_seed(99)
+    slots = torch.randperm(blocks * 256, device=dev, generator=g2)[:T].to(torch.int32)
+    slots[torch.randperm(T, device=dev, generator=g2)[:round(0.05 * T)]] = -1
+    kept = T - round(0.05 * T)
+    units = om.store_kvcache_bytes(T, hkv * d, 2, kept)
+
+    def launch():
+        store_kvcache(k, v, kc, vc, slots)
+
+    xc = {}
+
+    def cpu(tokens=T):
+        if not xc:
+            xc.update(k=k.cpu(), v=v.cpu(), kc=kc.cpu(), vc=vc.cpu(), s=slots.cpu())
+        om.store_kvcache(xc["k"][:tokens], xc["v"][:tokens], xc["kc"], xc["vc"], xc["s"][:tokens])
+        return om.store_kvcache_bytes(tokens, hkv * d, 2, int((xc["s"][:tokens] >= 0).sum()))
+
+    return dict(launch=launch, units=units, e2e=None, cpu=cpu, unit="GB/s", scale=1e9, bound="hbm",
+                metric="store_kvcache GB/s at T=8192 (Qwen3-0.6B heads)", dtype="bf16", launches_per_step=1,
+                traffic_key="storekv",
+                config={"workload": "storekv", "tokens_per_step": T, "kv_heads_per_gpu": hkv, "head_dim": d,
+                        "cache_blocks": blocks, "block_size": 256, "skip_fraction": 0.05,
+                        "parallelism": f"tp{world} (KV-head sharding, no collective)",
+                        "l2": "flushed between timed steps",
+                        "bytes_formula": "T*4 + kept*4*Hkv*D*2"})
+
+
 def make_workload(args, rank, world, dev):
     if args.workload == "fused8b":
         return fused_workload(args, rank, world, dev, 32, 8, 32768, 1024, "fused8b")
@@ -401,6 +519,10 @@ def make_workload(args, rank, world, dev):
         return gateup_workload(args, rank, world, dev)
     if args.workload == "rowpar":
         return rowpar_workload(args, rank, world, dev)
+    if args.workload == "attn":
+        return attn_workload(args, rank, world, dev)
+    if args.workload == "storekv":
+        return storekv_workload(args, rank, world, dev)
     return matmul_workload(args, rank, world, dev)
 
 
@@ -681,7 +803,29 @@ def main():
             e_s = max_over_ranks(e_start.elapsed_time(e_end) / 1e3, world)
             e2e = {"value": all_units / e_s / wl["scale"], "unit": wl["unit"], "h2d_bytes_per_step": h2d,
                    "d2h_bytes_per_step": d2h,
-                   "path": "nanovllm_b200.kernels.qk_norm_rope_kv (public API) with pinned host inputs/outputs"}
+                   "path": wl.get("e2e_path", "nanovllm_b200.kernels.qk_norm_rope_kv (public API) with pinned "
+                                                      "host inputs/outputs")}
+
+        library = None
+        if wl.get("library") is not None:
+            name, fn = wl["library"]
+            for _ in range(args.warmup):
+                flush_l2()
+                fn()
+            torch.cuda.synchronize()
+            lib_steps = min(args.steps, 500)
+            ls = [torch.cuda.Event(enable_timing=True) for _ in range(lib_steps)]
+            le = [torch.cuda.Event(enable_timing=True) for _ in range(lib_steps)]
+            for i in range(lib_steps):
+                flush_l2()
+                ls[i].record(stream)
+                fn()
+                le[i].record(stream)
+            torch.cuda.synchronize()
+            lib_s = sum(a.elapsed_time(b) for a, b in zip(ls, le)) / 1e3 / lib_steps
+            library = {"name": name, "us_per_step": 1e6 * lib_s, "value": wl["units"] / lib_s / wl["scale"],
+                       "ours_us_per_step": 1e6 * local_s / args.steps,
+                       "note": "the library kernel the reference calls, same inputs and L2 flush, this rank"}
 
     if wl["bound"] == "hbm":
         peak = peaks["hbm_gbs"]
@@ -702,6 +846,8 @@ def main():
             "gpu_launches_scope": "rank 0, timed region"}
     if e2e is not None:
         line["e2e"] = e2e
+    if library is not None:
+        line["library_comparison"] = library
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         torch.set_num_threads(os.cpu_count() or 1)
         full = wl["config"].get("tokens_per_step", wl["config"].get("M"))

@@ -171,6 +171,70 @@ NVB200_API int nvb200_matmul_allreduce(void *out, const void *a, const void *b, 
                             int64_t sam, int64_t sak, int64_t sbk, int64_t sbn, int64_t scm,
                             const nvb200_allreduce_group *group, int32_t *status, nvb200_stream_t stream);
 
+/* Paged KV-cache write without norm or RoPE: row t of key and value (row_elems = Hkv * D elements, contiguous) is
+ * copied to row slot_mapping[t] of k_cache and v_cache (row s at element s * row_elems); slot -1 is skipped.
+ * Replaces: nanovllm/layers/attention.py:34-41 (store_kvcache) and store_kvcache_kernel :11-31, the attention
+ * layer's non-fused route (:75-76).
+ * key, value: token t's row at key + t * key_token_stride (elements). slot_mapping: int32 (slot_bytes 4) or int64
+ * (slot_bytes 8). num_slots: rows the caches hold; a slot outside [-1, num_slots) is not stored and sets
+ * NVB200_STATUS_BAD_SLOT in *status (nullable). dtype: NVB200_BF16, NVB200_F16 or NVB200_F32 (a byte copy). */
+NVB200_API int nvb200_store_kvcache(const void *key, int64_t key_token_stride, const void *value,
+                                    int64_t value_token_stride, void *k_cache, void *v_cache,
+                                    const void *slot_mapping, int slot_bytes, int64_t num_tokens, int64_t row_elems,
+                                    int64_t num_slots, int dtype, int32_t *status, nvb200_stream_t stream);
+
+/* Paged decode attention: out[b, i, hq] = softmax(q[b, i, hq] . K^T * softmax_scale) V over the keys of sequence b
+ * in the paged cache, K and V of KV head hq / (num_q_heads / num_kv_heads). With causal != 0 query i of n =
+ * queries_per_seq sees keys [0, seqlens[b] - n + i] (bottom-right alignment); otherwise keys [0, seqlens[b]). A query
+ * that sees no key gets zeros.
+ * Replaces: the flash_attn_with_kvcache call of nanovllm/layers/attention.py:84-91 (the decode branch of
+ * Attention.forward: q [num_seqs, n, Hq, D], cache_seqlens = context_lens, block_table = block_tables, causal).
+ *   q: [batch, queries_per_seq, num_q_heads, head_dim] with the given element strides and a unit last stride.
+ *   k_cache, v_cache: [num_blocks, block_size, num_kv_heads, head_dim], both with the given strides, unit last stride.
+ *   block_table: [batch, max_blocks_per_seq] int32, row stride block_table_stride; key j of sequence b is token
+ *     j % block_size of block block_table[b, j / block_size]. NULL: sequence b is block b (max_blocks_per_seq 1).
+ *   seqlens: [batch] int32, the keys in the cache per sequence (the new tokens included).
+ *   out: [batch, queries_per_seq, num_q_heads, head_dim] contiguous, written.
+ *   num_splits: CTAs (a thread-block cluster) sharing one sequence's keys, 1..8; 0 = chosen from the sizes
+ *     (nvb200_paged_decode_splits tells which).
+ * Takes bf16, head_dim 128, queries_per_seq * (num_q_heads / num_kv_heads) <= 16 and 16-byte aligned cache rows;
+ * returns NVB200_ERR_UNSUPPORTED otherwise. Block-table entries outside [0, num_blocks) and seqlens beyond
+ * max_blocks_per_seq * block_size are not followed: NVB200_STATUS_BAD_SLOT is set in *status (nullable). */
+typedef struct nvb200_paged_decode_args {
+  void *out;
+  const void *q;
+  int64_t q_batch_stride;
+  int64_t q_token_stride;
+  int64_t q_head_stride;
+  const void *k_cache;
+  const void *v_cache;
+  int64_t cache_block_stride;
+  int64_t cache_token_stride;
+  int64_t cache_head_stride;
+  int64_t num_blocks;
+  const int32_t *block_table;
+  int64_t block_table_stride;
+  const int32_t *seqlens;
+  int32_t batch;
+  int32_t queries_per_seq;
+  int32_t num_q_heads;
+  int32_t num_kv_heads;
+  int32_t head_dim;
+  int32_t block_size;
+  int32_t max_blocks_per_seq;
+  int32_t causal;
+  int32_t num_splits;
+  int32_t dtype;
+  float softmax_scale;
+  int32_t *status;
+} nvb200_paged_decode_args;
+
+NVB200_API int nvb200_paged_decode_attention(const nvb200_paged_decode_args *args, nvb200_stream_t stream);
+
+/* The split count nvb200_paged_decode_attention uses for these sizes (num_splits 0 = its automatic choice). */
+NVB200_API int nvb200_paged_decode_splits(int32_t batch, int32_t num_kv_heads, int32_t max_blocks_per_seq,
+                                          int32_t block_size, int32_t num_splits);
+
 #ifdef __cplusplus
 }
 #endif

@@ -23,7 +23,8 @@ STATUS_BAD_POSITION, STATUS_BAD_SLOT, STATUS_WAIT_TIMEOUT = 1, 2, 4
 EXPORTS = ("nvb200_status_string", "nvb200_qk_norm_rope_kv", "nvb200_rms_norm", "nvb200_fused_add_rms_norm",
            "nvb200_silu_and_mul", "nvb200_matmul_workspace_size", "nvb200_matmul", "nvb200_matmul_silu_and_mul",
            "nvb200_allreduce_buffer_bytes", "nvb200_allreduce_buffer_create", "nvb200_allreduce_buffer_open",
-           "nvb200_allreduce_buffer_close", "nvb200_matmul_allreduce")
+           "nvb200_allreduce_buffer_close", "nvb200_matmul_allreduce", "nvb200_store_kvcache",
+           "nvb200_paged_decode_attention", "nvb200_paged_decode_splits")
 
 _vp, _i64, _i32, _f32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32, ctypes.c_float
 
@@ -38,6 +39,18 @@ class QkNormRopeKvArgs(ctypes.Structure):
         ("k_cache", _vp), ("v_cache", _vp), ("num_slots", _i64),
         ("num_tokens", _i64), ("num_q_heads", _i32), ("num_kv_heads", _i32), ("head_dim", _i32),
         ("eps", _f32), ("status", _vp),
+    ]
+
+
+class PagedDecodeArgs(ctypes.Structure):
+    """nvb200_paged_decode_args (field order and types as in nvb200.h)."""
+    _fields_ = [
+        ("out", _vp), ("q", _vp), ("q_batch_stride", _i64), ("q_token_stride", _i64), ("q_head_stride", _i64),
+        ("k_cache", _vp), ("v_cache", _vp), ("cache_block_stride", _i64), ("cache_token_stride", _i64),
+        ("cache_head_stride", _i64), ("num_blocks", _i64), ("block_table", _vp), ("block_table_stride", _i64),
+        ("seqlens", _vp), ("batch", _i32), ("queries_per_seq", _i32), ("num_q_heads", _i32), ("num_kv_heads", _i32),
+        ("head_dim", _i32), ("block_size", _i32), ("max_blocks_per_seq", _i32), ("causal", _i32),
+        ("num_splits", _i32), ("dtype", _i32), ("softmax_scale", _f32), ("status", _vp),
     ]
 
 
@@ -82,6 +95,13 @@ def _declare(lib):
     lib.nvb200_allreduce_buffer_close.restype = ctypes.c_int
     lib.nvb200_matmul_allreduce.argtypes = [_vp, _vp, _vp] + [_i64] * 8 + [ctypes.POINTER(AllreduceGroup), _vp, _vp]
     lib.nvb200_matmul_allreduce.restype = ctypes.c_int
+    lib.nvb200_store_kvcache.argtypes = [_vp, _i64, _vp, _i64, _vp, _vp, _vp, ctypes.c_int, _i64, _i64, _i64,
+                                         ctypes.c_int, _vp, _vp]
+    lib.nvb200_store_kvcache.restype = ctypes.c_int
+    lib.nvb200_paged_decode_attention.argtypes = [ctypes.POINTER(PagedDecodeArgs), _vp]
+    lib.nvb200_paged_decode_attention.restype = ctypes.c_int
+    lib.nvb200_paged_decode_splits.argtypes = [_i32] * 5
+    lib.nvb200_paged_decode_splits.restype = ctypes.c_int
 
 
 def lib():

@@ -16,7 +16,12 @@ The reference selects its kernels with the module-global string `nanovllm.kernel
    decode-sized batches (at most 64 rows, bf16, no bias) as one fused GEMM + NVLink all-reduce kernel per rank
    (nanovllm_b200.parallel.RowParallelAllReduce) instead of F.linear and an NCCL all-reduce. Its exchange buffers
    are set up collectively on the first call, which is the warm-up prefill (never a CUDA-graph capture), so the
-   decode graphs capture only the kernel.
+   decode graphs capture only the kernel;
+6. makes the attention layer's plain KV-cache write (store_kvcache, nanovllm/layers/attention.py:34-41, the route of
+   models whose q/k are normalised before the layer) and its decode attention (the flash_attn_with_kvcache call of
+   Attention.forward, :84-91) run the b200 kernels while the backend is "b200". Decode calls outside what the b200
+   kernel takes (`nanovllm_b200.kernels.attention.supports`: bf16, head_dim 128, at most 16 query rows per KV head)
+   keep flash-attn's; prefill attention (flash_attn_varlen_func, :79-83) stays flash-attn's.
 
 Call it once, before constructing `LLM(..., kernel_backend="b200")`.
 """
@@ -57,6 +62,7 @@ def install() -> None:
     import nanovllm.layers.layernorm as layernorm_mod
     import nanovllm.models.qwen3 as qwen3_mod
 
+    from nanovllm_b200.kernels import attention as b200_attention
     from nanovllm_b200.kernels import matmul as b200_matmul
     from nanovllm_b200.kernels import qk_norm_rope_kv as b200_fused
     from nanovllm_b200.kernels import rms_norm as b200_norm
@@ -84,9 +90,21 @@ def install() -> None:
         (layernorm_mod, "fused_add_rms_norm", b200_norm.fused_add_rms_norm),
         (activation_mod, "silu_and_mul", b200_swiglu.silu_and_mul),
         (attention_mod, "qk_norm_rope_kv", b200_fused.qk_norm_rope_kv),
+        (attention_mod, "store_kvcache", b200_attention.store_kvcache),
     ]
     for mod, name, ours in pairs:
         setattr(mod, name, _by_backend(kernels_mod, ours, getattr(mod, name)))
+
+    # Decode attention: the b200 kernel for the calls it takes, flash-attn's for the rest.
+    flash_decode = attention_mod.flash_attn_with_kvcache
+
+    @functools.wraps(flash_decode)
+    def flash_attn_with_kvcache(*args, **kwargs):
+        if kernels_mod.backend == BACKEND and b200_attention.supports(*args, **kwargs):
+            return b200_attention.flash_attn_with_kvcache(*args, **kwargs)
+        return flash_decode(*args, **kwargs)
+    flash_attn_with_kvcache.__b200__ = b200_attention.flash_attn_with_kvcache
+    attention_mod.flash_attn_with_kvcache = flash_attn_with_kvcache
 
     # 3. Qwen3Attention treats "b200" as a fused backend.
     attn_init = qwen3_mod.Qwen3Attention.__init__

@@ -1,0 +1,148 @@
+"""The attention layer's cache write and decode attention on B200 (drop-ins for nanovllm/layers/attention.py).
+
+* `store_kvcache(key, value, k_cache, v_cache, slot_mapping)`: the reference's plain KV-cache write
+  (nanovllm/layers/attention.py:34-41, the route Attention.forward takes when q/k norm and RoPE ran before it,
+  :75-76), with the same arguments and the same assertions. The copy runs in `nvb200_store_kvcache`.
+* `flash_attn_with_kvcache(q, k_cache, v_cache, cache_seqlens=..., block_table=..., softmax_scale=..., causal=...)`:
+  the decode attention of Attention.forward (:84-91), which calls flash-attn's function of that name with these
+  keywords. Same keywords and result ([B, n, Hq, D] in q's dtype); the work runs in `nvb200_paged_decode_attention`,
+  an sm_100a kernel that streams each sequence's K/V rows through the block table once. Options the decode branch
+  never passes (new k/v to append, rotary, batch indices, left padding, sliding windows, softcap, ALiBi, the
+  log-sum-exp output) raise NotImplementedError; `supports()` tells beforehand whether a call is covered.
+
+Both launch on the current torch stream, allocate their outputs with torch (graph-capture safe) and never read
+device data on the host. Out-of-range slots, block-table entries and sequence lengths are skipped (never read or
+written) and flagged in the device status word (nanovllm_b200.status()).
+"""
+import ctypes
+
+import torch
+
+from nanovllm_b200 import _lib
+
+_SLOT_BYTES = {torch.int32: 4, torch.int64: 8}
+
+
+def _require(cond: bool, msg: str = "") -> None:
+    if not cond:
+        raise AssertionError(msg)
+
+
+def _max_rows(t: torch.Tensor, row: int) -> int:
+    """Rows of `row` elements reachable from t's first element (the extent of t's strides), for bounds."""
+    if t.numel() == 0:
+        return 0
+    extent = 1 + sum((s - 1) * st for s, st in zip(t.shape, t.stride()))
+    return extent // row
+
+
+def store_kvcache(key: torch.Tensor, value: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                  slot_mapping: torch.Tensor) -> None:
+    """key, value: [N, Hkv, D] with contiguous heads (any token stride). k_cache, v_cache: caches whose dim-1 stride
+    is Hkv * D (a [blocks, block_size, Hkv, D] or [slots, Hkv * D] cache); row slot of the flattened cache receives
+    token t when slot_mapping[t] = slot, and slot -1 stores nothing. In place."""
+    N, num_heads, head_dim = key.shape
+    D = num_heads * head_dim
+    _require(key.stride(-1) == 1 and value.stride(-1) == 1)
+    _require(key.stride(1) == head_dim and value.stride(1) == head_dim)
+    _require(k_cache.stride(1) == D and v_cache.stride(1) == D)
+    _require(slot_mapping.numel() == N)
+    _require(value.shape == key.shape and key.dtype == value.dtype == k_cache.dtype == v_cache.dtype,
+             "key, value and the caches must share shape [N, Hkv, D] and dtype")
+    _require(key.dtype in _lib.DTYPE_CODE, "dtype must be bf16, fp16 or fp32")
+    _require(slot_mapping.dtype in _SLOT_BYTES, "slot_mapping must be int32 or int64")
+    _require(key.device.type == "cuda", "key must be a CUDA tensor")
+    if N == 0:
+        return
+    slots = slot_mapping if slot_mapping.is_contiguous() else slot_mapping.contiguous()
+    num_slots = min(_max_rows(k_cache, D), _max_rows(v_cache, D))
+    _lib.check(_lib.lib().nvb200_store_kvcache(
+        key.data_ptr(), key.stride(0), value.data_ptr(), value.stride(0), k_cache.data_ptr(), v_cache.data_ptr(),
+        slots.data_ptr(), _SLOT_BYTES[slots.dtype], N, D, num_slots, _lib.DTYPE_CODE[key.dtype],
+        _lib.status_word(key.device).data_ptr(), _lib.stream_of(key)), "store_kvcache")
+
+
+def supports(q, k_cache, v_cache, k=None, v=None, rotary_cos=None, rotary_sin=None, cache_seqlens=None,
+             cache_batch_idx=None, cache_leftpad=None, block_table=None, softmax_scale=None, causal=False,
+             window_size=(-1, -1), softcap=0.0, rotary_interleaved=True, alibi_slopes=None, num_splits=0,
+             return_softmax_lse=False) -> bool:
+    """Whether flash_attn_with_kvcache below takes this call: the decode form (no new k/v, rotary, batch index,
+    left padding, window, softcap, ALiBi or lse), bf16 with head_dim 128, at most 16 query rows per KV head
+    (n * Hq / Hkv), a unit last stride everywhere and 16-byte aligned cache rows."""
+    if any(x is not None for x in (k, v, rotary_cos, rotary_sin, cache_batch_idx, cache_leftpad, alibi_slopes)):
+        return False
+    if tuple(window_size) != (-1, -1) or softcap != 0.0 or return_softmax_lse or cache_seqlens is None:
+        return False
+    if q.dim() != 4 or k_cache.dim() != 4 or v_cache.shape != k_cache.shape:
+        return False
+    B, n, hq, d = q.shape
+    hkv = k_cache.shape[2]
+    if not (q.dtype == k_cache.dtype == v_cache.dtype == torch.bfloat16) or d != 128 or k_cache.shape[3] != d:
+        return False
+    if hkv == 0 or hq % hkv or n * (hq // hkv) > 16:
+        return False
+    if q.stride(-1) != 1 or k_cache.stride(-1) != 1 or v_cache.stride() != k_cache.stride():
+        return False
+    if any(s % 8 for s in k_cache.stride()[:3]) or k_cache.data_ptr() % 16 or v_cache.data_ptr() % 16:
+        return False
+    if block_table is not None and (block_table.dtype != torch.int32 or block_table.dim() != 2
+                                    or block_table.stride(-1) != 1):
+        return False
+    if block_table is None and k_cache.shape[0] < B:
+        return False
+    return True
+
+
+def flash_attn_with_kvcache(q, k_cache, v_cache, k=None, v=None, rotary_cos=None, rotary_sin=None,
+                            cache_seqlens=None, cache_batch_idx=None, cache_leftpad=None, block_table=None,
+                            softmax_scale=None, causal=False, window_size=(-1, -1), softcap=0.0,
+                            rotary_interleaved=True, alibi_slopes=None, num_splits=0, return_softmax_lse=False):
+    """Decode attention over a paged KV cache. q: [B, n, Hq, D]; k_cache, v_cache: [num_blocks, block_size, Hkv, D]
+    (with block_table [B, max_blocks] int32) or [B, max_len, Hkv, D] (without); cache_seqlens: [B] int32 or an int,
+    the keys in the cache per sequence. softmax_scale defaults to D ** -0.5; causal aligns query i of n with key
+    L - n + i. num_splits: CTAs sharing one sequence (0 = chosen from the sizes, at most 8). Returns
+    [B, n, Hq, D]."""
+    if isinstance(cache_seqlens, int):
+        cache_seqlens = torch.full((q.shape[0],), cache_seqlens, dtype=torch.int32, device=q.device)
+    if not supports(q, k_cache, v_cache, k, v, rotary_cos, rotary_sin, cache_seqlens, cache_batch_idx,
+                    cache_leftpad, block_table, softmax_scale, causal, window_size, softcap, rotary_interleaved,
+                    alibi_slopes, num_splits, return_softmax_lse):
+        raise NotImplementedError("nanovllm_b200 flash_attn_with_kvcache: only the decode form (bf16, head_dim 128, "
+                                  "n * Hq / Hkv <= 16, no new k/v, rotary, window, softcap, ALiBi or lse) is built")
+    B, n, hq, d = q.shape
+    nb, bs, hkv, _ = k_cache.shape
+    _require(q.device.type == "cuda" and k_cache.device == q.device, "q and the caches must be on one CUDA device")
+    _require(cache_seqlens.shape == (B,) and cache_seqlens.dtype == torch.int32, "cache_seqlens must be [B] int32")
+    seqlens = cache_seqlens if cache_seqlens.is_contiguous() else cache_seqlens.contiguous()
+    if block_table is not None:
+        _require(block_table.shape[0] == B and block_table.shape[1] > 0, "block_table must be [B, max_blocks]")
+    scale = d ** -0.5 if softmax_scale is None else float(softmax_scale)
+    out = torch.empty(B, n, hq, d, dtype=q.dtype, device=q.device)
+    if B == 0:
+        return out
+    a = _lib.PagedDecodeArgs()
+    a.out, a.q = out.data_ptr(), q.data_ptr()
+    a.q_batch_stride, a.q_token_stride, a.q_head_stride = q.stride(0), q.stride(1), q.stride(2)
+    a.k_cache, a.v_cache = k_cache.data_ptr(), v_cache.data_ptr()
+    a.cache_block_stride, a.cache_token_stride, a.cache_head_stride = k_cache.stride()[:3]
+    a.num_blocks = nb
+    if block_table is not None:
+        a.block_table, a.block_table_stride, a.max_blocks_per_seq = (block_table.data_ptr(), block_table.stride(0),
+                                                                     block_table.shape[1])
+    else:
+        a.block_table, a.block_table_stride, a.max_blocks_per_seq = None, 0, 1
+    a.seqlens = seqlens.data_ptr()
+    a.batch, a.queries_per_seq, a.num_q_heads, a.num_kv_heads, a.head_dim, a.block_size = B, n, hq, hkv, d, bs
+    a.causal, a.num_splits, a.dtype = int(bool(causal)), max(0, int(num_splits)), _lib.BF16
+    a.softmax_scale = scale
+    a.status = _lib.status_word(q.device).data_ptr()
+    _lib.check(_lib.lib().nvb200_paged_decode_attention(ctypes.byref(a), _lib.stream_of(q)), "flash_attn_with_kvcache")
+    return out
+
+
+def decode_splits(batch: int, num_kv_heads: int, max_blocks_per_seq: int, block_size: int, num_splits: int = 0) -> int:
+    """The number of CTAs per (sequence, KV head) the kernel uses for these sizes."""
+    return _lib.lib().nvb200_paged_decode_splits(batch, num_kv_heads, max_blocks_per_seq, block_size, num_splits)
+
+
+__all__ = ["store_kvcache", "flash_attn_with_kvcache", "supports", "decode_splits"]

@@ -92,6 +92,46 @@ def qk_norm_rope_kv(q, k, v, positions, q_weight, k_weight, eps, cos_sin_cache, 
     return qr.contiguous(), (kr.contiguous() if write_k else None)
 
 
+def paged_decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, cache_seqlens: torch.Tensor,
+                           block_table: torch.Tensor | None, softmax_scale: float, causal: bool) -> torch.Tensor:
+    """The decode branch of Attention.forward (nanovllm/layers/attention.py:84-91): flash_attn_with_kvcache(q,
+    k_cache, v_cache, cache_seqlens=context_lens, block_table=block_tables, softmax_scale, causal=True) of the
+    third-party flash-attn package (pip "flash-attn", unpinned in the reference's pyproject.toml:18; 2.8.3 in this
+    image), restated from its documented semantics:
+      * q [B, n, Hq, D]; caches [num_blocks, block_size, Hkv, D]; key j of sequence b is token j % block_size of
+        block block_table[b, j // block_size] (no table: the cache is [B, max_len, Hkv, D] per sequence);
+      * q head hq reads KV head hq // (Hq / Hkv) (grouped-query attention);
+      * causal: query i of n sees keys [0, L - n + i], L = cache_seqlens[b] (the bottom-right alignment the
+        reference's comment at attention.py:86-87 states); otherwise keys [0, L);
+      * a query that sees no key gets zeros.
+    Computed in float64 and returned as fp32 [B, n, Hq, D]."""
+    B, n, hq, d = q.shape
+    hkv = k_cache.shape[2]
+    group = hq // hkv
+    out = torch.zeros(B, n, hq, d, dtype=torch.float64, device=q.device)
+    for b in range(B):
+        L = int(cache_seqlens[b])
+        if L <= 0:
+            continue
+        if block_table is None:
+            keys, vals = k_cache[b, :L], v_cache[b, :L]
+        else:
+            bs = k_cache.shape[1]
+            pages = block_table[b, :(L + bs - 1) // bs].long()
+            keys = k_cache[pages].reshape(-1, hkv, d)[:L]
+            vals = v_cache[pages].reshape(-1, hkv, d)[:L]
+        kk = keys.double().repeat_interleave(group, dim=1)  # [L, Hq, D]
+        vv = vals.double().repeat_interleave(group, dim=1)
+        s = torch.einsum("ihd,jhd->hij", q[b].double(), kk) * softmax_scale  # [Hq, n, L]
+        j = torch.arange(L, device=q.device)
+        last = (L - n + torch.arange(n, device=q.device)) if causal else torch.full((n,), L - 1, device=q.device)
+        s = s.masked_fill(j[None, None, :] > last[None, :, None], float("-inf"))
+        seen = (last >= 0)[None, :, None]
+        p = torch.softmax(s, dim=-1).nan_to_num(0.0) * seen
+        out[b] = torch.einsum("hij,jhd->ihd", p, vv)
+    return out.float()
+
+
 def silu_and_mul(x: torch.Tensor) -> torch.Tensor:
     """SiluAndMul.silu_and_mul_compiled (nanovllm/layers/activation.py:15-18) run eagerly: silu of the gate half in
     fp32 rounded to x's dtype, times the up half in x's dtype."""
@@ -134,6 +174,23 @@ def add_rms_norm_bytes(T: int, n: int) -> int:
 
 def silu_and_mul_bytes(T: int, n: int) -> int:
     return 3 * T * n * 2
+
+
+def store_kvcache_bytes(T: int, row_elems: int, elem_bytes: int = 2, kept: int | None = None) -> int:
+    """store_kvcache: every token's slot is read (4 bytes); each kept token reads and writes its k and v rows."""
+    kept = T if kept is None else kept
+    return T * 4 + kept * 4 * row_elems * elem_bytes
+
+
+def paged_decode_attention_bytes(seqlens, n: int, hq: int, hkv: int, d: int, block_size: int) -> int:
+    """Decode attention reads every cached key and value row of its KV heads once (bf16), the queries and the
+    block-table entries it follows, and writes the output: sum_b L_b * Hkv * D * 2 * 2 + 2 * B * n * Hq * D * 2 +
+    4 * B + 4 * sum_b ceil(L_b / block_size)."""
+    seqlens = [int(x) for x in seqlens]
+    kv = sum(seqlens) * hkv * d * 2 * 2
+    qo = 2 * len(seqlens) * n * hq * d * 2
+    meta = 4 * len(seqlens) + 4 * sum((L + block_size - 1) // block_size for L in seqlens)
+    return kv + qo + meta
 
 
 def matmul_flops(m: int, n: int, k: int) -> int:

@@ -47,16 +47,44 @@ def test_no_gpu_means_error_not_crash():
 
 
 @pytest.mark.skipif(shutil.which("gcc") is None, reason="gcc not available")
-def test_struct_layout_matches_header(tmp_path):
-    fields = [f[0] for f in _lib.QkNormRopeKvArgs._fields_]
+@pytest.mark.parametrize("ctype,cname", [(_lib.QkNormRopeKvArgs, "nvb200_qk_norm_rope_kv_args"),
+                                         (_lib.PagedDecodeArgs, "nvb200_paged_decode_args"),
+                                         (_lib.AllreduceGroup, "nvb200_allreduce_group")])
+def test_struct_layout_matches_header(tmp_path, ctype, cname):
+    fields = [f[0] for f in ctype._fields_]
     src = tmp_path / "layout.c"
-    body = "\n".join(f'  printf("{f} %zu\\n", offsetof(nvb200_qk_norm_rope_kv_args, {f}));' for f in fields)
+    body = "\n".join(f'  printf("{f} %zu\\n", offsetof({cname}, {f}));' for f in fields)
     src.write_text('#include <stddef.h>\n#include <stdio.h>\n#include "nvb200.h"\nint main(void) {\n' + body +
-                   '\n  printf("sizeof %zu\\n", sizeof(nvb200_qk_norm_rope_kv_args));\n  return 0;\n}\n')
+                   f'\n  printf("sizeof %zu\\n", sizeof({cname}));\n  return 0;\n}}\n')
     exe = tmp_path / "layout"
     subprocess.run(["gcc", "-I", os.path.dirname(HEADER), str(src), "-o", str(exe)], check=True)
     out = dict(line.split() for line in subprocess.run([str(exe)], capture_output=True, text=True,
                                                        check=True).stdout.splitlines())
     for f in fields:
-        assert int(out[f]) == getattr(_lib.QkNormRopeKvArgs, f).offset, f
-    assert int(out["sizeof"]) == ctypes.sizeof(_lib.QkNormRopeKvArgs)
+        assert int(out[f]) == getattr(ctype, f).offset, f
+    assert int(out["sizeof"]) == ctypes.sizeof(ctype)
+
+
+def test_new_entry_points_reject_bad_arguments_without_a_gpu():
+    """Argument checks run before any CUDA call (so they hold on a machine without a GPU too)."""
+    lib = _lib.lib()
+    # store_kvcache: negative sizes, bad slot width, null pointers with work to do.
+    assert lib.nvb200_store_kvcache(8, 0, 8, 0, 8, 8, 8, 4, -1, 16, 4, _lib.BF16, None, None) == _lib.ERR_ARG
+    assert lib.nvb200_store_kvcache(8, 0, 8, 0, 8, 8, 8, 2, 1, 16, 4, _lib.BF16, None, None) == _lib.ERR_ARG
+    assert lib.nvb200_store_kvcache(None, 0, 8, 0, 8, 8, 8, 4, 1, 16, 4, _lib.BF16, None, None) == _lib.ERR_ARG
+    assert lib.nvb200_store_kvcache(None, 0, None, 0, None, None, None, 4, 0, 16, 4, _lib.BF16, None, None) == _lib.OK
+    # paged decode attention: a null args pointer, Hq not a multiple of Hkv, an empty batch (no launch).
+    assert lib.nvb200_paged_decode_attention(None, None) == _lib.ERR_ARG
+    a = _lib.PagedDecodeArgs()
+    a.batch, a.queries_per_seq, a.num_q_heads, a.num_kv_heads, a.head_dim = 0, 1, 16, 8, 128
+    a.block_size, a.max_blocks_per_seq, a.dtype = 256, 1, _lib.BF16
+    assert lib.nvb200_paged_decode_attention(ctypes.byref(a), None) == _lib.OK
+    a.num_q_heads = 12
+    a.num_kv_heads = 8
+    assert lib.nvb200_paged_decode_attention(ctypes.byref(a), None) == _lib.ERR_ARG
+    # The split choice: one wave of two CTAs per SM (148 SMs when no GPU answers), at most 8, at least one tile per
+    # warp of the longest sequence.
+    assert lib.nvb200_paged_decode_splits(32, 8, 4, 256, 0) == 1
+    assert lib.nvb200_paged_decode_splits(1, 8, 8, 256, 0) == 8
+    assert lib.nvb200_paged_decode_splits(1, 1, 1, 64, 0) == 1
+    assert lib.nvb200_paged_decode_splits(4, 4, 64, 256, 3) == 3

@@ -52,6 +52,28 @@ def test_kernel_names_follow_the_backend(ref):
     assert att.qk_norm_rope_kv.__b200__ is qk_norm_rope_kv.qk_norm_rope_kv
 
 
+def test_attention_layer_routes(ref):
+    """The plain KV-cache write and decode attention of layers/attention.py resolve to the b200 kernels for "b200";
+    decode calls the b200 kernel does not take keep flash-attn's function."""
+    import torch
+    import nanovllm.layers.attention as att
+    from nanovllm_b200.kernels import attention
+    assert att.store_kvcache.__b200__ is attention.store_kvcache
+    assert att.flash_attn_with_kvcache.__b200__ is attention.flash_attn_with_kvcache
+    q = torch.zeros(2, 1, 16, 128, dtype=torch.bfloat16)
+    cache = torch.zeros(4, 256, 8, 128, dtype=torch.bfloat16)
+    table = torch.zeros(2, 2, dtype=torch.int32)
+    lens = torch.ones(2, dtype=torch.int32)
+    kw = dict(cache_seqlens=lens, block_table=table, softmax_scale=0.1, causal=True)
+    assert attention.supports(q, cache, cache, **kw)                      # the decode branch's call
+    assert not attention.supports(q.float(), cache.float(), cache.float(), **kw)
+    assert not attention.supports(q[..., :64], cache[..., :64], cache[..., :64], **kw)
+    assert not attention.supports(torch.zeros(2, 9, 16, 128, dtype=torch.bfloat16), cache, cache, **kw)  # 18 rows
+    assert not attention.supports(q, cache, cache, window_size=(8, 0), **kw)
+    with pytest.raises(NotImplementedError):
+        attention.flash_attn_with_kvcache(q, cache, cache, return_softmax_lse=True, **kw)
+
+
 def test_qwen3_attention_is_fused_for_b200(ref):
     import torch
     import torch.distributed as dist
