@@ -7,9 +7,11 @@
 // the kernel is organised around the stream:
 //   * grid (splits, Hkv, batch); a thread-block cluster of `splits` CTAs shares one (sequence, KV head) and each
 //     CTA takes a contiguous share of its keys, in 16-token tiles;
-//   * each of a CTA's 4 warps streams every 4th tile through its own 3-stage cp.async ring (16-byte copies of whole
-//     256-byte K and V rows, looked up token by token through the block table; rows past the share are zero-filled),
-//     so no CTA-wide barrier sits in the loop;
+//   * each of a CTA's 4 warps streams every 4th tile through its own cp.async ring (2 stages: one tile in flight while
+//     one is consumed; 16-byte copies of whole 256-byte K and V rows, looked up token by token through the block
+//     table; rows past the share are zero-filled), so no CTA-wide barrier sits in the loop. At 2 query rows a CTA
+//     holds 66 KB of shared memory and three share an SM (a 3-stage ring measured the same or up to 4 % slower at
+//     two CTAs per SM, a 4-stage ring 25-30 % slower at one);
 //   * q k^T: two lanes per token, each dotting half of the K row (read from a swizzled layout, conflict-free) with
 //     the fp32 query rows held in shared memory (pre-scaled by scale * log2(e), broadcast reads); p v: each lane
 //     owns 4 of the 128 output columns and reads V rows and the tile's probabilities from shared memory;
@@ -28,15 +30,24 @@
 namespace nvb200 {
 namespace {
 
-constexpr int kAttnWarps = 4;
+// Warps per CTA and cp.async ring depth per warp (build-time: -DNVB200_ATTN_WARPS=..., -DNVB200_ATTN_STAGES=...).
+#ifndef NVB200_ATTN_WARPS
+#define NVB200_ATTN_WARPS 4
+#endif
+#ifndef NVB200_ATTN_STAGES
+#define NVB200_ATTN_STAGES 2
+#endif
+constexpr int kAttnWarps = NVB200_ATTN_WARPS;
 constexpr int kAttnThreads = kAttnWarps * 32;
 constexpr int kHeadDim = 128;
+// The merges give thread d output column d (and the partial pushes address records by thread index).
+static_assert(kAttnThreads == kHeadDim, "one thread per output column: 4 warps at head_dim 128");
 constexpr int kRowBytes = kHeadDim * 2;                          // one bf16 K or V row
 constexpr int kTileTokens = 16;                                  // keys per warp tile
 constexpr int kTileBytes = kTileTokens * kRowBytes;              // 4 KB of K (or of V)
-constexpr int kStages = 3;                                       // cp.async ring depth per warp
+constexpr int kStages = NVB200_ATTN_STAGES;                      // cp.async ring depth per warp
 constexpr int kStageBytes = 2 * kTileBytes;                      // the K tile, then the V tile
-constexpr int kRingBytes = kAttnWarps * kStages * kStageBytes;   // 96 KB
+constexpr int kRingBytes = kAttnWarps * kStages * kStageBytes;   // 64 KB at 4 warps x 2 stages
 constexpr int kMaxRows = 16;                                     // query rows per KV head (queries x group)
 constexpr int kMaxSplits = 8;                                    // portable cluster size
 constexpr int kStateStride = 132;  // floats per partial-state record: o[128], running max, running sum, 2 pad
@@ -106,8 +117,14 @@ NVB200_DEVICE int k_chunk(int t, int c) { return c ^ (t & 7) ^ ((c >> 3) << 2); 
 // reading half 0 and half 1 of a chunk hit different banks.
 NVB200_DEVICE int q_index(int r, int d) { return (r * 8 + ((d >> 3) & 7)) * 16 + (d >> 6) * 8 + (d & 7); }
 
+constexpr int smem_bytes(int R) { return kRingBytes + R * kHeadDim * 4 + kAttnWarps * kTileTokens * R * 4; }
+// CTAs per SM at the largest row count (228 KB of shared memory per SM, 1 KB reserved per CTA).
+constexpr int kSmemPerSm = 228 * 1024;
+constexpr int kFitBlocks = kSmemPerSm / (smem_bytes(kMaxRows) + 1024);
+constexpr int kMinBlocks = kFitBlocks > 0 ? kFitBlocks : 1;
+
 template <int R>
-__global__ void __launch_bounds__(kAttnThreads, 2) paged_decode_kernel(const __grid_constant__ AttnParams p) {
+__global__ void __launch_bounds__(kAttnThreads, kMinBlocks) paged_decode_kernel(const __grid_constant__ AttnParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int h = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -165,8 +182,9 @@ __global__ void __launch_bounds__(kAttnThreads, 2) paged_decode_kernel(const __g
     float x = 0.f;
     if (r < p.rows) {
       const int qi = r / p.group, g = r - qi * p.group;
-      x = __bfloat162float(p.q[static_cast<int64_t>(b) * p.q_batch_stride + static_cast<int64_t>(qi) * p.q_token_stride +
-                               (static_cast<int64_t>(h) * p.group + g) * p.q_head_stride + d]) * p.scale_log2;
+      const int64_t at = static_cast<int64_t>(b) * p.q_batch_stride + static_cast<int64_t>(qi) * p.q_token_stride +
+                         (static_cast<int64_t>(h) * p.group + g) * p.q_head_stride + d;
+      x = __bfloat162float(p.q[at]) * p.scale_log2;
     }
     q_s[q_index(r, d)] = x;
   }
@@ -276,7 +294,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2) paged_decode_kernel(const __g
 #pragma unroll
     for (int off = 1; off < 32; off <<= 1) l[r] += __shfl_xor_sync(0xffffffffu, l[r], off);
   }
-  __syncthreads();  // every warp is done with its ring: the state records below reuse it
+  __syncthreads();  // every warp is done with its ring, queries and probabilities: the records below reuse them
 
   // Merge the warps: record (o, m, l) per warp and row, then thread d combines column d.
   float *rec = reinterpret_cast<float *>(smem);  // [kAttnWarps][R][kStateStride]
@@ -349,10 +367,13 @@ __global__ void __launch_bounds__(kAttnThreads, 2) paged_decode_kernel(const __g
   }
 }
 
-constexpr int smem_bytes(int R) { return kRingBytes + R * kHeadDim * 4 + kAttnWarps * kTileTokens * R * 4; }
-static_assert(kAttnWarps * kMaxRows * kStateStride * 4 <= kRingBytes, "warp records must fit in the ring");
-static_assert(kMaxSplits * kMaxRows * kStateStride * 4 <= kRingBytes, "cluster partials must fit in the ring");
-static_assert(2 * (smem_bytes(kMaxRows) + 1024) <= 228 * 1024, "two CTAs per SM at the largest row count");
+// The merge records (per warp, then per cluster CTA) reuse the whole dynamic shared memory; both grow linearly in R,
+// as the shared memory does, so fitting at the largest R means fitting at every R.
+static_assert(kAttnWarps * kMaxRows * kStateStride * 4 <= smem_bytes(kMaxRows), "warp records must fit");
+static_assert(kMaxSplits * kMaxRows * kStateStride * 4 <= smem_bytes(kMaxRows), "cluster partials must fit");
+static_assert(kAttnWarps * kStateStride * 4 <= kRingBytes && kMaxSplits * kStateStride * 4 <= kRingBytes,
+              "records of one row fit in the ring (so they fit at every R once they fit at the largest)");
+static_assert(smem_bytes(kMaxRows) <= 227 * 1024, "a CTA's shared memory");
 
 template <int R> int launch_rows(const AttnParams &p, int batch, int hkv, cudaStream_t stream) {
   static std::atomic<int> configured[64];
