@@ -235,6 +235,20 @@ NVB200_API int nvb200_paged_decode_attention(const nvb200_paged_decode_args *arg
 NVB200_API int nvb200_paged_decode_splits(int32_t batch, int32_t num_kv_heads, int32_t max_blocks_per_seq,
                                           int32_t block_size, int32_t num_splits);
 
+/* The same attention (same arguments, same results within rounding) with the work split evenly over every SM: a
+ * persistent grid of as many CTAs as are resident at once, each taking an equal share of all (sequence, KV head,
+ * 16-key tile) units of the batch, so that SMs stay equally loaded whatever the number of (sequence, head) pairs.
+ * A pair split between CTAs is merged by the last of them to finish, through the workspace. num_splits is ignored.
+ * Replaces: the same flash_attn_with_kvcache call of nanovllm/layers/attention.py:84-91.
+ *   workspace: device memory of at least nvb200_paged_decode_workspace_size(args) bytes, 256-byte aligned, zero-filled
+ *     before its first use; each call leaves its counters at zero again, so it is zeroed once, not per call. Calls
+ *     that may run at the same time (different streams) need separate workspaces.
+ * Returns NVB200_ERR_ARG for a missing or short workspace, NVB200_ERR_UNSUPPORTED where the plain entry point does
+ * and when batch * num_kv_heads * (max_blocks_per_seq * block_size / 16) reaches 2^31. */
+NVB200_API int64_t nvb200_paged_decode_workspace_size(const nvb200_paged_decode_args *args);
+NVB200_API int nvb200_paged_decode_attention_streamk(const nvb200_paged_decode_args *args, void *workspace,
+                                                     int64_t workspace_bytes, nvb200_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -123,6 +123,152 @@ constexpr int kSmemPerSm = 228 * 1024;
 constexpr int kFitBlocks = kSmemPerSm / (smem_bytes(kMaxRows) + 1024);
 constexpr int kMinBlocks = kFitBlocks > 0 ? kFitBlocks : 1;
 
+// Online-softmax state of one warp over R query rows (base 2, scores pre-scaled by scale * log2 e). Lane 2t + half
+// scores key t of a tile against half `half` of each query row; o[r][e] is output column 4 * lane + e of row r;
+// l[r] is the lane's share of row r's sum (lanes with half = 0 count their key), summed over the warp at the end.
+template <int R> struct WarpSoftmax {
+  float m[R], l[R], o[R][4];
+  NVB200_DEVICE void reset() {
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      m[r] = -INFINITY, l[r] = 0.f;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) o[r][e] = 0.f;
+    }
+  }
+  // Sums the lanes' shares of the row sums (every lane ends with the warp's total).
+  NVB200_DEVICE void reduce_sums() {
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) l[r] += __shfl_xor_sync(0xffffffffu, l[r], off);
+    }
+  }
+};
+
+// Last key (inclusive) each query row may see in a sequence of L keys: row r is query r / group of sq.
+template <int R>
+NVB200_DEVICE void row_limits(int64_t (&lim)[R], int64_t L, int rows, int group, int sq, int causal) {
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int qi = r < rows ? r / group : sq - 1;
+    lim[r] = causal ? L - sq + qi : L - 1;
+  }
+}
+
+// Folds one 16-key tile into the warp's state: kt is the ring stage (K tile, then V tile, both landed and visible to
+// the whole warp), q_addr the fp32 query block, p_w / p_addr the warp's [kTileTokens][R] probability scratch. j0 is
+// the index of the tile's first key; keys at or past je, or past a row's limit, get probability zero. Ends with a
+// __syncwarp, after which the stage and p_w may be refilled.
+template <int R>
+NVB200_DEVICE void fold_tile(WarpSoftmax<R> &st, uint32_t kt, uint32_t q_addr, float *p_w, uint32_t p_addr, int lane,
+                             int64_t j0, int64_t je, const int64_t (&lim)[R]) {
+  const int t = lane >> 1, half = lane & 1;
+  // Scores of key t against every query row, half of the row per lane.
+  float s[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) s[r] = 0.f;
+  const uint32_t krow = kt + t * kRowBytes;
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    float kf[8];
+    unpack8(ld_shared_v4(krow + k_chunk(t, half * 8 + c) * 16), kf);
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const uint32_t qa = q_addr + ((r * 8 + c) * 16 + half * 8) * 4;
+      const float4 x = ld_shared_f4(qa), y = ld_shared_f4(qa + 16);
+      float acc = s[r];
+      acc = fmaf(kf[0], x.x, acc), acc = fmaf(kf[1], x.y, acc), acc = fmaf(kf[2], x.z, acc);
+      acc = fmaf(kf[3], x.w, acc), acc = fmaf(kf[4], y.x, acc), acc = fmaf(kf[5], y.y, acc);
+      acc = fmaf(kf[6], y.z, acc), acc = fmaf(kf[7], y.w, acc);
+      s[r] = acc;
+    }
+  }
+  const int64_t j = j0 + t;
+  float alpha[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    float sc = s[r] + __shfl_xor_sync(0xffffffffu, s[r], 1);
+    if (j >= je || j > lim[r]) sc = -INFINITY;
+    float mt = sc;
+    mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 2));
+    mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 4));
+    mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 8));
+    mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 16));
+    const float mn = fmaxf(st.m[r], mt);
+    const float mu = mn == -INFINITY ? 0.f : mn;  // no key seen yet: any finite reference keeps exp2 at 0
+    alpha[r] = exp2f(st.m[r] - mu);
+    st.m[r] = mn;
+    const float pr = exp2f(sc - mu);
+    st.l[r] = fmaf(st.l[r], alpha[r], half ? 0.f : pr);  // one lane of the pair counts the key
+    if (half == (r & 1)) p_w[t * R + r] = pr;
+  }
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) st.o[r][e] *= alpha[r];
+  }
+  __syncwarp();  // the tile's probabilities are in p_w
+
+  const uint32_t vt = kt + kTileBytes + lane * 8;
+#pragma unroll 4
+  for (int tt = 0; tt < kTileTokens; ++tt) {
+    const uint2 vv = ld_shared_v2(vt + tt * kRowBytes);
+    const float v0 = bf16_lo(vv.x), v1 = bf16_hi(vv.x), v2 = bf16_lo(vv.y), v3 = bf16_hi(vv.y);
+    float pr[R];
+    const uint32_t pa = p_addr + tt * R * 4;
+    if constexpr (R >= 4) {
+#pragma unroll
+      for (int r = 0; r < R; r += 4) {
+        const float4 x = ld_shared_f4(pa + r * 4);
+        pr[r] = x.x, pr[r + 1] = x.y, pr[r + 2] = x.z, pr[r + 3] = x.w;
+      }
+    } else if constexpr (R == 2) {
+      const float2 x = ld_shared_f2(pa);
+      pr[0] = x.x, pr[1] = x.y;
+    } else {
+      pr[0] = ld_shared_f1(pa);
+    }
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      st.o[r][0] = fmaf(pr[r], v0, st.o[r][0]), st.o[r][1] = fmaf(pr[r], v1, st.o[r][1]);
+      st.o[r][2] = fmaf(pr[r], v2, st.o[r][2]), st.o[r][3] = fmaf(pr[r], v3, st.o[r][3]);
+    }
+  }
+  __syncwarp();  // every lane is done with this stage and p_w before they are refilled
+}
+
+// Writes the warp's (o, m, l) per row into records rec[warp][R][kStateStride] (after reduce_sums).
+template <int R> NVB200_DEVICE void store_warp_record(const WarpSoftmax<R> &st, float *rec, int warp, int lane) {
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    float *w = rec + (warp * R + r) * kStateStride;
+    *reinterpret_cast<float4 *>(w + 4 * lane) = make_float4(st.o[r][0], st.o[r][1], st.o[r][2], st.o[r][3]);
+    if (lane == 0) w[kHeadDim] = st.m[r], w[kHeadDim + 1] = st.l[r];
+  }
+}
+
+// Thread d merges column d of the CTA's warp records: unnormalised output oc, max mc and sum lc per row.
+template <int R>
+NVB200_DEVICE void merge_warp_records(const float *rec, int tid, float (&oc)[R], float (&mc)[R], float (&lc)[R]) {
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    float mx = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kAttnWarps; ++w) mx = fmaxf(mx, rec[(w * R + r) * kStateStride + kHeadDim]);
+    const float mu = mx == -INFINITY ? 0.f : mx;
+    float acc = 0.f, sum = 0.f;
+#pragma unroll
+    for (int w = 0; w < kAttnWarps; ++w) {
+      const float *x = rec + (w * R + r) * kStateStride;
+      const float sc = exp2f(x[kHeadDim] - mu);
+      acc = fmaf(sc, x[tid], acc);
+      sum = fmaf(sc, x[kHeadDim + 1], sum);
+    }
+    oc[r] = acc, mc[r] = mx, lc[r] = sum;
+  }
+}
+
 template <int R>
 __global__ void __launch_bounds__(kAttnThreads, kMinBlocks) paged_decode_kernel(const __grid_constant__ AttnParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
@@ -190,138 +336,29 @@ __global__ void __launch_bounds__(kAttnThreads, kMinBlocks) paged_decode_kernel(
   }
   __syncthreads();
 
-  // Last key each row may see (inclusive).
   int64_t lim[R];
-#pragma unroll
-  for (int r = 0; r < R; ++r) {
-    const int qi = r < p.rows ? r / p.group : p.sq - 1;
-    lim[r] = p.causal ? L - p.sq + qi : L - 1;
-  }
-
-  float m[R], l[R], o[R][4];
-#pragma unroll
-  for (int r = 0; r < R; ++r) {
-    m[r] = -INFINITY, l[r] = 0.f;
-#pragma unroll
-    for (int e = 0; e < 4; ++e) o[r][e] = 0.f;
-  }
-  const int t = lane >> 1, half = lane & 1;
+  row_limits<R>(lim, L, p.rows, p.group, p.sq, p.causal);
+  WarpSoftmax<R> st;
+  st.reset();
 
   for (int i = 0; i < my_tiles; ++i) {
     if (i + kStages - 1 < my_tiles) issue(i + kStages - 1, (i + kStages - 1) % kStages);
     cp_async_commit();
     cp_async_wait<kStages - 1>();  // this lane's copies of tile i have landed
     __syncwarp();                  // ... and every other lane's
-    const uint32_t kt = wring + (i % kStages) * kStageBytes;
-
-    // Scores of key t against every query row, half of the row per lane.
-    float s[R];
-#pragma unroll
-    for (int r = 0; r < R; ++r) s[r] = 0.f;
-    const uint32_t krow = kt + t * kRowBytes;
-#pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      float kf[8];
-      unpack8(ld_shared_v4(krow + k_chunk(t, half * 8 + c) * 16), kf);
-#pragma unroll
-      for (int r = 0; r < R; ++r) {
-        const uint32_t qa = q_addr + ((r * 8 + c) * 16 + half * 8) * 4;
-        const float4 x = ld_shared_f4(qa), y = ld_shared_f4(qa + 16);
-        float acc = s[r];
-        acc = fmaf(kf[0], x.x, acc), acc = fmaf(kf[1], x.y, acc), acc = fmaf(kf[2], x.z, acc);
-        acc = fmaf(kf[3], x.w, acc), acc = fmaf(kf[4], y.x, acc), acc = fmaf(kf[5], y.y, acc);
-        acc = fmaf(kf[6], y.z, acc), acc = fmaf(kf[7], y.w, acc);
-        s[r] = acc;
-      }
-    }
-    const int64_t j = js + static_cast<int64_t>(warp + i * kAttnWarps) * kTileTokens + t;
-    float alpha[R];
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-      float sc = s[r] + __shfl_xor_sync(0xffffffffu, s[r], 1);
-      if (j >= je || j > lim[r]) sc = -INFINITY;
-      float mt = sc;
-      mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 2));
-      mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 4));
-      mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 8));
-      mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 16));
-      const float mn = fmaxf(m[r], mt);
-      const float mu = mn == -INFINITY ? 0.f : mn;  // no key seen yet: any finite reference keeps exp2 at 0
-      alpha[r] = exp2f(m[r] - mu);
-      m[r] = mn;
-      const float pr = exp2f(sc - mu);
-      l[r] = fmaf(l[r], alpha[r], half ? 0.f : pr);  // one lane of the pair counts the key
-      if (half == (r & 1)) p_w[t * R + r] = pr;
-    }
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-#pragma unroll
-      for (int e = 0; e < 4; ++e) o[r][e] *= alpha[r];
-    }
-    __syncwarp();  // the tile's probabilities are in p_w
-
-    const uint32_t vt = kt + kTileBytes + lane * 8;
-#pragma unroll 4
-    for (int tt = 0; tt < kTileTokens; ++tt) {
-      const uint2 vv = ld_shared_v2(vt + tt * kRowBytes);
-      const float v0 = bf16_lo(vv.x), v1 = bf16_hi(vv.x), v2 = bf16_lo(vv.y), v3 = bf16_hi(vv.y);
-      float pr[R];
-      const uint32_t pa = p_addr + tt * R * 4;
-      if constexpr (R >= 4) {
-#pragma unroll
-        for (int r = 0; r < R; r += 4) {
-          const float4 x = ld_shared_f4(pa + r * 4);
-          pr[r] = x.x, pr[r + 1] = x.y, pr[r + 2] = x.z, pr[r + 3] = x.w;
-        }
-      } else if constexpr (R == 2) {
-        const float2 x = ld_shared_f2(pa);
-        pr[0] = x.x, pr[1] = x.y;
-      } else {
-        pr[0] = ld_shared_f1(pa);
-      }
-#pragma unroll
-      for (int r = 0; r < R; ++r) {
-        o[r][0] = fmaf(pr[r], v0, o[r][0]), o[r][1] = fmaf(pr[r], v1, o[r][1]);
-        o[r][2] = fmaf(pr[r], v2, o[r][2]), o[r][3] = fmaf(pr[r], v3, o[r][3]);
-      }
-    }
-    __syncwarp();  // every lane is done with this stage and p_w before they are refilled
+    fold_tile<R>(st, wring + (i % kStages) * kStageBytes, q_addr, p_w, p_addr, lane,
+                 js + static_cast<int64_t>(warp + i * kAttnWarps) * kTileTokens, je, lim);
   }
   cp_async_wait<0>();
-
-#pragma unroll
-  for (int r = 0; r < R; ++r) {
-#pragma unroll
-    for (int off = 1; off < 32; off <<= 1) l[r] += __shfl_xor_sync(0xffffffffu, l[r], off);
-  }
+  st.reduce_sums();
   __syncthreads();  // every warp is done with its ring, queries and probabilities: the records below reuse them
 
   // Merge the warps: record (o, m, l) per warp and row, then thread d combines column d.
   float *rec = reinterpret_cast<float *>(smem);  // [kAttnWarps][R][kStateStride]
-#pragma unroll
-  for (int r = 0; r < R; ++r) {
-    float *w = rec + (warp * R + r) * kStateStride;
-    *reinterpret_cast<float4 *>(w + 4 * lane) = make_float4(o[r][0], o[r][1], o[r][2], o[r][3]);
-    if (lane == 0) w[kHeadDim] = m[r], w[kHeadDim + 1] = l[r];
-  }
+  store_warp_record<R>(st, rec, warp, lane);
   __syncthreads();
   float oc[R], mc[R], lc[R];
-#pragma unroll
-  for (int r = 0; r < R; ++r) {
-    float mx = -INFINITY;
-#pragma unroll
-    for (int w = 0; w < kAttnWarps; ++w) mx = fmaxf(mx, rec[(w * R + r) * kStateStride + kHeadDim]);
-    const float mu = mx == -INFINITY ? 0.f : mx;
-    float acc = 0.f, sum = 0.f;
-#pragma unroll
-    for (int w = 0; w < kAttnWarps; ++w) {
-      const float *x = rec + (w * R + r) * kStateStride;
-      const float sc = exp2f(x[kHeadDim] - mu);
-      acc = fmaf(sc, x[tid], acc);
-      sum = fmaf(sc, x[kHeadDim + 1], sum);
-    }
-    oc[r] = acc, mc[r] = mx, lc[r] = sum;
-  }
+  merge_warp_records<R>(rec, tid, oc, mc, lc);
 
   auto write_row = [&](int r, float acc, float sum) {
     if (r >= p.rows) return;
@@ -375,6 +412,352 @@ static_assert(kAttnWarps * kStateStride * 4 <= kRingBytes && kMaxSplits * kState
               "records of one row fit in the ring (so they fit at every R once they fit at the largest)");
 static_assert(smem_bytes(kMaxRows) <= 227 * 1024, "a CTA's shared memory");
 
+// ---------------------------------------------------------------------------------------------------------------
+// Stream-K form. The work of one call is a sequence of units (sequence b, KV head h, 16-key tile), ordered by b, then
+// h, then tile; sequence b has T_b = ceil(L_b / 16) tiles per head, so U = Hkv * sum_b T_b units in all. A persistent
+// grid of G CTAs (as many as are resident at once) gives CTA c the units [c U / G, (c + 1) U / G): every SM gets the
+// same number of tiles whatever the batch shape, where one CTA per (sequence, head) leaves some SMs with one CTA
+// and others with two. A CTA walks its range one segment (the units of one (b, h)) at a time; its warps split each
+// segment's tiles (warp w takes every 4th) and keep their cp.async rings running across segment ends, so a new
+// segment's first tiles are in flight while the last one is merged. A segment that is a whole (b, h) writes its
+// output rows directly. A (b, h) split between CTAs (only the first and last segment of a range can be) leaves one
+// partial record (o, m, l per row) per CTA in the workspace; each such CTA then takes a ticket from the (b, h)'s
+// arrival counter and the last to arrive merges the records in CTA order (so results do not depend on timing) and
+// resets the counter to zero. No CTA waits for another.
+//
+// Workspace: counters int32 [batch * Hkv] at offset 0 (zero before the first call; every call leaves them zero), then
+// at kCounterAlign-rounded offset the partial records fp32 [2 * grid][R][kStateStride] (CTA c writes slots 2c and 2c+1).
+constexpr int64_t kCounterAlign = 256;
+
+struct StreamKParams {
+  int32_t *counters;
+  float *partials;
+  int batch, hkv;
+};
+
+constexpr int streamk_smem_bytes(int R) { return smem_bytes(R) + kAttnWarps * R * kStateStride * 4 + 16; }
+static_assert(streamk_smem_bytes(kMaxRows) <= 227 * 1024, "a stream-K CTA's shared memory");
+// CTAs per SM that the shared memory of R rows allows (the register budget follows it through the launch bounds).
+constexpr int streamk_min_blocks(int R) {
+  return kSmemPerSm / (streamk_smem_bytes(R) + 1024) > 0 ? kSmemPerSm / (streamk_smem_bytes(R) + 1024) : 1;
+}
+
+// Keys of sequence b, clamped to [0, what its block-table row addresses].
+NVB200_DEVICE int64_t seq_keys(const AttnParams &p, int b) {
+  const int64_t L = p.seqlens[b];
+  const int64_t cap = static_cast<int64_t>(p.max_pages) * p.block_size;
+  return L < 0 ? 0 : (L > cap ? cap : L);
+}
+NVB200_DEVICE int64_t tiles_of(int64_t keys) { return (keys + kTileTokens - 1) / kTileTokens; }
+
+// The units of one (b, h) inside one CTA's range. CTA-uniform: every thread of the CTA holds the same values. Unit
+// indices fit in 32 bits (the host checks batch * Hkv * the longest sequence's tiles < 2^31).
+struct Segment {
+  int32_t u;       // global index of the segment's first unit
+  int32_t pair_u;  // global index of unit 0 of (b, h)
+  int32_t pre;     // tiles of the sequences before b (units before b = hkv * pre)
+  int32_t tiles;   // T_b
+  int32_t t0;      // first tile of the segment within (b, h)
+  int32_t n;       // tiles in the segment; 0 = the range is exhausted
+  int32_t b, h;
+  int64_t L;       // keys of sequence b
+
+  // Moves to the next (b, h) of the range [., u1).
+  NVB200_DEVICE void next(const AttnParams &p, int batch, int hkv, int32_t u1) {
+    u += n;
+    if (u >= u1) {
+      n = 0;
+      return;
+    }
+    if (h + 1 < hkv) {
+      ++h;
+    } else {
+      pre += tiles;
+      h = 0;
+      do {
+        ++b;
+        L = seq_keys(p, b);
+        tiles = static_cast<int32_t>(tiles_of(L));
+      } while (tiles == 0 && b + 1 < batch);
+    }
+    pair_u = hkv * pre + h * tiles;
+    t0 = 0;
+    n = min(tiles, u1 - u);
+  }
+  NVB200_DEVICE bool whole() const { return t0 == 0 && n == tiles; }
+};
+
+// First unit of CTA c's range, and the CTA whose range holds unit u (G <= U, so no range is empty).
+NVB200_DEVICE int64_t range_start(int64_t c, int64_t U, int64_t G) { return c * U / G; }
+NVB200_DEVICE int64_t range_owner(int64_t u, int64_t U, int64_t G) { return ((u + 1) * G - 1) / U; }
+// Partial-record slot of CTA c for the (b, h) whose unit 0 is pair_u: 2c if (b, h) holds c's first unit, else 2c + 1
+// (then it is c's last segment).
+NVB200_DEVICE int64_t partial_slot(int64_t c, int64_t pair_u, int64_t U, int64_t G) {
+  return 2 * c + (pair_u <= range_start(c, U, G) ? 0 : 1);
+}
+
+NVB200_DEVICE long long warp_sum_i64(long long x) {
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) x += __shfl_xor_sync(0xffffffffu, x, off);
+  return x;
+}
+NVB200_DEVICE long long warp_inclusive_scan_i64(long long x, int lane) {
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const long long y = __shfl_up_sync(0xffffffffu, x, off);
+    if (lane >= off) x += y;
+  }
+  return x;
+}
+
+template <int R>
+__global__ void __launch_bounds__(kAttnThreads, streamk_min_blocks(R))
+    paged_decode_streamk_kernel(const __grid_constant__ AttnParams p, const __grid_constant__ StreamKParams sk) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  float *q_s = reinterpret_cast<float *>(smem + kRingBytes);
+  float *p_w = q_s + R * kHeadDim + warp * kTileTokens * R;
+  float *rec = q_s + R * kHeadDim + kAttnWarps * kTileTokens * R;  // [kAttnWarps][R][kStateStride]
+  long long *meta = reinterpret_cast<long long *>(rec + kAttnWarps * R * kStateStride);  // [2]: U, then a flag
+  const uint32_t q_addr = smem_addr(q_s), p_addr = smem_addr(p_w);
+  const uint32_t wring = smem_addr(smem) + warp * (kStages * kStageBytes);
+  const int hkv = sk.hkv, batch = sk.batch;
+
+  auto write_row = [&](int b, int h, int r, float acc, float sum) {
+    if (r >= p.rows) return;
+    const int qi = r / p.group, g = r - qi * p.group;
+    const int64_t idx = ((static_cast<int64_t>(b) * p.sq + qi) * p.hq + static_cast<int64_t>(h) * p.group + g) *
+                        kHeadDim + tid;
+    p.out[idx] = __float2bfloat16_rn(sum > 0.f ? acc / sum : 0.f);
+  };
+
+  // Sequences without keys own no units: their rows are zeros, written by CTA (b * hkv + h) mod grid.
+  for (int64_t pr = blockIdx.x; pr < static_cast<int64_t>(batch) * hkv; pr += gridDim.x) {
+    const int b = static_cast<int>(pr / hkv), h = static_cast<int>(pr - static_cast<int64_t>(b) * hkv);
+    if (seq_keys(p, b) == 0) {
+      for (int r = 0; r < p.rows; ++r) write_row(b, h, r, 0.f, 0.f);
+    }
+  }
+
+  // U, by warp 0 (CTA 0 also flags lengths outside [0, what the block table addresses]).
+  if (warp == 0) {
+    long long tot = 0;
+    bool bad = false;
+    const int64_t cap = static_cast<int64_t>(p.max_pages) * p.block_size;
+    for (int b0 = 0; b0 < batch; b0 += 32) {
+      const int b = b0 + lane;
+      long long t = 0;
+      if (b < batch) {
+        const int64_t raw = p.seqlens[b];
+        bad |= raw < 0 || raw > cap;
+        t = tiles_of(seq_keys(p, b));
+      }
+      tot += warp_sum_i64(t);
+    }
+    if (blockIdx.x == 0 && __any_sync(0xffffffffu, bad) && lane == 0) set_status(p.status, NVB200_STATUS_BAD_SLOT);
+    if (lane == 0) meta[0] = tot * hkv;
+  }
+  __syncthreads();
+  const int64_t U = meta[0];
+  const int64_t G = min(static_cast<int64_t>(gridDim.x), U);
+  const int64_t c = blockIdx.x;
+  if (c >= G) return;
+  const int32_t u0 = static_cast<int32_t>(range_start(c, U, G)), u1 = static_cast<int32_t>(range_start(c + 1, U, G));
+
+  // The segment holding u0: sequence b with hkv * P(b) <= u0 < hkv * P(b + 1), P the tile prefix (every warp scans,
+  // so the result is in every thread's registers without another barrier).
+  Segment seg{};
+  {
+    long long base = 0;
+    for (int b0 = 0; b0 < batch; b0 += 32) {
+      const int b = b0 + lane;
+      const long long t = b < batch ? tiles_of(seq_keys(p, b)) : 0;
+      const long long incl = warp_inclusive_scan_i64(t, lane);
+      const unsigned hit = __ballot_sync(0xffffffffu, b < batch && (base + incl) * hkv > u0);
+      if (hit) {
+        const int first = __ffs(hit) - 1;
+        seg.b = b0 + first;
+        seg.tiles = static_cast<int32_t>(__shfl_sync(0xffffffffu, t, first));
+        seg.pre = static_cast<int32_t>(base + __shfl_sync(0xffffffffu, incl, first)) - seg.tiles;
+        break;
+      }
+      base += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    seg.L = seq_keys(p, seg.b);
+    const int32_t within = u0 - hkv * seg.pre;
+    seg.h = within / seg.tiles;
+    seg.t0 = within - seg.h * seg.tiles;
+    seg.pair_u = hkv * seg.pre + seg.h * seg.tiles;
+    seg.u = u0;
+    seg.n = min(seg.tiles - seg.t0, u1 - u0);
+  }
+
+  // This warp's issue cursor: item i of segment `is` is tile is.t0 + warp + 4 i of (is.b, is.h).
+  Segment is = seg;
+  int ii = 0;
+  auto skip_empty = [&]() {
+    while (is.n > 0 && warp + ii * kAttnWarps >= is.n) {
+      is.next(p, batch, hkv, u1);
+      ii = 0;
+    }
+  };
+  skip_empty();
+  auto issue_next = [&](int stage) {
+    const int64_t j = (is.t0 + warp + static_cast<int64_t>(ii) * kAttnWarps) * kTileTokens + (lane & 15);
+    int64_t off = -1;  // element offset of key j's row for head is.h; -1 = not read (zero-filled)
+    if (j < is.L) {
+      const int64_t page = j / p.block_size;
+      const int64_t blk =
+          p.block_table ? static_cast<int64_t>(__ldg(p.block_table + static_cast<int64_t>(is.b) * p.bt_stride + page))
+                        : is.b;
+      if (blk >= 0 && blk < p.num_blocks)
+        off = blk * p.blk_stride + (j - page * p.block_size) * p.tok_stride +
+              static_cast<int64_t>(is.h) * p.head_stride;
+      else if (lane < 16)
+        set_status(p.status, NVB200_STATUS_BAD_SLOT);
+    }
+    const uint32_t dst = wring + stage * kStageBytes;
+#pragma unroll
+    for (int r2 = 0; r2 < kTileTokens / 2; ++r2) {
+      const int row = r2 * 2 + (lane >> 4), cc = lane & 15;
+      const long long o = __shfl_sync(0xffffffffu, static_cast<long long>(off), row);
+      const bool ok = o >= 0;
+      cp_async16(dst + row * kRowBytes + k_chunk(row, cc) * 16, p.k_cache + (ok ? o + cc * 8 : 0), ok ? 16u : 0u);
+      cp_async16(dst + kTileBytes + row * kRowBytes + cc * 16, p.v_cache + (ok ? o + cc * 8 : 0), ok ? 16u : 0u);
+    }
+    ++ii;
+    skip_empty();
+  };
+#pragma unroll
+  for (int s = 0; s < kStages - 1; ++s) {
+    if (is.n > 0) issue_next(s);
+    cp_async_commit();
+  }
+
+  auto load_q = [&](int b, int h) {
+    for (int i = tid; i < R * kHeadDim; i += kAttnThreads) {
+      const int r = i / kHeadDim, d = i % kHeadDim;
+      float x = 0.f;
+      if (r < p.rows) {
+        const int qi = r / p.group, g = r - qi * p.group;
+        const int64_t at = static_cast<int64_t>(b) * p.q_batch_stride + static_cast<int64_t>(qi) * p.q_token_stride +
+                           (static_cast<int64_t>(h) * p.group + g) * p.q_head_stride + d;
+        x = __bfloat162float(p.q[at]) * p.scale_log2;
+      }
+      q_s[q_index(r, d)] = x;
+    }
+  };
+  load_q(seg.b, seg.h);
+  __syncthreads();
+
+  int g = 0;  // this warp's items consumed so far (ring stage g % kStages)
+  while (seg.n > 0) {
+    const int my = seg.n > warp ? static_cast<int>((seg.n - warp + kAttnWarps - 1) / kAttnWarps) : 0;
+    int64_t lim[R];
+    row_limits<R>(lim, seg.L, p.rows, p.group, p.sq, p.causal);
+    WarpSoftmax<R> st;
+    st.reset();
+    for (int i = 0; i < my; ++i, ++g) {
+      if (is.n > 0) issue_next((g + kStages - 1) % kStages);
+      cp_async_commit();
+      cp_async_wait<kStages - 1>();  // this lane's copies of item g have landed
+      __syncwarp();                  // ... and every other lane's
+      fold_tile<R>(st, wring + (g % kStages) * kStageBytes, q_addr, p_w, p_addr, lane,
+                   (seg.t0 + warp + static_cast<int64_t>(i) * kAttnWarps) * kTileTokens, seg.L, lim);
+    }
+    st.reduce_sums();
+    store_warp_record<R>(st, rec, warp, lane);
+    __syncthreads();  // records complete; every warp is done with the segment's queries
+    float oc[R], mc[R], lc[R];
+    merge_warp_records<R>(rec, tid, oc, mc, lc);
+
+    if (seg.whole()) {
+#pragma unroll
+      for (int r = 0; r < R; ++r) write_row(seg.b, seg.h, r, oc[r], lc[r]);
+    } else {
+      // Publish this CTA's partial, then take a ticket; the last of the (b, h)'s CTAs merges.
+      float *mine = sk.partials + partial_slot(c, seg.pair_u, U, G) * (R * kStateStride);
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        mine[r * kStateStride + tid] = oc[r];
+        if (tid == 0) mine[r * kStateStride + kHeadDim] = mc[r], mine[r * kStateStride + kHeadDim + 1] = lc[r];
+      }
+      __threadfence();
+      __syncthreads();
+      const int64_t pair = static_cast<int64_t>(seg.b) * hkv + seg.h;
+      const int64_t first = range_owner(seg.pair_u, U, G), last = range_owner(seg.pair_u + seg.tiles - 1, U, G);
+      if (tid == 0) {
+        const int ticket = atomicAdd(sk.counters + pair, 1);
+        const bool closing = ticket == static_cast<int>(last - first);
+        if (closing) {
+          sk.counters[pair] = 0;  // every other contributor has taken its ticket
+          __threadfence();
+        }
+        meta[1] = closing ? 1 : 0;
+      }
+      __syncthreads();
+      if (meta[1]) {
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          float mx = -INFINITY;
+          for (int64_t cc = first; cc <= last; ++cc) {
+            const float *x = sk.partials + (partial_slot(cc, seg.pair_u, U, G) * R + r) * kStateStride;
+            mx = fmaxf(mx, __ldcg(x + kHeadDim));
+          }
+          const float mu = mx == -INFINITY ? 0.f : mx;
+          float acc = 0.f, sum = 0.f;
+          for (int64_t cc = first; cc <= last; ++cc) {
+            const float *x = sk.partials + (partial_slot(cc, seg.pair_u, U, G) * R + r) * kStateStride;
+            const float sc = exp2f(__ldcg(x + kHeadDim) - mu);
+            acc = fmaf(sc, __ldcg(x + tid), acc);
+            sum = fmaf(sc, __ldcg(x + kHeadDim + 1), sum);
+          }
+          write_row(seg.b, seg.h, r, acc, sum);
+        }
+      }
+    }
+    seg.next(p, batch, hkv, u1);
+    if (seg.n > 0) load_q(seg.b, seg.h);
+    __syncthreads();  // the next segment's queries are in place; records and the flag may be rewritten
+  }
+  cp_async_wait<0>();
+}
+
+// Rounds v up to a multiple of a.
+constexpr int64_t round_up(int64_t v, int64_t a) { return (v + a - 1) / a * a; }
+
+// Resident CTAs of the stream-K kernel for R rows on the current device (cached per device), times the SM count.
+template <int R> int streamk_grid() {
+  static std::atomic<int> cached[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) return 0;
+  int per_sm = dev < 64 ? cached[dev].load(std::memory_order_acquire) : 0;
+  if (per_sm == 0) {
+    const int smem = streamk_smem_bytes(R);
+    if (cudaFuncSetAttribute(paged_decode_streamk_kernel<R>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+        cudaSuccess)
+      return 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, paged_decode_streamk_kernel<R>, kAttnThreads, smem) !=
+            cudaSuccess ||
+        per_sm <= 0)
+      return 0;
+    if (dev < 64) cached[dev].store(per_sm, std::memory_order_release);
+  }
+  return per_sm * sm_count();
+}
+
+// Bytes of the partial records for `grid` CTAs at R rows.
+constexpr int64_t streamk_partial_bytes(int64_t grid, int R) { return 2 * grid * R * kStateStride * 4; }
+
+template <int R>
+int launch_streamk(const AttnParams &p, int batch, int hkv, int grid, int32_t *counters, float *partials,
+                   cudaStream_t stream) {
+  StreamKParams sk{};
+  sk.counters = counters, sk.partials = partials, sk.batch = batch, sk.hkv = hkv;
+  paged_decode_streamk_kernel<R><<<grid, kAttnThreads, streamk_smem_bytes(R), stream>>>(p, sk);
+  return launch_status();
+}
+
 template <int R> int launch_rows(const AttnParams &p, int batch, int hkv, cudaStream_t stream) {
   static std::atomic<int> configured[64];
   int dev = 0;
@@ -418,7 +801,13 @@ extern "C" int nvb200_paged_decode_splits(int32_t batch, int32_t num_kv_heads, i
   return static_cast<int>(std::max<int64_t>(1, splits));
 }
 
-extern "C" int nvb200_paged_decode_attention(const nvb200_paged_decode_args *a, nvb200_stream_t stream) {
+namespace nvb200 {
+namespace {
+
+// Checks a call's arguments and fills the kernel parameters (splits not set). Returns NVB200_OK with *launch = false
+// for an empty batch (nothing to do), NVB200_OK with *launch = true, or the error code.
+int prepare_decode(const nvb200_paged_decode_args *a, AttnParams &p, bool *launch) {
+  *launch = false;
   if (!a) return NVB200_ERR_ARG;
   if (a->batch < 0 || a->queries_per_seq <= 0 || a->num_q_heads <= 0 || a->num_kv_heads <= 0 || a->head_dim <= 0 ||
       a->block_size <= 0 || a->max_blocks_per_seq <= 0 || a->num_blocks < 0 || a->num_splits < 0 ||
@@ -437,7 +826,7 @@ extern "C" int nvb200_paged_decode_attention(const nvb200_paged_decode_args *a, 
   if (a->batch > 65535 || a->num_kv_heads > 65535) return NVB200_ERR_UNSUPPORTED;
   if (int rc = check_device()) return rc;
 
-  AttnParams p{};
+  p = AttnParams{};
   p.q = static_cast<const __nv_bfloat16 *>(a->q);
   p.q_batch_stride = a->q_batch_stride, p.q_token_stride = a->q_token_stride, p.q_head_stride = a->q_head_stride;
   p.k_cache = static_cast<const __nv_bfloat16 *>(a->k_cache);
@@ -450,14 +839,96 @@ extern "C" int nvb200_paged_decode_attention(const nvb200_paged_decode_args *a, 
   p.sq = a->queries_per_seq, p.hq = a->num_q_heads, p.group = group;
   p.block_size = a->block_size, p.max_pages = a->max_blocks_per_seq, p.rows = static_cast<int>(rows);
   p.causal = a->causal != 0;
-  p.splits = nvb200_paged_decode_splits(a->batch, a->num_kv_heads, a->max_blocks_per_seq, a->block_size,
-                                        a->num_splits);
   p.scale_log2 = static_cast<float>(static_cast<double>(a->softmax_scale) * 1.4426950408889634);
   p.status = a->status;
+  *launch = true;
+  return NVB200_OK;
+}
+
+// Query-row bucket (the kernels' template R) of a call with `rows` rows.
+int row_bucket(int rows) { return rows <= 1 ? 1 : rows <= 2 ? 2 : rows <= 4 ? 4 : rows <= 8 ? 8 : 16; }
+
+int streamk_grid_for(int R) {
+  switch (R) {
+    case 1: return streamk_grid<1>();
+    case 2: return streamk_grid<2>();
+    case 4: return streamk_grid<4>();
+    case 8: return streamk_grid<8>();
+    default: return streamk_grid<16>();
+  }
+}
+
+// Whether the stream-K kernel's unit indices fit: batch * Hkv * tiles of the longest addressable sequence < 2^31.
+bool streamk_fits(const nvb200_paged_decode_args *a) {
+  const int64_t cap_tiles = (static_cast<int64_t>(a->max_blocks_per_seq) * a->block_size + kTileTokens - 1) /
+                            kTileTokens;
+  return static_cast<int64_t>(a->batch) * a->num_kv_heads * cap_tiles < (int64_t{1} << 31);
+}
+
+// Workspace bytes of a stream-K call: the counters, then the partial records for `grid` CTAs at R rows.
+int64_t streamk_workspace_bytes(int64_t batch, int64_t hkv, int64_t grid, int R) {
+  return round_up(batch * hkv * 4, kCounterAlign) + streamk_partial_bytes(grid, R);
+}
+
+int launch_streamk_rows(int R, const AttnParams &p, int batch, int hkv, int grid, int32_t *counters, float *partials,
+                        cudaStream_t s) {
+  switch (R) {
+    case 1: return launch_streamk<1>(p, batch, hkv, grid, counters, partials, s);
+    case 2: return launch_streamk<2>(p, batch, hkv, grid, counters, partials, s);
+    case 4: return launch_streamk<4>(p, batch, hkv, grid, counters, partials, s);
+    case 8: return launch_streamk<8>(p, batch, hkv, grid, counters, partials, s);
+    default: return launch_streamk<16>(p, batch, hkv, grid, counters, partials, s);
+  }
+}
+
+}  // namespace
+}  // namespace nvb200
+
+extern "C" int nvb200_paged_decode_attention(const nvb200_paged_decode_args *a, nvb200_stream_t stream) {
+  AttnParams p;
+  bool launch = false;
+  if (int rc = prepare_decode(a, p, &launch)) return rc;
+  if (!launch) return NVB200_OK;
+  const int64_t rows = p.rows;
+  p.splits = nvb200_paged_decode_splits(a->batch, a->num_kv_heads, a->max_blocks_per_seq, a->block_size,
+                                        a->num_splits);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (rows <= 1) return launch_rows<1>(p, a->batch, a->num_kv_heads, s);
   if (rows <= 2) return launch_rows<2>(p, a->batch, a->num_kv_heads, s);
   if (rows <= 4) return launch_rows<4>(p, a->batch, a->num_kv_heads, s);
   if (rows <= 8) return launch_rows<8>(p, a->batch, a->num_kv_heads, s);
   return launch_rows<16>(p, a->batch, a->num_kv_heads, s);
+}
+
+extern "C" int64_t nvb200_paged_decode_workspace_size(const nvb200_paged_decode_args *a) {
+  if (!a || a->batch < 0 || a->num_kv_heads <= 0 || a->num_q_heads <= 0 || a->queries_per_seq <= 0 ||
+      a->num_q_heads % a->num_kv_heads != 0)
+    return -1;
+  const int64_t rows = static_cast<int64_t>(a->queries_per_seq) * (a->num_q_heads / a->num_kv_heads);
+  if (rows > kMaxRows) return -1;
+  const int R = row_bucket(static_cast<int>(rows));
+  const int grid = streamk_grid_for(R);
+  if (grid <= 0) return -1;
+  return streamk_workspace_bytes(a->batch, a->num_kv_heads, grid, R);
+}
+
+extern "C" int nvb200_paged_decode_attention_streamk(const nvb200_paged_decode_args *a, void *workspace,
+                                                     int64_t workspace_bytes, nvb200_stream_t stream) {
+  AttnParams p;
+  bool launch = false;
+  if (int rc = prepare_decode(a, p, &launch)) return rc;
+  if (!launch) return NVB200_OK;
+  if (!streamk_fits(a)) return NVB200_ERR_UNSUPPORTED;
+  const int R = row_bucket(p.rows);
+  const int grid = streamk_grid_for(R);
+  if (grid <= 0) return NVB200_ERR_CUDA;
+  const int64_t need = streamk_workspace_bytes(a->batch, a->num_kv_heads, grid, R);
+  if (!workspace || (reinterpret_cast<uintptr_t>(workspace) & (kCounterAlign - 1)) != 0 || workspace_bytes < need)
+    return NVB200_ERR_ARG;
+  p.splits = 1;
+  auto *base = static_cast<uint8_t *>(workspace);
+  return launch_streamk_rows(R, p, a->batch, a->num_kv_heads, grid, reinterpret_cast<int32_t *>(base),
+                             reinterpret_cast<float *>(base + round_up(static_cast<int64_t>(a->batch) *
+                                                                        a->num_kv_heads * 4, kCounterAlign)),
+                             reinterpret_cast<cudaStream_t>(stream));
 }

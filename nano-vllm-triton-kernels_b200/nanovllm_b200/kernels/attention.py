@@ -93,6 +93,35 @@ def supports(q, k_cache, v_cache, k=None, v=None, rotary_cos=None, rotary_sin=No
     return True
 
 
+# How flash_attn_with_kvcache runs when the caller leaves num_splits at 0: "cluster" (nvb200_paged_decode_attention:
+# one thread-block cluster per (sequence, KV head)) or "streamk" (nvb200_paged_decode_attention_streamk: a persistent
+# grid with equal shares of all tiles, merging split pairs through a per-device workspace).
+DEFAULT_METHOD = "cluster"
+
+# One workspace per device for the stream-K kernel: zeroed once at allocation (the kernel leaves its counters at
+# zero), sized generously so that it rarely grows. Calls on one device share it, which is safe for calls ordered on
+# one stream (nano-vllm runs one stream per rank); a workspace replaced by a larger one is kept alive, since a
+# captured CUDA graph may still use it.
+_MIN_WORKSPACE_BYTES = 8 << 20
+_workspaces = {}
+_retired = []
+
+
+def _decode_workspace(device: torch.device, nbytes: int):
+    """This device's stream-K workspace with at least nbytes, or None when it would have to be allocated while a
+    CUDA graph is being captured (a buffer allocated there belongs to the graph's pool)."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    ws = _workspaces.get(idx)
+    if ws is None or ws.numel() < nbytes:
+        if torch.cuda.is_current_stream_capturing():
+            return None
+        fresh = torch.zeros(max(nbytes, _MIN_WORKSPACE_BYTES), dtype=torch.uint8, device=torch.device("cuda", idx))
+        if ws is not None:
+            _retired.append(ws)
+        _workspaces[idx] = ws = fresh
+    return ws
+
+
 def flash_attn_with_kvcache(q, k_cache, v_cache, k=None, v=None, rotary_cos=None, rotary_sin=None,
                             cache_seqlens=None, cache_batch_idx=None, cache_leftpad=None, block_table=None,
                             softmax_scale=None, causal=False, window_size=(-1, -1), softcap=0.0,
@@ -100,15 +129,29 @@ def flash_attn_with_kvcache(q, k_cache, v_cache, k=None, v=None, rotary_cos=None
     """Decode attention over a paged KV cache. q: [B, n, Hq, D]; k_cache, v_cache: [num_blocks, block_size, Hkv, D]
     (with block_table [B, max_blocks] int32) or [B, max_len, Hkv, D] (without); cache_seqlens: [B] int32 or an int,
     the keys in the cache per sequence. softmax_scale defaults to D ** -0.5; causal aligns query i of n with key
-    L - n + i. num_splits: CTAs sharing one sequence (0 = chosen from the sizes, at most 8). Returns
-    [B, n, Hq, D]."""
-    if isinstance(cache_seqlens, int):
-        cache_seqlens = torch.full((q.shape[0],), cache_seqlens, dtype=torch.int32, device=q.device)
+    L - n + i. num_splits: CTAs of one thread-block cluster sharing one sequence (1-8, the cluster kernel); 0 = the
+    module's DEFAULT_METHOD with its own split choice. Returns [B, n, Hq, D]."""
     if not supports(q, k_cache, v_cache, k, v, rotary_cos, rotary_sin, cache_seqlens, cache_batch_idx,
                     cache_leftpad, block_table, softmax_scale, causal, window_size, softcap, rotary_interleaved,
                     alibi_slopes, num_splits, return_softmax_lse):
         raise NotImplementedError("nanovllm_b200 flash_attn_with_kvcache: only the decode form (bf16, head_dim 128, "
                                   "n * Hq / Hkv <= 16, no new k/v, rotary, window, softcap, ALiBi or lse) is built")
+    method = "cluster" if num_splits and num_splits > 0 else DEFAULT_METHOD
+    return decode_attention(q, k_cache, v_cache, cache_seqlens, block_table=block_table, softmax_scale=softmax_scale,
+                            causal=causal, num_splits=num_splits, method=method)
+
+
+def decode_attention(q, k_cache, v_cache, cache_seqlens, block_table=None, softmax_scale=None, causal=False,
+                     num_splits=0, method="cluster"):
+    """flash_attn_with_kvcache's decode form with the kernel named: method "cluster" (num_splits CTAs per sequence,
+    0 = automatic) or "streamk" (num_splits ignored). A stream-K call made while a CUDA graph is being captured,
+    before this device's workspace exists, runs the cluster kernel (make one call before capturing)."""
+    if method not in ("cluster", "streamk"):
+        raise ValueError(f"decode_attention: unknown method {method!r}")
+    if isinstance(cache_seqlens, int):
+        cache_seqlens = torch.full((q.shape[0],), cache_seqlens, dtype=torch.int32, device=q.device)
+    if not supports(q, k_cache, v_cache, cache_seqlens=cache_seqlens, block_table=block_table):
+        raise NotImplementedError("nanovllm_b200 decode_attention: bf16, head_dim 128, n * Hq / Hkv <= 16")
     B, n, hq, d = q.shape
     nb, bs, hkv, _ = k_cache.shape
     _require(q.device.type == "cuda" and k_cache.device == q.device, "q and the caches must be on one CUDA device")
@@ -136,7 +179,17 @@ def flash_attn_with_kvcache(q, k_cache, v_cache, k=None, v=None, rotary_cos=None
     a.causal, a.num_splits, a.dtype = int(bool(causal)), max(0, int(num_splits)), _lib.BF16
     a.softmax_scale = scale
     a.status = _lib.status_word(q.device).data_ptr()
-    _lib.check(_lib.lib().nvb200_paged_decode_attention(ctypes.byref(a), _lib.stream_of(q)), "flash_attn_with_kvcache")
+    L = _lib.lib()
+    if method == "streamk":
+        need = L.nvb200_paged_decode_workspace_size(ctypes.byref(a))
+        _require(need > 0, "decode_attention: no stream-K launch shape for these sizes")
+        ws = _decode_workspace(q.device, need)
+        if ws is not None:
+            a.num_splits = 0
+            _lib.check(L.nvb200_paged_decode_attention_streamk(ctypes.byref(a), ws.data_ptr(), ws.numel(),
+                                                               _lib.stream_of(q)), "decode_attention (stream-K)")
+            return out
+    _lib.check(L.nvb200_paged_decode_attention(ctypes.byref(a), _lib.stream_of(q)), "flash_attn_with_kvcache")
     return out
 
 
@@ -145,4 +198,4 @@ def decode_splits(batch: int, num_kv_heads: int, max_blocks_per_seq: int, block_
     return _lib.lib().nvb200_paged_decode_splits(batch, num_kv_heads, max_blocks_per_seq, block_size, num_splits)
 
 
-__all__ = ["store_kvcache", "flash_attn_with_kvcache", "supports", "decode_splits"]
+__all__ = ["store_kvcache", "flash_attn_with_kvcache", "decode_attention", "supports", "decode_splits"]

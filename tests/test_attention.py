@@ -259,3 +259,93 @@ def test_decode_attention_bad_table_and_length(cuda):
                                   causal=True)
     assert nanovllm_b200.status(cuda, clear=True) == 2
     assert torch.equal(out[2], good[2]) and out.isfinite().all()
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# GPU: the stream-K decode kernel (nvb200_paged_decode_attention_streamk through decode_attention(method="streamk")).
+
+STREAMK_CASES = DECODE_CASES + [
+    # one sequence split over every resident CTA: hundreds of partial records merged by the last CTA to finish
+    (1, 1, 8, 1, 256, [8192], True, 0),
+    # many short sequences: ranges of many whole (sequence, head) segments, empty ones among them
+    (300, 1, 16, 8, 16, [(i * 37) % 41 for i in range(300)], True, 0),
+    # every sequence empty: no units at all, every output row zero
+    (4, 1, 16, 8, 256, [0, 0, 0, 0], True, 0),
+    # 16 query rows per KV head with long sequences (two CTAs per SM)
+    (6, 4, 16, 4, 64, [3000, 17, 2048, 1, 999, 4096], True, 0),
+    # 8 rows per KV head, non-causal, block size 16
+    (9, 1, 64, 8, 16, [513] * 9, False, 0),
+]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("B,n,hq,hkv,bs,lens,causal,splits", STREAMK_CASES)
+def test_decode_streamk_matches_oracle(cuda, B, n, hq, hkv, bs, lens, causal, splits):
+    from nanovllm_b200.kernels.attention import decode_attention
+    import nanovllm_b200
+    q, kc, vc, sl, table = _decode_inputs(B, n, hq, hkv, bs, lens, cuda)
+    scale = 128 ** -0.5
+    nanovllm_b200.status(cuda, clear=True)
+    out = decode_attention(q, kc, vc, sl, block_table=table, softmax_scale=scale, causal=causal, method="streamk")
+    ref = om.paged_decode_attention(q, kc, vc, sl, table, scale, causal)
+    assert out.shape == (B, n, hq, 128) and out.dtype == torch.bfloat16
+    torch.testing.assert_close(out.float(), ref, rtol=RTOL, atol=ATOL)
+    assert nanovllm_b200.status(cuda) == 0
+    if all(L == 0 for L in lens):
+        assert torch.equal(out, torch.zeros_like(out))
+
+
+@pytest.mark.gpu
+def test_decode_streamk_deterministic_and_close_to_cluster(cuda):
+    """Repeated stream-K calls give identical bits (split pairs merge in CTA order, whichever CTA finishes last), and
+    agree with the cluster kernel within the bf16 tolerance at the decode-step shape."""
+    from nanovllm_b200.kernels.attention import decode_attention
+    q, kc, vc, sl, table = _decode_inputs(32, 1, 16, 8, 256, [1024] * 31 + [777], cuda, seed=11)
+    kw = dict(block_table=table, softmax_scale=128 ** -0.5, causal=True)
+    first = decode_attention(q, kc, vc, sl, method="streamk", **kw)
+    for _ in range(3):
+        assert torch.equal(decode_attention(q, kc, vc, sl, method="streamk", **kw), first)
+    cluster = decode_attention(q, kc, vc, sl, method="cluster", **kw)
+    torch.testing.assert_close(first.float(), cluster.float(), rtol=RTOL, atol=ATOL)
+
+
+@pytest.mark.gpu
+def test_decode_streamk_graph_replay(cuda):
+    """Captured once (after an eager call created the workspace), replayed on new cache contents and lengths: equal to
+    eager stream-K calls bit for bit, so the workspace's counters are back at zero after every replay."""
+    from nanovllm_b200.kernels.attention import decode_attention
+    q, kc, vc, sl, table = _decode_inputs(8, 1, 16, 8, 256, [900] * 8, cuda, seed=1)
+    kw = dict(block_table=table, softmax_scale=0.088, causal=True, method="streamk")
+    decode_attention(q, kc, vc, sl, **kw)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        out = decode_attention(q, kc, vc, sl, **kw)
+    for seed in range(3):
+        g = torch.Generator().manual_seed(200 + seed)
+        kc.copy_(torch.randn(kc.shape, generator=g).bfloat16())
+        sl.copy_(torch.randint(0, 1024, (8,), generator=g, dtype=torch.int32))
+        graph.replay()
+        eager = decode_attention(q, kc, vc, sl, **kw)
+        torch.cuda.synchronize()
+        assert torch.equal(out, eager)
+        ref = om.paged_decode_attention(q, kc, vc, sl, table, 0.088, True)
+        torch.testing.assert_close(out.float(), ref, rtol=RTOL, atol=ATOL)
+    del graph
+
+
+@pytest.mark.gpu
+def test_decode_streamk_bad_table_and_length(cuda):
+    """As for the cluster kernel: out-of-range table entries and lengths are flagged, never followed, and the other
+    sequences' rows are unaffected."""
+    from nanovllm_b200.kernels.attention import decode_attention
+    import nanovllm_b200
+    q, kc, vc, sl, table = _decode_inputs(3, 1, 16, 8, 256, [300, 300, 300], cuda, seed=2)
+    kw = dict(softmax_scale=0.1, causal=True, method="streamk")
+    good = decode_attention(q, kc, vc, sl, block_table=table, **kw)
+    bad_table, bad_len = table.clone(), sl.clone()
+    bad_table[0, 1] = kc.shape[0] + 5
+    bad_len[1] = 10 ** 6
+    nanovllm_b200.status(cuda, clear=True)
+    out = decode_attention(q, kc, vc, bad_len, block_table=bad_table, **kw)
+    assert nanovllm_b200.status(cuda, clear=True) == 2
+    assert torch.equal(out[2], good[2]) and out.isfinite().all()
