@@ -425,9 +425,14 @@ static_assert(smem_bytes(kMaxRows) <= 227 * 1024, "a CTA's shared memory");
 // arrival counter and the last to arrive merges the records in CTA order (so results do not depend on timing) and
 // resets the counter to zero. No CTA waits for another.
 //
-// Workspace: counters int32 [batch * Hkv] at offset 0 (zero before the first call; every call leaves them zero), then
-// at kCounterAlign-rounded offset the partial records fp32 [2 * grid][R][kStateStride] (CTA c writes slots 2c and 2c+1).
+// Workspace: the partial records fp32 [2 * grid][R][kStateStride] at offset 0 (CTA c writes slots 2c and 2c + 1), in a
+// region of one fixed size per device (the largest any row count needs), then the counters int32 [batch * Hkv] (zero
+// before the first call; every call leaves them zero). The fixed split keeps every call's counters off every other
+// call's records, whatever their batch sizes and row counts.
 constexpr int64_t kCounterAlign = 256;
+// Fewest tiles a CTA takes (4 per warp) when the batch has too few for every resident CTA: shorter ranges spend more
+// time starting and merging than streaming.
+constexpr int64_t kMinTilesPerCta = 16;
 
 struct StreamKParams {
   int32_t *counters;
@@ -559,9 +564,9 @@ __global__ void __launch_bounds__(kAttnThreads, streamk_min_blocks(R))
   }
   __syncthreads();
   const int64_t U = meta[0];
-  const int64_t G = min(static_cast<int64_t>(gridDim.x), U);
+  const int64_t G = min(static_cast<int64_t>(gridDim.x), max(int64_t{1}, U / kMinTilesPerCta));
   const int64_t c = blockIdx.x;
-  if (c >= G) return;
+  if (U == 0 || c >= G) return;
   const int32_t u0 = static_cast<int32_t>(range_start(c, U, G)), u1 = static_cast<int32_t>(range_start(c + 1, U, G));
 
   // The segment holding u0: sequence b with hkv * P(b) <= u0 < hkv * P(b + 1), P the tile prefix (every warp scans,
@@ -650,8 +655,29 @@ __global__ void __launch_bounds__(kAttnThreads, streamk_min_blocks(R))
   load_q(seg.b, seg.h);
   __syncthreads();
 
+  // Query element (row k, column tid) of (b, h), scaled; rows past `rows` are zero.
+  auto fetch_q = [&](int b, int h, int k) {
+    if (k >= p.rows) return 0.f;
+    const int qi = k / p.group, gg = k - qi * p.group;
+    const int64_t at = static_cast<int64_t>(b) * p.q_batch_stride + static_cast<int64_t>(qi) * p.q_token_stride +
+                       (static_cast<int64_t>(h) * p.group + gg) * p.q_head_stride + tid;
+    return __bfloat162float(p.q[at]) * p.scale_log2;
+  };
+  // Up to 8 rows, the next segment's queries are fetched into registers when a segment starts, so that their loads
+  // are in flight while it streams rather than after it.
+  constexpr bool kPrefetchQ = R <= 8;
+  float qn[kPrefetchQ ? R : 1];
+
   int g = 0;  // this warp's items consumed so far (ring stage g % kStages)
   while (seg.n > 0) {
+    Segment nx = seg;
+    nx.next(p, batch, hkv, u1);
+    if constexpr (kPrefetchQ) {
+      if (nx.n > 0) {
+#pragma unroll
+        for (int k = 0; k < R; ++k) qn[k] = fetch_q(nx.b, nx.h, k);
+      }
+    }
     const int my = seg.n > warp ? static_cast<int>((seg.n - warp + kAttnWarps - 1) / kAttnWarps) : 0;
     int64_t lim[R];
     row_limits<R>(lim, seg.L, p.rows, p.group, p.sq, p.causal);
@@ -697,27 +723,40 @@ __global__ void __launch_bounds__(kAttnThreads, streamk_min_blocks(R))
       }
       __syncthreads();
       if (meta[1]) {
+        // One pass over the contributors in CTA order with a running maximum; the loads of consecutive contributors
+        // do not depend on one another, so the unrolled loop keeps several in flight.
+        float mx[R], acc[R], sum[R];
 #pragma unroll
-        for (int r = 0; r < R; ++r) {
-          float mx = -INFINITY;
-          for (int64_t cc = first; cc <= last; ++cc) {
-            const float *x = sk.partials + (partial_slot(cc, seg.pair_u, U, G) * R + r) * kStateStride;
-            mx = fmaxf(mx, __ldcg(x + kHeadDim));
+        for (int r = 0; r < R; ++r) mx[r] = -INFINITY, acc[r] = 0.f, sum[r] = 0.f;
+#pragma unroll 4
+        for (int64_t cc = first; cc <= last; ++cc) {
+          const float *x = sk.partials + partial_slot(cc, seg.pair_u, U, G) * (R * kStateStride);
+#pragma unroll
+          for (int r = 0; r < R; ++r) {
+            const float m_c = __ldcg(x + r * kStateStride + kHeadDim);
+            const float l_c = __ldcg(x + r * kStateStride + kHeadDim + 1);
+            const float o_c = __ldcg(x + r * kStateStride + tid);
+            const float mn = fmaxf(mx[r], m_c);
+            const float mu = mn == -INFINITY ? 0.f : mn;
+            const float a_old = exp2f(mx[r] - mu), a_new = exp2f(m_c - mu);
+            acc[r] = fmaf(a_new, o_c, acc[r] * a_old);
+            sum[r] = fmaf(a_new, l_c, sum[r] * a_old);
+            mx[r] = mn;
           }
-          const float mu = mx == -INFINITY ? 0.f : mx;
-          float acc = 0.f, sum = 0.f;
-          for (int64_t cc = first; cc <= last; ++cc) {
-            const float *x = sk.partials + (partial_slot(cc, seg.pair_u, U, G) * R + r) * kStateStride;
-            const float sc = exp2f(__ldcg(x + kHeadDim) - mu);
-            acc = fmaf(sc, __ldcg(x + tid), acc);
-            sum = fmaf(sc, __ldcg(x + kHeadDim + 1), sum);
-          }
-          write_row(seg.b, seg.h, r, acc, sum);
         }
+#pragma unroll
+        for (int r = 0; r < R; ++r) write_row(seg.b, seg.h, r, acc[r], sum[r]);
       }
     }
-    seg.next(p, batch, hkv, u1);
-    if (seg.n > 0) load_q(seg.b, seg.h);
+    seg = nx;
+    if (seg.n > 0) {
+      if constexpr (kPrefetchQ) {
+#pragma unroll
+        for (int k = 0; k < R; ++k) q_s[q_index(k, tid)] = qn[k];
+      } else {
+        load_q(seg.b, seg.h);
+      }
+    }
     __syncthreads();  // the next segment's queries are in place; records and the flag may be rewritten
   }
   cp_async_wait<0>();
@@ -865,9 +904,28 @@ bool streamk_fits(const nvb200_paged_decode_args *a) {
   return static_cast<int64_t>(a->batch) * a->num_kv_heads * cap_tiles < (int64_t{1} << 31);
 }
 
-// Workspace bytes of a stream-K call: the counters, then the partial records for `grid` CTAs at R rows.
-int64_t streamk_workspace_bytes(int64_t batch, int64_t hkv, int64_t grid, int R) {
-  return round_up(batch * hkv * 4, kCounterAlign) + streamk_partial_bytes(grid, R);
+// Bytes of the workspace's record region on the current device: the most that any row count's grid writes (cached
+// per device; 0 if a launch shape could not be determined).
+int64_t streamk_record_region() {
+  static std::atomic<int64_t> cached[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) return 0;
+  int64_t v = dev < 64 ? cached[dev].load(std::memory_order_acquire) : 0;
+  if (v == 0) {
+    for (int R : {1, 2, 4, 8, 16}) {
+      const int grid = streamk_grid_for(R);
+      if (grid <= 0) return 0;
+      v = std::max(v, round_up(streamk_partial_bytes(grid, R), kCounterAlign));
+    }
+    if (dev < 64) cached[dev].store(v, std::memory_order_release);
+  }
+  return v;
+}
+
+// Workspace bytes of a stream-K call: the record region, then the counters.
+int64_t streamk_workspace_bytes(int64_t batch, int64_t hkv) {
+  const int64_t region = streamk_record_region();
+  return region > 0 ? region + round_up(batch * hkv * 4, kCounterAlign) : -1;
 }
 
 int launch_streamk_rows(int R, const AttnParams &p, int batch, int hkv, int grid, int32_t *counters, float *partials,
@@ -906,10 +964,7 @@ extern "C" int64_t nvb200_paged_decode_workspace_size(const nvb200_paged_decode_
     return -1;
   const int64_t rows = static_cast<int64_t>(a->queries_per_seq) * (a->num_q_heads / a->num_kv_heads);
   if (rows > kMaxRows) return -1;
-  const int R = row_bucket(static_cast<int>(rows));
-  const int grid = streamk_grid_for(R);
-  if (grid <= 0) return -1;
-  return streamk_workspace_bytes(a->batch, a->num_kv_heads, grid, R);
+  return streamk_workspace_bytes(a->batch, a->num_kv_heads);
 }
 
 extern "C" int nvb200_paged_decode_attention_streamk(const nvb200_paged_decode_args *a, void *workspace,
@@ -922,13 +977,14 @@ extern "C" int nvb200_paged_decode_attention_streamk(const nvb200_paged_decode_a
   const int R = row_bucket(p.rows);
   const int grid = streamk_grid_for(R);
   if (grid <= 0) return NVB200_ERR_CUDA;
-  const int64_t need = streamk_workspace_bytes(a->batch, a->num_kv_heads, grid, R);
+  const int64_t need = streamk_workspace_bytes(a->batch, a->num_kv_heads);
+  if (need <= 0) return NVB200_ERR_CUDA;
   if (!workspace || (reinterpret_cast<uintptr_t>(workspace) & (kCounterAlign - 1)) != 0 || workspace_bytes < need)
     return NVB200_ERR_ARG;
   p.splits = 1;
   auto *base = static_cast<uint8_t *>(workspace);
-  return launch_streamk_rows(R, p, a->batch, a->num_kv_heads, grid, reinterpret_cast<int32_t *>(base),
-                             reinterpret_cast<float *>(base + round_up(static_cast<int64_t>(a->batch) *
-                                                                        a->num_kv_heads * 4, kCounterAlign)),
-                             reinterpret_cast<cudaStream_t>(stream));
+  return launch_streamk_rows(R, p, a->batch, a->num_kv_heads, grid,
+                             reinterpret_cast<int32_t *>(base + streamk_record_region()),
+                             reinterpret_cast<float *>(base), reinterpret_cast<cudaStream_t>(stream));
 }
+

@@ -15,6 +15,7 @@ device data on the host. Out-of-range slots, block-table entries and sequence le
 written) and flagged in the device status word (nanovllm_b200.status()).
 """
 import ctypes
+import math
 
 import torch
 
@@ -94,9 +95,39 @@ def supports(q, k_cache, v_cache, k=None, v=None, rotary_cos=None, rotary_sin=No
 
 
 # How flash_attn_with_kvcache runs when the caller leaves num_splits at 0: "cluster" (nvb200_paged_decode_attention:
-# one thread-block cluster per (sequence, KV head)) or "streamk" (nvb200_paged_decode_attention_streamk: a persistent
-# grid with equal shares of all tiles, merging split pairs through a per-device workspace).
-DEFAULT_METHOD = "cluster"
+# one CTA, or a thread-block cluster of CTAs, per (sequence, KV head)), "streamk" (nvb200_paged_decode_attention_streamk:
+# a persistent grid with equal shares of all tiles, merging split pairs through a per-device workspace) or "auto".
+DEFAULT_METHOD = "auto"
+
+# "auto" picks stream-K only where it was measured faster on B200 (L2 flushed, median of 200): at 1-2 query rows per
+# KV head, when the (sequence, head) pairs overfill the cluster kernel's resident CTAs (3 per SM at these row counts)
+# and leave its last wave less than 70 % full. 64 x 2048 keys (512 pairs, 1.15 waves): 96 vs 115 us; 64 x 1024:
+# 57 vs 63 us. Elsewhere the cluster kernel was as fast or faster (32 x 1024: 32.8 vs 36.9 us; 96 x 1024, 1.73 waves:
+# 71.7 vs 77.8 us; 128 x 512: 59.4 vs 61.4 us).
+_AUTO_MAX_ROWS = 2
+_CLUSTER_CTAS_PER_SM = 3
+_AUTO_LAST_WAVE_FILL = 0.7
+_sm_counts = {}
+
+
+def _sm_count(device: torch.device) -> int:
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    n = _sm_counts.get(idx)
+    if n is None:
+        n = _sm_counts[idx] = torch.cuda.get_device_properties(idx).multi_processor_count
+    return n
+
+
+def choose_method(batch: int, num_kv_heads: int, rows: int, device: torch.device) -> str:
+    """The kernel "auto" runs for `batch` sequences of `rows` query rows per KV head (queries x group)."""
+    if rows > _AUTO_MAX_ROWS:
+        return "cluster"
+    slots = _CLUSTER_CTAS_PER_SM * _sm_count(device)
+    pairs = batch * num_kv_heads
+    if pairs <= slots:
+        return "cluster"
+    waves = pairs / slots
+    return "streamk" if waves / math.ceil(waves) < _AUTO_LAST_WAVE_FILL else "cluster"
 
 # One workspace per device for the stream-K kernel: zeroed once at allocation (the kernel leaves its counters at
 # zero), sized generously so that it rarely grows. Calls on one device share it, which is safe for calls ordered on
@@ -144,9 +175,10 @@ def flash_attn_with_kvcache(q, k_cache, v_cache, k=None, v=None, rotary_cos=None
 def decode_attention(q, k_cache, v_cache, cache_seqlens, block_table=None, softmax_scale=None, causal=False,
                      num_splits=0, method="cluster"):
     """flash_attn_with_kvcache's decode form with the kernel named: method "cluster" (num_splits CTAs per sequence,
-    0 = automatic) or "streamk" (num_splits ignored). A stream-K call made while a CUDA graph is being captured,
-    before this device's workspace exists, runs the cluster kernel (make one call before capturing)."""
-    if method not in ("cluster", "streamk"):
+    0 = automatic), "streamk" (num_splits ignored) or "auto" (choose_method). A stream-K call made while a CUDA graph
+    is being captured, before this device's workspace exists, runs the cluster kernel (make one call before
+    capturing)."""
+    if method not in ("cluster", "streamk", "auto"):
         raise ValueError(f"decode_attention: unknown method {method!r}")
     if isinstance(cache_seqlens, int):
         cache_seqlens = torch.full((q.shape[0],), cache_seqlens, dtype=torch.int32, device=q.device)
@@ -180,6 +212,8 @@ def decode_attention(q, k_cache, v_cache, cache_seqlens, block_table=None, softm
     a.softmax_scale = scale
     a.status = _lib.status_word(q.device).data_ptr()
     L = _lib.lib()
+    if method == "auto":
+        method = choose_method(B, hkv, n * (hq // hkv), q.device)
     if method == "streamk":
         need = L.nvb200_paged_decode_workspace_size(ctypes.byref(a))
         _require(need > 0, "decode_attention: no stream-K launch shape for these sizes")
@@ -198,4 +232,5 @@ def decode_splits(batch: int, num_kv_heads: int, max_blocks_per_seq: int, block_
     return _lib.lib().nvb200_paged_decode_splits(batch, num_kv_heads, max_blocks_per_seq, block_size, num_splits)
 
 
-__all__ = ["store_kvcache", "flash_attn_with_kvcache", "decode_attention", "supports", "decode_splits"]
+__all__ = ["store_kvcache", "flash_attn_with_kvcache", "decode_attention", "choose_method", "supports",
+           "decode_splits"]

@@ -66,6 +66,21 @@ def test_store_kvcache_checks_mirror_the_reference():
         store_kvcache(key, key, cache.transpose(1, 2), cache, torch.zeros(4, dtype=torch.int32))
 
 
+def test_auto_method_follows_the_measured_crossover(monkeypatch):
+    """"auto" keeps the cluster kernel unless, at 1-2 rows per KV head, the (sequence, head) pairs overfill its
+    resident CTAs (3 per SM) and leave the last wave less than 70 % full (148 SMs: 444 slots)."""
+    from nanovllm_b200.kernels import attention as at
+    monkeypatch.setitem(at._sm_counts, 0, 148)
+    dev = torch.device("cuda", 0)
+    assert at.choose_method(32, 8, 2, dev) == "cluster"      # decode step, 256 pairs: one partial wave
+    assert at.choose_method(64, 8, 2, dev) == "streamk"      # 512 pairs: 1.15 waves
+    assert at.choose_method(48, 8, 2, dev) == "cluster"      # 384 pairs fit
+    assert at.choose_method(96, 8, 2, dev) == "cluster"      # 1.73 waves
+    assert at.choose_method(128, 8, 2, dev) == "cluster"     # 2.31 waves
+    assert at.choose_method(64, 8, 4, dev) == "cluster"      # more rows: not measured faster
+    assert at.choose_method(100, 5, 1, dev) == "streamk"     # 500 pairs: 1.13 waves
+
+
 # ---------------------------------------------------------------------------------------------------------------
 # GPU: store_kvcache.
 
@@ -336,7 +351,8 @@ def test_decode_streamk_graph_replay(cuda):
 @pytest.mark.gpu
 def test_decode_streamk_bad_table_and_length(cuda):
     """As for the cluster kernel: out-of-range table entries and lengths are flagged, never followed, and the other
-    sequences' rows are unaffected."""
+    sequences' rows are unaffected (within rounding: the clamped length changes how the batch's tiles are divided
+    between CTAs, so a sequence may be merged from different pieces)."""
     from nanovllm_b200.kernels.attention import decode_attention
     import nanovllm_b200
     q, kc, vc, sl, table = _decode_inputs(3, 1, 16, 8, 256, [300, 300, 300], cuda, seed=2)
@@ -348,4 +364,19 @@ def test_decode_streamk_bad_table_and_length(cuda):
     nanovllm_b200.status(cuda, clear=True)
     out = decode_attention(q, kc, vc, bad_len, block_table=bad_table, **kw)
     assert nanovllm_b200.status(cuda, clear=True) == 2
-    assert torch.equal(out[2], good[2]) and out.isfinite().all()
+    torch.testing.assert_close(out[2].float(), good[2].float(), rtol=RTOL, atol=ATOL)
+    assert out.isfinite().all()
+
+
+@pytest.mark.gpu
+def test_decode_streamk_consecutive_shapes_share_the_workspace(cuda):
+    """Calls whose batch sizes and row counts differ, one after another on the device's one workspace: each call's
+    counters lie apart from every call's partial records, so no call reads another's leftovers."""
+    from nanovllm_b200.kernels.attention import decode_attention
+    shapes = [(2, 1, 16, 8, 256, [4096, 3000]), (300, 1, 16, 8, 16, [(i * 13) % 50 for i in range(300)]),
+              (1, 4, 16, 4, 64, [5000]), (64, 1, 16, 8, 256, [700] * 64), (2, 1, 16, 8, 256, [4096, 1])]
+    for i, (B, n, hq, hkv, bs, lens) in enumerate(shapes * 2):
+        q, kc, vc, sl, table = _decode_inputs(B, n, hq, hkv, bs, lens, cuda, seed=50 + i)
+        out = decode_attention(q, kc, vc, sl, block_table=table, softmax_scale=0.1, causal=True, method="streamk")
+        ref = om.paged_decode_attention(q, kc, vc, sl, table, 0.1, True)
+        torch.testing.assert_close(out.float(), ref, rtol=RTOL, atol=ATOL)
