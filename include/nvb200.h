@@ -249,6 +249,26 @@ NVB200_API int64_t nvb200_paged_decode_workspace_size(const nvb200_paged_decode_
 NVB200_API int nvb200_paged_decode_attention_streamk(const nvb200_paged_decode_args *args, void *workspace,
                                                      int64_t workspace_bytes, nvb200_stream_t stream);
 
+/* The stream-K attention above for callers that cannot allocate device memory when they call: an engine that has
+ * already handed nearly all free HBM to its KV cache (as nano-vllm does at start-up), a decode loop that must not
+ * risk cudaMalloc/cudaFree synchronising the device, or a host plugin interface that passes a kernel only its input
+ * and output pointers. It allocates nothing and takes no workspace: its scratch is a fixed array of
+ * NVB200_DECODE_NOALLOC_SCRATCH_BYTES (4 MiB) in the library's own device memory, which every GPU that loads the
+ * library holds until the process exits.
+ * No counterpart in the reference: an addition of this library.
+ *   - The first call on a device looks up the array's device address (cudaGetSymbolAddress, with that device
+ *     current); make that first call before any stream capture.
+ *   - Each call clears the array's counters on `stream` (cudaMemsetAsync) before its kernel, since the array keeps
+ *     what the previous call left.
+ *   - Every call on a device shares the one array: calls that may overlap on the GPU (different streams without
+ *     ordering between them) race and give wrong results. Order them on one stream.
+ *   - Returns NVB200_ERR_UNSUPPORTED when batch * num_kv_heads exceeds NVB200_DECODE_NOALLOC_MAX_PAIRS (16384), and
+ *     otherwise where nvb200_paged_decode_attention_streamk does. With 16 query rows per KV head it runs 244 CTAs
+ *     (the array's limit) rather than one per resident slot. */
+#define NVB200_DECODE_NOALLOC_SCRATCH_BYTES (4 << 20)
+#define NVB200_DECODE_NOALLOC_MAX_PAIRS 16384
+NVB200_API int nvb200_paged_decode_attention_noalloc(const nvb200_paged_decode_args *args, nvb200_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -988,3 +988,68 @@ extern "C" int nvb200_paged_decode_attention_streamk(const nvb200_paged_decode_a
                              reinterpret_cast<float *>(base), reinterpret_cast<cudaStream_t>(stream));
 }
 
+// ---------------------------------------------------------------------------------------------------------------
+// Allocation-free decode attention: the stream-K kernel with its workspace in a fixed array of the library's own
+// device memory, for callers that cannot allocate device memory at call time. nano-vllm-style engines reserve nearly
+// all free HBM for the KV cache at start-up (gpu_memory_utilization), so a later allocation can fail; cudaMalloc and
+// cudaFree may synchronise the device in the middle of a decode loop; and some host plugin interfaces hand a kernel
+// only its input and output pointers, with no allocator to draw a workspace from.
+//
+// The array (NVB200_DECODE_NOALLOC_SCRATCH_BYTES, 4 MiB) is part of the library's device image, so every GPU that
+// loads the library holds it until the process exits. It holds the arrival counters of at most
+// NVB200_DECODE_NOALLOC_MAX_PAIRS (sequence, KV head) pairs, then the partial records; calls with 16 query rows per KV
+// head get fewer CTAs than the SMs could hold (244 instead of 296) so that their records fit.
+namespace nvb200 {
+namespace {
+
+constexpr int64_t kNoAllocBytes = NVB200_DECODE_NOALLOC_SCRATCH_BYTES;
+constexpr int64_t kNoAllocPairs = NVB200_DECODE_NOALLOC_MAX_PAIRS;
+constexpr int64_t kNoAllocCounterBytes = round_up(kNoAllocPairs * 4, kCounterAlign);
+static_assert(kNoAllocCounterBytes < kNoAllocBytes, "the counters leave room for partial records");
+static_assert(streamk_partial_bytes(1, kMaxRows) <= kNoAllocBytes - kNoAllocCounterBytes, "one CTA's records fit");
+
+static __device__ __align__(256) uint8_t g_decode_scratch[kNoAllocBytes];
+
+// Device address of g_decode_scratch on each device (0 = not looked up yet). The host-side name of the array is a
+// stand-in, not a device address, so the address is taken once per device with that device current.
+std::atomic<uintptr_t> g_decode_scratch_addr[64];
+
+int decode_scratch(uint8_t **out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return NVB200_ERR_CUDA;
+  uintptr_t a = g_decode_scratch_addr[dev].load(std::memory_order_acquire);
+  if (a == 0) {
+    void *ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_decode_scratch) != cudaSuccess || ptr == nullptr) return NVB200_ERR_CUDA;
+    a = reinterpret_cast<uintptr_t>(ptr);
+    g_decode_scratch_addr[dev].store(a, std::memory_order_release);
+  }
+  *out = reinterpret_cast<uint8_t *>(a);
+  return NVB200_OK;
+}
+
+}  // namespace
+}  // namespace nvb200
+
+extern "C" int nvb200_paged_decode_attention_noalloc(const nvb200_paged_decode_args *a, nvb200_stream_t stream) {
+  AttnParams p;
+  bool launch = false;
+  if (int rc = prepare_decode(a, p, &launch)) return rc;
+  if (!launch) return NVB200_OK;
+  if (!streamk_fits(a)) return NVB200_ERR_UNSUPPORTED;
+  const int64_t pairs = static_cast<int64_t>(a->batch) * a->num_kv_heads;
+  if (pairs > kNoAllocPairs) return NVB200_ERR_UNSUPPORTED;  // beyond the fixed array's counters
+  const int R = row_bucket(p.rows);
+  int grid = streamk_grid_for(R);
+  if (grid <= 0) return NVB200_ERR_CUDA;
+  const int64_t fit = (kNoAllocBytes - kNoAllocCounterBytes) / streamk_partial_bytes(1, R);
+  grid = static_cast<int>(std::min<int64_t>(grid, fit));
+  uint8_t *scratch = nullptr;
+  if (int rc = decode_scratch(&scratch)) return rc;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  // The array keeps whatever the last call left; the counters must start at zero.
+  if (cudaMemsetAsync(scratch, 0, static_cast<size_t>(pairs) * 4, s) != cudaSuccess) return NVB200_ERR_CUDA;
+  p.splits = 1;
+  return launch_streamk_rows(R, p, a->batch, a->num_kv_heads, grid, reinterpret_cast<int32_t *>(scratch),
+                             reinterpret_cast<float *>(scratch + kNoAllocCounterBytes), s);
+}

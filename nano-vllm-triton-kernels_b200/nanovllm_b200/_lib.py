@@ -25,7 +25,7 @@ EXPORTS = ("nvb200_status_string", "nvb200_qk_norm_rope_kv", "nvb200_rms_norm", 
            "nvb200_allreduce_buffer_bytes", "nvb200_allreduce_buffer_create", "nvb200_allreduce_buffer_open",
            "nvb200_allreduce_buffer_close", "nvb200_matmul_allreduce", "nvb200_store_kvcache",
            "nvb200_paged_decode_attention", "nvb200_paged_decode_splits", "nvb200_paged_decode_workspace_size",
-           "nvb200_paged_decode_attention_streamk")
+           "nvb200_paged_decode_attention_streamk", "nvb200_paged_decode_attention_noalloc")
 
 _vp, _i64, _i32, _f32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32, ctypes.c_float
 
@@ -107,6 +107,8 @@ def _declare(lib):
     lib.nvb200_paged_decode_workspace_size.restype = _i64
     lib.nvb200_paged_decode_attention_streamk.argtypes = [ctypes.POINTER(PagedDecodeArgs), _vp, _i64, _vp]
     lib.nvb200_paged_decode_attention_streamk.restype = ctypes.c_int
+    lib.nvb200_paged_decode_attention_noalloc.argtypes = [ctypes.POINTER(PagedDecodeArgs), _vp]
+    lib.nvb200_paged_decode_attention_noalloc.restype = ctypes.c_int
 
 
 def lib():
