@@ -2,8 +2,9 @@
  *
  * Every entry point takes plain device pointers, element strides and sizes, launches on the given CUDA
  * stream, never synchronises, never allocates and never reads device data on the host, so each call can be
- * captured in a CUDA graph. The return value is NVB200_OK or an NVB200_ERR_* code; no C++ exception crosses
- * this boundary. Strides are in ELEMENTS (as torch's Tensor.stride()), sizes in elements.
+ * captured in a CUDA graph (nvb200_paged_decode_attention_noalloc aside: nothing is stated about capturing it).
+ * The return value is NVB200_OK or an NVB200_ERR_* code; no C++ exception crosses this boundary. Strides are in
+ * ELEMENTS (as torch's Tensor.stride()), sizes in elements.
  *
  * The Python functions that mirror the reference's nanovllm/kernels API (nanovllm_b200.kernels.*) validate
  * their torch arguments exactly as the reference's wrappers do, allocate the outputs with torch, and then call

@@ -19,6 +19,9 @@
 //     shared memory and across the cluster's CTAs through distributed shared memory (each CTA stores its partial
 //     into rank 0's shared memory with st.shared::cluster; one cluster barrier; rank 0 writes the output). No global
 //     scratch and one launch per call.
+// A second kernel below (stream-K) runs the same per-tile code on a persistent grid that divides all of a batch's
+// tiles evenly between the SMs and merges split sequences through a workspace; it pays off when the batch has more
+// (sequence, head) pairs than one wave of the first kernel holds.
 // Keys whose block-table entry lies outside [0, num_blocks), and sequence lengths beyond what the block-table row
 // addresses, are never read: they are skipped (zero rows, clamped length) and reported in the status word.
 #include <algorithm>
