@@ -88,3 +88,21 @@ def test_new_entry_points_reject_bad_arguments_without_a_gpu():
     assert lib.nvb200_paged_decode_splits(1, 8, 8, 256, 0) == 8
     assert lib.nvb200_paged_decode_splits(1, 1, 1, 64, 0) == 1
     assert lib.nvb200_paged_decode_splits(4, 4, 64, 256, 3) == 3
+
+
+def test_streamk_entry_points_check_arguments_without_a_gpu():
+    """The stream-K decode entry point rejects what the plain one rejects before any CUDA call, takes an empty batch
+    without a workspace (no launch), and without a GPU its workspace size is unknown (-1)."""
+    import torch
+    lib = _lib.lib()
+    assert lib.nvb200_paged_decode_attention_streamk(None, None, 0, None) == _lib.ERR_ARG
+    a = _lib.PagedDecodeArgs()
+    a.batch, a.queries_per_seq, a.num_q_heads, a.num_kv_heads, a.head_dim = 0, 1, 16, 8, 128
+    a.block_size, a.max_blocks_per_seq, a.dtype = 256, 1, _lib.BF16
+    assert lib.nvb200_paged_decode_attention_streamk(ctypes.byref(a), None, 0, None) == _lib.OK
+    a.num_q_heads = 12
+    assert lib.nvb200_paged_decode_attention_streamk(ctypes.byref(a), None, 0, None) == _lib.ERR_ARG
+    assert lib.nvb200_paged_decode_workspace_size(ctypes.byref(a)) == -1  # Hq not a multiple of Hkv
+    if not torch.cuda.is_available():
+        a.num_q_heads = 16
+        assert lib.nvb200_paged_decode_workspace_size(ctypes.byref(a)) == -1

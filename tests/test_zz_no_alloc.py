@@ -94,3 +94,14 @@ def test_noalloc_rejects_more_pairs_than_its_array_holds(cuda):
     assert lib.nvb200_paged_decode_attention_noalloc(ctypes.byref(a), _lib.stream_of(q)) == _lib.ERR_UNSUPPORTED
     torch.cuda.synchronize()
     assert torch.equal(out, torch.zeros_like(out))
+
+
+def test_noalloc_checks_arguments_without_a_gpu():
+    """Argument checks come before any CUDA call: a null argument block is refused, an empty batch does nothing."""
+    from nanovllm_b200 import _lib
+    lib = _lib.lib()
+    assert lib.nvb200_paged_decode_attention_noalloc(None, None) == _lib.ERR_ARG
+    a = _lib.PagedDecodeArgs()
+    a.batch, a.queries_per_seq, a.num_q_heads, a.num_kv_heads, a.head_dim = 0, 1, 16, 8, 128
+    a.block_size, a.max_blocks_per_seq, a.dtype = 256, 1, _lib.BF16
+    assert lib.nvb200_paged_decode_attention_noalloc(ctypes.byref(a), None) == _lib.OK
