@@ -27,6 +27,7 @@ backend).
 """
 import argparse
 import datetime
+import importlib.util
 import json
 import os
 import statistics
@@ -62,6 +63,8 @@ def parse_args():
     ap.add_argument("--scaling", choices=["weak", "strong"], default="weak")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-decode-step", action="store_true",
+                    help="skip the decode-step measurement the default (fused8b, one GPU) line carries")
     return ap.parse_args()
 
 
@@ -71,6 +74,21 @@ def load_peaks():
         with open(path) as f:
             return json.load(f), "measured"
     return FALLBACK_PEAKS, "fallback"
+
+
+def reference_kernel_module(name):
+    """The reference's own Triton module nanovllm/kernels/<name>.py from its offline install (baseline/_ref), loaded
+    by file so that the package's engine imports are not pulled in. Returns (module, None) or (None, why not)."""
+    path = os.path.join(ROOT, "baseline", "_ref", "nanovllm", "kernels", name + ".py")
+    if not os.path.exists(path):
+        return None, "the reference is not installed in baseline/_ref"
+    try:
+        spec = importlib.util.spec_from_file_location(f"_reference_kernels_{name}", path)
+        mod = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(mod)
+        return mod, None
+    except Exception as e:  # e.g. triton missing on the box
+        return None, f"importing the reference's {name}.py failed: {type(e).__name__}: {e}"[:300]
 
 
 def load_traffic(key):
@@ -143,11 +161,12 @@ class ClockSampler:
         self.t0 = self.t1 = None
 
     def __enter__(self):
+        # Started before the warm-up steps, so that nvidia-smi's start-up overlaps GPU work and nothing idles the
+        # GPU between the warm-up and the timed steps.
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
                                           "--format=csv,noheader,nounits", "-lms", "20"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            time.sleep(0.3)
         except OSError:
             self.proc = None
         return self
@@ -188,6 +207,15 @@ class ClockSampler:
         reasons = sorted({n for r in use for n, v in zip(names, r[3]) if v.lower() == "active"})
         return {"sm_mhz": statistics.median(r[1] for r in use), "sm_max_mhz": max(r[2] for r in use),
                 "reasons": reasons, "samples": len(use), "samples_in_timed_region": len(inside)}
+
+
+def step_stats(per_step_ms):
+    """Distribution of this rank's per-step event times (us): the line's value uses their sum; these show whether a
+    few slow steps (e.g. the first after the warm-up) move it."""
+    us = sorted(1e3 * x for x in per_step_ms)
+    n = len(us)
+    return {"mean": sum(us) / n, "min": us[0], "median": statistics.median(us), "p90": us[min(n - 1, (9 * n) // 10)],
+            "max": us[-1], "first3": [round(1e3 * x, 2) for x in per_step_ms[:3]]}
 
 
 # ---------------------------------------------------------------------------------------------------------------
@@ -253,8 +281,25 @@ def fused_workload(args, rank, world, dev, hq_total, hkv_total, max_pos, num_blo
                            c["k_w"], c["eps"], c["cos_sin"], c["k_cache"], c["v_cache"], c["slots"][:tokens], False)
         return tokens * ((hq + 2 * hkv) * d * 2 * 2 + 8 + 4 + d * 4) + 2 * d * 2
 
+    # The reference's own Triton kernel on the same inputs (the same-box bar): it takes kv heads in groups of 4
+    # (qk_norm_rope_kv.py:107), so shards of 1-2 kv heads (4/8 GPUs) have no reference kernel to time.
+    library = None
+    if hkv % 4 == 0:
+        mod, why = reference_kernel_module("qk_norm_rope_kv")
+        if mod is None:
+            library = ("reference Triton qk_norm_rope_kv", why)
+        else:
+            def ref_launch():
+                mod.qk_norm_rope_kv(x["q"], x["k"], x["v"], x["positions"], x["q_w"], x["k_w"], x["eps"],
+                                    x["cos_sin"], x["k_cache"], x["v_cache"], x["slots"], False)
+            library = ("reference Triton kernel nanovllm/kernels/qk_norm_rope_kv.py:92-125 (baseline/_ref, "
+                       "JIT-compiled on this GPU)", ref_launch)
+    else:
+        library = ("reference Triton qk_norm_rope_kv", f"the reference kernel needs Hkv % 4 == 0; this shard has "
+                                                       f"{hkv} kv heads")
+
     return dict(launch=launch, units=bytes_per_step, e2e=e2e, cpu=cpu, unit="GB/s", scale=1e9, bound="hbm",
-                metric=METRIC_FUSED, dtype="bf16", launches_per_step=1,
+                metric=METRIC_FUSED, dtype="bf16", launches_per_step=1, library=library,
                 traffic_key=label,
                 config={"workload": label, "tokens_per_step": T, "tokens_per_gpu_step_at_n1": args.tokens,
                         "q_heads": hq_total, "kv_heads": hkv_total, "head_dim": d,
@@ -317,8 +362,16 @@ def matmul_workload(args, rank, world, dev):
         xc["a"][:tokens] @ xc["b"]  # torch CPU bf16 matmul (fp32 accumulation) over the first `tokens` rows
         return 2 * tokens * n_local * K
 
+    mod, why = reference_kernel_module("matmul")
+    if mod is None:
+        library = ("reference Triton matmul", why)
+    else:
+        library = ("reference Triton kernel nanovllm/kernels/matmul.py:84-99 (baseline/_ref, autotuned and "
+                   "JIT-compiled on this GPU)", lambda: mod.matmul(x["a"], x["b"]))
+
     return dict(launch=launch, units=units, e2e=None, cpu=cpu, unit="TFLOP/s", scale=1e12, bound="tensor",
                 metric="matmul bf16 TFLOP/s at M=K=N=4096", dtype="bf16", launches_per_step=1, traffic_key="matmul",
+                library=library,
                 config={"workload": "matmul", "M": M, "N": n_local, "K": K, "b_layout": "weight.t() (K-major)",
                         "parallelism": f"column-parallel x{world}", "l2": "flushed between timed steps"})
 
@@ -666,9 +719,11 @@ def decode_worker(backend: str, bs: int, ctx: int, tp: int = 1) -> dict:
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         if tp > 1:
             mr.dist.barrier()
+        clocks = ClockSampler(int(os.environ.get("LOCAL_RANK", "0"))).__enter__()
         for _ in range(10):
             graph.replay()
         per_run = []
+        clocks.mark_start()
         for _ in range(3):
             if tp > 1:
                 torch.cuda.synchronize()
@@ -684,9 +739,12 @@ def decode_worker(backend: str, bs: int, ctx: int, tp: int = 1) -> dict:
                 mr.dist.all_reduce(tt, op=mr.dist.ReduceOp.MAX)
                 t = float(tt.item())
             per_run.append(t)
+        clocks.mark_end()
+        clocks.__exit__(None, None, None)
         out = gv["outputs"]["target"][:bs].float()
         res = {"backend": backend, "graph_replay_us": 1e3 * sorted(per_run)[1], "runs_us": [1e3 * x for x in per_run],
-               "finite": bool(torch.isfinite(out).all()), "kv_blocks": cfg.num_kvcache_blocks, "tp": tp}
+               "finite": bool(torch.isfinite(out).all()), "kv_blocks": cfg.num_kvcache_blocks, "tp": tp,
+               "clocks": clocks.summary()}
     if tp > 1:
         torch.cuda.synchronize()
         del graph
@@ -706,7 +764,8 @@ def decode_worker(backend: str, bs: int, ctx: int, tp: int = 1) -> dict:
     return res
 
 
-def run_decode(args) -> None:
+def decode_backends(args) -> dict:
+    """Runs the decode-step worker once per backend, each in a fresh process (group), and returns their results."""
     results = {}
     for backend in args.decode_backends.split(","):
         cmd = [sys.executable, os.path.abspath(__file__), "--decode-worker", backend, "--decode-batch",
@@ -714,12 +773,37 @@ def run_decode(args) -> None:
         if args.decode_tp > 1:
             cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={args.decode_tp}",
                    "--master-addr", "127.0.0.1", "--master-port", "29581", *cmd[1:]]
-        out = subprocess.run(cmd, capture_output=True, text=True)
+        t0 = time.perf_counter()
+        try:
+            out = subprocess.run(cmd, capture_output=True, text=True, timeout=900)
+        except subprocess.TimeoutExpired:
+            results[backend] = {"backend": backend, "error": "worker did not finish within 900 s"}
+            continue
         lines = [ln for ln in out.stdout.splitlines() if ln.startswith("{")]
         if out.returncode == 0 and lines:
             results[backend] = json.loads(lines[-1])
         else:
             results[backend] = {"backend": backend, "error": (out.stderr or out.stdout)[-800:]}
+        results[backend]["worker_wall_s"] = round(time.perf_counter() - t0, 1)
+    return results
+
+
+def decode_summary(results: dict) -> dict:
+    """The decode_step object of the headline line: each backend's median graph replay (us) and clocks."""
+    out = {"metric": "decode-step graph replay us (Qwen3-0.6B arch, batch 32, ctx 1024, whole-step CUDA graph)",
+           "method": "the reference's ModelRunner per backend in a fresh process; CUDA events around 50 replays, "
+                     "median of 3 (scripts/bench_decode.py:82-95)", "higher_is_better": False}
+    for name, r in results.items():
+        key = name.replace("-", "_")
+        out[f"{key}_us"] = r.get("graph_replay_us")
+        out[f"{key}_detail"] = {k: v for k, v in r.items() if k not in ("backend", "graph_replay_us")}
+    b, c = out.get("b200_us"), out.get("compile_us")
+    out["b200_vs_compile"] = (c / b) if (b and c) else None
+    return out
+
+
+def run_decode(args) -> None:
+    results = decode_backends(args)
     ours = results.get("b200", {})
     line = {"metric": "decode-step graph replay us (Qwen3-0.6B arch, batch 32, ctx 1024)",
             "value": ours.get("graph_replay_us"), "unit": "us", "n_gpus": args.decode_tp, "steps": 150, "warmup": 10,
@@ -764,23 +848,21 @@ def main():
         flush_w.zero_()
         flush_r.max()
 
-    with torch.inference_mode():
+    with torch.inference_mode(), ClockSampler(local) as clocks:
+        starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
         for _ in range(args.warmup):
             flush_l2()
             wl["launch"]()
-        torch.cuda.synchronize()
-        starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-        ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
         barrier(world)
-        with ClockSampler(local) as clocks:
-            clocks.mark_start()
-            for i in range(args.steps):
-                flush_l2()
-                starts[i].record(stream)
-                wl["launch"]()
-                ends[i].record(stream)
-            barrier(world)
-            clocks.mark_end()
+        clocks.mark_start()
+        for i in range(args.steps):
+            flush_l2()
+            starts[i].record(stream)
+            wl["launch"]()
+            ends[i].record(stream)
+        barrier(world)
+        clocks.mark_end()
         per_step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
         local_s = sum(per_step_ms) / 1e3
         total_s = max_over_ranks(local_s, world)
@@ -809,23 +891,32 @@ def main():
         library = None
         if wl.get("library") is not None:
             name, fn = wl["library"]
-            for _ in range(args.warmup):
-                flush_l2()
-                fn()
-            torch.cuda.synchronize()
-            lib_steps = min(args.steps, 500)
-            ls = [torch.cuda.Event(enable_timing=True) for _ in range(lib_steps)]
-            le = [torch.cuda.Event(enable_timing=True) for _ in range(lib_steps)]
-            for i in range(lib_steps):
-                flush_l2()
-                ls[i].record(stream)
-                fn()
-                le[i].record(stream)
-            torch.cuda.synchronize()
-            lib_s = sum(a.elapsed_time(b) for a, b in zip(ls, le)) / 1e3 / lib_steps
-            library = {"name": name, "us_per_step": 1e6 * lib_s, "value": wl["units"] / lib_s / wl["scale"],
-                       "ours_us_per_step": 1e6 * local_s / args.steps,
-                       "note": "the library kernel the reference calls, same inputs and L2 flush, this rank"}
+            if isinstance(fn, str):
+                library = {"name": name, "unavailable": fn}
+            else:
+                # As many warm-up calls as our arm had, plus one for Triton's JIT/autotune on the first call; then
+                # the same number of steps (at most 500), each after the same L2 flush, timed the same way.
+                for _ in range(args.warmup + 1):
+                    flush_l2()
+                    fn()
+                torch.cuda.synchronize()
+                lib_steps = min(args.steps, 500)
+                ls = [torch.cuda.Event(enable_timing=True) for _ in range(lib_steps)]
+                le = [torch.cuda.Event(enable_timing=True) for _ in range(lib_steps)]
+                for i in range(lib_steps):
+                    flush_l2()
+                    ls[i].record(stream)
+                    fn()
+                    le[i].record(stream)
+                torch.cuda.synchronize()
+                lib_ms = [a.elapsed_time(b) for a, b in zip(ls, le)]
+                lib_s = sum(lib_ms) / 1e3 / lib_steps
+                ours_s = local_s / args.steps
+                library = {"name": name, "us_per_step": 1e6 * lib_s, "value": wl["units"] / lib_s / wl["scale"],
+                           "unit": wl["unit"], "ours_us_per_step": 1e6 * ours_s, "speedup": lib_s / ours_s,
+                           "step_us": step_stats(lib_ms),
+                           "note": "the kernel the reference itself runs for this op, same inputs, same L2 flush and "
+                                   "step timing, this rank"}
 
     if wl["bound"] == "hbm":
         peak = peaks["hbm_gbs"]
@@ -843,7 +934,7 @@ def main():
                          if peak_kind == "measured" else "fallback", "traffic": traffic,
                          "frac_of_nominal_8tbs": achieved / 8000.0 if wl["bound"] == "hbm" else None},
             "clocks": clocks.summary(), "gpu_launches": args.steps * wl["launches_per_step"],
-            "gpu_launches_scope": "rank 0, timed region"}
+            "gpu_launches_scope": "rank 0, timed region", "step_us": step_stats(per_step_ms)}
     if e2e is not None:
         line["e2e"] = e2e
     if library is not None:
@@ -858,6 +949,13 @@ def main():
                                 "cores": torch.get_num_threads(), "kind": "port",
                                 "sample": f"{what} on the host (torch CPU bf16 restatement of the reference), "
                                           f"median of {reps} runs"}
+    if rank == 0 and world == 1 and args.workload == "fused8b" and not args.no_decode_step:
+        # The headline metric's second half: the decode step per backend, same box, same run.
+        # Each backend's worker is a fresh process; this process's tensors are released first.
+        wl = None
+        flush_w = flush_r = None
+        torch.cuda.empty_cache()
+        line["decode_step"] = decode_summary(decode_backends(args))
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:

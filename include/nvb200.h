@@ -91,6 +91,21 @@ typedef struct nvb200_qk_norm_rope_kv_args {
 
 NVB200_API int nvb200_qk_norm_rope_kv(const nvb200_qk_norm_rope_kv_args *args, nvb200_stream_t stream);
 
+/* Which kernel nvb200_qk_norm_rope_kv would launch for these arguments on the current device, without launching
+ * anything: *kernel gets an NVB200_QKNR_KERNEL_* code and *tokens_per_unit the tokens one work unit covers (either
+ * pointer may be NULL). Returns what nvb200_qk_norm_rope_kv would return for an argument error; T = 0 gives
+ * NVB200_QKNR_KERNEL_NONE. Host-only (reads the SM count), for tests and tools that check a shape's route.
+ * Replaces: nothing in the reference (its wrapper always launches one Triton kernel, qk_norm_rope_kv.py:117-124). */
+enum {
+  NVB200_QKNR_KERNEL_NONE = 0,    /* T = 0: no launch                                                        */
+  NVB200_QKNR_KERNEL_GENERIC = 1, /* rows not 16-byte aligned or D outside {64, 128, 256}: one warp per head  */
+  NVB200_QKNR_KERNEL_DIRECT = 2,  /* T <= 512: direct loads and stores, no staging                            */
+  NVB200_QKNR_KERNEL_MULTI = 3,   /* small tokens in a rank's qkv_proj layout: units of 4-16 tokens, bulk copies */
+  NVB200_QKNR_KERNEL_BULK = 4     /* one token (or a head group of one) per unit, bulk-copy pipeline          */
+};
+NVB200_API int nvb200_qk_norm_rope_kv_plan(const nvb200_qk_norm_rope_kv_args *args, int32_t *kernel,
+                                           int32_t *tokens_per_unit);
+
 /* RMSNorm over the last dim, y contiguous [groups * rows_per_group, n].
  * Replaces: nanovllm/kernels/rms_norm.py:83-98 (rms_norm) and _rms_norm_kernel :34-54.
  * Row g * rows_per_group + r of x starts at x + g * group_stride + r * row_stride (a 2-D [rows, n] view is

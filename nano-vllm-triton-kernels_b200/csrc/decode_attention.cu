@@ -1050,7 +1050,9 @@ extern "C" int nvb200_paged_decode_attention_noalloc(const nvb200_paged_decode_a
   uint8_t *scratch = nullptr;
   if (int rc = decode_scratch(&scratch)) return rc;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  // The array keeps whatever the last call left; the counters must start at zero.
+  // The kernel leaves every counter it used at zero, so after a completed call this memset finds zeros; it is kept
+  // so that each call starts from zeroed counters even when a previous call on the array was aborted, faulted or
+  // used more pairs in a way that left them non-zero (the array keeps whatever the last call left).
   if (cudaMemsetAsync(scratch, 0, static_cast<size_t>(pairs) * 4, s) != cudaSuccess) return NVB200_ERR_CUDA;
   p.splits = 1;
   return launch_streamk_rows(R, p, a->batch, a->num_kv_heads, grid, reinterpret_cast<int32_t *>(scratch),

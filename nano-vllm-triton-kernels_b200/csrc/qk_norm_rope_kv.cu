@@ -795,12 +795,16 @@ template <int D> int launch_bulk_shaped(QknrParams &p, int sms, cudaStream_t str
 
 }  // namespace
 
-int qk_norm_rope_kv_launch(const nvb200_qk_norm_rope_kv_args *a, cudaStream_t stream) {
+// Checks the arguments and launches the kernel the sizes and layout call for. With `plan` non-null nothing is
+// launched: the kernel that would run is written to plan[0] (an NVB200_QKNR_KERNEL_* code) and its tokens per work
+// unit to plan[1].
+int qk_norm_rope_kv_launch(const nvb200_qk_norm_rope_kv_args *a, cudaStream_t stream, int32_t *plan) {
   if (a == nullptr) return NVB200_ERR_ARG;
   const int64_t T = a->num_tokens;
   const int hq = a->num_q_heads, hkv = a->num_kv_heads, D = a->head_dim;
   if (T < 0 || hq <= 0 || hkv <= 0 || D <= 0 || hq % hkv != 0 || D % 2 != 0) return NVB200_ERR_ARG;
   if (D > 2 * 32 * kGenericMaxPairs) return NVB200_ERR_UNSUPPORTED;
+  if (plan) plan[0] = NVB200_QKNR_KERNEL_NONE, plan[1] = 0;
   if (T == 0) return NVB200_OK;
   const bool store = a->k_cache != nullptr || a->v_cache != nullptr;
   if (!a->q_out || !a->q || !a->k || !a->positions || !a->q_weight || !a->k_weight || !a->cos_sin) return NVB200_ERR_ARG;
@@ -846,11 +850,19 @@ int qk_norm_rope_kv_launch(const nvb200_qk_norm_rope_kv_args *a, cudaStream_t st
     p.g = hkv;
     dim3 grid(static_cast<unsigned>(T), (hq + hkv + kGenericWarps - 1) / kGenericWarps);
     if (T > 0x7fffffffLL) return NVB200_ERR_UNSUPPORTED;
+    if (plan) {
+      plan[0] = NVB200_QKNR_KERNEL_GENERIC, plan[1] = 1;
+      return NVB200_OK;
+    }
     qknr_generic_kernel<<<grid, 32 * kGenericWarps, 0, stream>>>(p, D);
     return launch_status();
   }
 
   if (T <= kDirectMaxTokens) {
+    if (plan) {
+      plan[0] = NVB200_QKNR_KERNEL_DIRECT, plan[1] = 1;
+      return NVB200_OK;
+    }
     switch (D) {
       case 64: return launch_direct<64>(p, stream);
       case 128: return launch_direct<128>(p, stream);
@@ -877,6 +889,10 @@ int qk_norm_rope_kv_launch(const nvb200_qk_norm_rope_kv_args *a, cudaStream_t st
       p.g = hkv;
       p.units = (T + B - 1) / B;
       p.stage_bytes = static_cast<int>((B * unit1 + 127) / 128 * 128);
+      if (plan) {
+        plan[0] = NVB200_QKNR_KERNEL_MULTI, plan[1] = B;
+        return NVB200_OK;
+      }
       switch (D) {
         case 64: return launch_multi_shaped<64>(p, sms, stream);
         case 128: return launch_multi_shaped<128>(p, sms, stream);
@@ -903,6 +919,10 @@ int qk_norm_rope_kv_launch(const nvb200_qk_norm_rope_kv_args *a, cudaStream_t st
               a->k_token_stride == a->v_token_stride;
   const int unit_bytes = (p.g * p.r + 2 * p.g) * D * 2 + D * 4;
   p.stage_bytes = (unit_bytes + 127) / 128 * 128;
+  if (plan) {
+    plan[0] = NVB200_QKNR_KERNEL_BULK, plan[1] = 1;
+    return NVB200_OK;
+  }
   switch (D) {
     case 64: return launch_bulk_shaped<64>(p, sms, stream);
     case 128: return launch_bulk_shaped<128>(p, sms, stream);
@@ -913,5 +933,14 @@ int qk_norm_rope_kv_launch(const nvb200_qk_norm_rope_kv_args *a, cudaStream_t st
 }  // namespace nvb200
 
 extern "C" int nvb200_qk_norm_rope_kv(const nvb200_qk_norm_rope_kv_args *args, nvb200_stream_t stream) {
-  return nvb200::qk_norm_rope_kv_launch(args, reinterpret_cast<cudaStream_t>(stream));
+  return nvb200::qk_norm_rope_kv_launch(args, reinterpret_cast<cudaStream_t>(stream), nullptr);
+}
+
+extern "C" int nvb200_qk_norm_rope_kv_plan(const nvb200_qk_norm_rope_kv_args *args, int32_t *kernel,
+                                           int32_t *tokens_per_unit) {
+  int32_t plan[2] = {NVB200_QKNR_KERNEL_NONE, 0};
+  const int rc = nvb200::qk_norm_rope_kv_launch(args, nullptr, plan);
+  if (kernel) *kernel = plan[0];
+  if (tokens_per_unit) *tokens_per_unit = plan[1];
+  return rc;
 }

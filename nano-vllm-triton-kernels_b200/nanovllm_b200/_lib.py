@@ -10,17 +10,19 @@ import threading
 
 import torch
 
-# NVB200_LIBRARY may name another build of the same library (e.g. one compiled with different tile constants).
-LIB_PATH = os.environ.get("NVB200_LIBRARY") or os.path.join(os.path.dirname(os.path.abspath(__file__)), "libnvb200.so")
+LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libnvb200.so")
 
 # Return codes and dtype codes of nvb200.h.
 OK, ERR_ARG, ERR_UNSUPPORTED, ERR_CUDA, ERR_NO_DEVICE = 0, 1, 2, 3, 4
 BF16, F16, F32 = 0, 1, 2
 DTYPE_CODE = {torch.bfloat16: BF16, torch.float16: F16, torch.float32: F32}
 STATUS_BAD_POSITION, STATUS_BAD_SLOT, STATUS_WAIT_TIMEOUT = 1, 2, 4
+# NVB200_QKNR_KERNEL_* codes of nvb200_qk_norm_rope_kv_plan.
+QKNR_KERNELS = {0: "none", 1: "generic", 2: "direct", 3: "multi", 4: "bulk"}
 
 # Every extern "C" function of include/nvb200.h; tests check that the library exports each one.
-EXPORTS = ("nvb200_status_string", "nvb200_qk_norm_rope_kv", "nvb200_rms_norm", "nvb200_fused_add_rms_norm",
+EXPORTS = ("nvb200_status_string", "nvb200_qk_norm_rope_kv", "nvb200_qk_norm_rope_kv_plan", "nvb200_rms_norm",
+           "nvb200_fused_add_rms_norm",
            "nvb200_silu_and_mul", "nvb200_matmul_workspace_size", "nvb200_matmul", "nvb200_matmul_silu_and_mul",
            "nvb200_allreduce_buffer_bytes", "nvb200_allreduce_buffer_create", "nvb200_allreduce_buffer_open",
            "nvb200_allreduce_buffer_close", "nvb200_matmul_allreduce", "nvb200_store_kvcache",
@@ -73,6 +75,9 @@ def _declare(lib):
     lib.nvb200_status_string.restype = ctypes.c_char_p
     lib.nvb200_qk_norm_rope_kv.argtypes = [ctypes.POINTER(QkNormRopeKvArgs), _vp]
     lib.nvb200_qk_norm_rope_kv.restype = ctypes.c_int
+    lib.nvb200_qk_norm_rope_kv_plan.argtypes = [ctypes.POINTER(QkNormRopeKvArgs), ctypes.POINTER(_i32),
+                                                ctypes.POINTER(_i32)]
+    lib.nvb200_qk_norm_rope_kv_plan.restype = ctypes.c_int
     lib.nvb200_rms_norm.argtypes = [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _f32, ctypes.c_int, _vp, _vp]
     lib.nvb200_rms_norm.restype = ctypes.c_int
     lib.nvb200_fused_add_rms_norm.argtypes = [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _f32, ctypes.c_int, _vp,

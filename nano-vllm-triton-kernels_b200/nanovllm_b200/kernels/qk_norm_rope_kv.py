@@ -62,19 +62,45 @@ def qk_norm_rope_kv(
     q_out = torch.empty(T, Hq, D, dtype=q.dtype, device=dev)
     k_out = torch.empty(T, Hkv, D, dtype=k.dtype, device=dev) if write_k else None
     if T:
-        a = _lib.QkNormRopeKvArgs()
-        a.q_out, a.k_out = q_out.data_ptr(), _lib.ptr(k_out)
-        a.q, a.k, a.v = q.data_ptr(), k.data_ptr(), v.data_ptr()
-        a.q_token_stride, a.k_token_stride, a.v_token_stride = q.stride(0), k.stride(0), v.stride(0)
-        a.positions = positions.data_ptr()
-        a.slot_mapping = slot_mapping.data_ptr() if store else None
-        a.q_weight, a.k_weight = q_weight.data_ptr(), k_weight.data_ptr()
-        a.cos_sin, a.cos_sin_stride, a.num_positions = (cos_sin_cache.data_ptr(), cos_sin_cache.stride(0),
-                                                        cos_sin_cache.shape[0])
-        if store:
-            a.k_cache, a.v_cache, a.num_slots = k_cache.data_ptr(), v_cache.data_ptr(), k_cache.numel() // (Hkv * D)
-        a.num_tokens, a.num_q_heads, a.num_kv_heads, a.head_dim = T, Hq, Hkv, D
-        a.eps = eps
-        a.status = _lib.status_word(dev).data_ptr()
+        a = _args(q_out, k_out, q, k, v, positions, q_weight, k_weight, eps, cos_sin_cache, k_cache, v_cache,
+                  slot_mapping, store)
         _lib.check(_lib.lib().nvb200_qk_norm_rope_kv(ctypes.byref(a), _lib.stream_of(q)), "qk_norm_rope_kv")
     return q_out, k_out
+
+
+def _args(q_out, k_out, q, k, v, positions, q_weight, k_weight, eps, cos_sin_cache, k_cache, v_cache, slot_mapping,
+          store):
+    T, Hq, D = q.shape
+    Hkv = k.shape[1]
+    a = _lib.QkNormRopeKvArgs()
+    a.q_out, a.k_out = q_out.data_ptr(), _lib.ptr(k_out)
+    a.q, a.k, a.v = q.data_ptr(), k.data_ptr(), v.data_ptr()
+    a.q_token_stride, a.k_token_stride, a.v_token_stride = q.stride(0), k.stride(0), v.stride(0)
+    a.positions = positions.data_ptr()
+    a.slot_mapping = slot_mapping.data_ptr() if store else None
+    a.q_weight, a.k_weight = q_weight.data_ptr(), k_weight.data_ptr()
+    a.cos_sin, a.cos_sin_stride, a.num_positions = (cos_sin_cache.data_ptr(), cos_sin_cache.stride(0),
+                                                    cos_sin_cache.shape[0])
+    if store:
+        a.k_cache, a.v_cache, a.num_slots = k_cache.data_ptr(), v_cache.data_ptr(), k_cache.numel() // (Hkv * D)
+    a.num_tokens, a.num_q_heads, a.num_kv_heads, a.head_dim = T, Hq, Hkv, D
+    a.eps = eps
+    a.status = _lib.status_word(q.device).data_ptr()
+    return a
+
+
+def kernel_plan(q, k, v, positions, q_weight, k_weight, eps, cos_sin_cache, k_cache, v_cache, slot_mapping,
+                write_k) -> tuple[str, int]:
+    """Which kernel `qk_norm_rope_kv` with these arguments runs on their device, and the tokens one work unit covers:
+    ("bulk" | "multi" | "direct" | "generic" | "none", tokens). Launches nothing (nvb200_qk_norm_rope_kv_plan)."""
+    T, Hq, D = q.shape
+    store = k_cache.numel() > 0
+    # The plan query only checks the outputs' addresses (16-byte alignment, as a fresh torch allocation has), so one
+    # small allocation stands in for q_out and k_out.
+    stand_in = torch.empty(16, dtype=q.dtype, device=q.device)
+    a = _args(stand_in, stand_in if write_k else None, q, k, v, positions, q_weight, k_weight, eps, cos_sin_cache,
+              k_cache, v_cache, slot_mapping, store)
+    kernel, tpu = ctypes.c_int32(-1), ctypes.c_int32(0)
+    _lib.check(_lib.lib().nvb200_qk_norm_rope_kv_plan(ctypes.byref(a), ctypes.byref(kernel), ctypes.byref(tpu)),
+               "qk_norm_rope_kv_plan")
+    return _lib.QKNR_KERNELS[kernel.value], tpu.value

@@ -1,8 +1,10 @@
 """nanovllm_b200.install() against the reference package, on CPU (no kernels run).
 
-Needs an importable reference nano-vllm: the offline install under baseline/_ref, or the path in
-$NANOVLLM_REFERENCE. Checks that kernel_backend="b200" is accepted by Config, that the layers' kernel names resolve
-to the b200 functions only while the backend is "b200", and that Qwen3Attention takes the fused path for it.
+Needs an importable reference nano-vllm, looked for in this order: the offline install under baseline/_ref
+(`pip install --no-deps --target baseline/_ref <reference checkout>`), the path in $NANOVLLM_REFERENCE, and a
+checkout named `reference` beside this repository. Checks that kernel_backend="b200" is accepted by Config, that the
+layers' kernel names resolve to the b200 functions only while the backend is "b200", and that Qwen3Attention takes
+the fused path for it.
 """
 import json
 import os
@@ -11,7 +13,8 @@ import sys
 import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-CANDIDATES = [os.path.join(ROOT, "baseline", "_ref"), os.environ.get("NANOVLLM_REFERENCE", "")]
+CANDIDATES = [os.path.join(ROOT, "baseline", "_ref"), os.environ.get("NANOVLLM_REFERENCE", ""),
+              os.path.join(os.path.dirname(ROOT), "reference")]
 REF = next((p for p in CANDIDATES if p and os.path.isdir(os.path.join(p, "nanovllm"))), None)
 pytestmark = pytest.mark.skipif(REF is None, reason="no importable reference nano-vllm")
 

@@ -299,3 +299,85 @@ def test_full_size_properties(cuda, world):
     assert torch.equal(q_out, rq) and torch.equal(k_out, rk)
     # exact slot placement and untouched slots
     check_kv_write(dict(xs, cache=before), dict(k_cache=cache[0], v_cache=cache[1], k_out=k_out), hkv)
+
+
+# ---------------------------------------------------------------------------------------------------------------
+# Tensor-parallel ranks' own qkv_proj outputs (BASELINE config 3 sharded by KV head at 4 and 8 GPUs). A rank's
+# QKVParallelLinear writes [T, (Hq/w + 2 Hkv/w) D] with its q | k | v heads consecutive in each row
+# (nanovllm/layers/linear.py:106-128): the layout that routes 1-2 kv heads per rank to the multi-token kernel
+# (units of 4 or 8 consecutive tokens moved by one bulk copy). Same checks as the full-size test above, and the
+# route itself is asserted through nvb200_qk_norm_rope_kv_plan.
+
+from nanovllm_b200 import parallel  # noqa: E402
+from nanovllm_b200.kernels.qk_norm_rope_kv import kernel_plan  # noqa: E402
+
+
+def rank_inputs(dev, T, world, rank, seed=11):
+    """Rank `rank`'s inputs at the Qwen3-8B shape: its own contiguous qkv_proj output (cut from a full one with the
+    column split QKVParallelLinear makes), its cache slice [1024, 256, 8 / world, 128] (random), replicated
+    positions (uniform in [0, 32768)) and slots (distinct, 5 % -1)."""
+    hq, hkv = 32, 8
+    g = torch.Generator(device=dev).manual_seed(seed + T)
+    full = torch.randn(T, (hq + 2 * hkv) * D, device=dev, generator=g).to(torch.bfloat16)
+    qkv = parallel.shard_qkv_columns(full, hq, hkv, D, rank, world)
+    del full
+    rq, rkv = hq // world, hkv // world
+    q, k, v = qkv.split([rq * D, rkv * D, rkv * D], dim=-1)
+    q, k, v = q.view(T, rq, D), k.view(T, rkv, D), v.view(T, rkv, D)
+    q_w = (1 + 0.1 * torch.randn(D, device=dev, generator=g)).to(torch.bfloat16)
+    k_w = (1 + 0.1 * torch.randn(D, device=dev, generator=g)).to(torch.bfloat16)
+    positions = torch.randint(0, 32768, (T,), device=dev, generator=g)
+    blocks = 1024
+    slots = torch.randperm(blocks * BLOCK, device=dev, generator=g)[:T].to(torch.int32)
+    slots[torch.randperm(T, device=dev, generator=g)[:round(0.05 * T)]] = -1
+    cache = torch.randn(2, blocks, BLOCK, rkv, D, device=dev, generator=g).to(torch.bfloat16)
+    return dict(q=q, k=k, v=v, q_w=q_w, k_w=k_w, positions=positions, slots=slots, cache=cache, eps=1e-6,
+                cos_sin=table(dev, 32768), hkv=rkv)
+
+
+# (world, T): the multi-token route needs ceil(T / B) >= 2 x SMs units (B = 4 at 4 ranks, 8 at 8 ranks); T = 1024
+# is below that and runs the one-token kernel (checked for parity all the same); 8193 leaves a last unit of one
+# token, 8190 one of 2 (B = 4) / 6 (B = 8) tokens.
+MULTI_CASES = [(w, t) for w in (4, 8) for t in (1024, 8192, 8193, 8190)]
+
+
+@pytest.mark.parametrize("write_k", [True, False], ids=["k_out", "no_k_out"])
+@pytest.mark.parametrize("store", [True, False], ids=["cache", "no_cache"])
+@pytest.mark.parametrize("world,tokens", MULTI_CASES, ids=[f"tp{w}-T{t}" for w, t in MULTI_CASES])
+def test_rank_qkv_layout_multi_token_kernel(cuda, world, tokens, store, write_k):
+    x = rank_inputs(cuda, tokens, world, world - 1)
+    hkv = x["hkv"]
+    cache = x["cache"].clone()
+    empty = torch.empty(0, device=cuda, dtype=torch.bfloat16)
+    kc, vc = (cache[0], cache[1]) if store else (empty, empty)
+    slots = x["slots"] if store else None
+    args = (x["q"], x["k"], x["v"], x["positions"], x["q_w"], x["k_w"], x["eps"], x["cos_sin"], kc, vc, slots,
+            write_k)
+    route, tpu = kernel_plan(*args)
+    sms = torch.cuda.get_device_properties(cuda).multi_processor_count
+    B = 4 if world == 4 else 8
+    if (tokens + B - 1) // B >= 2 * sms:
+        assert (route, tpu) == ("multi", B), (route, tpu)
+    else:
+        assert route == "bulk", route
+    _lib.status(cuda, clear=True)
+    q_out, k_out = qk_norm_rope_kv(*args)
+    # The normed heads: the same layout through an identity rotation (cos 1, sin 0 at position 0), k_out on.
+    ident = identity_table(cuda)
+    nargs = (x["q"], x["k"], x["v"], torch.zeros_like(x["positions"]), x["q_w"], x["k_w"], x["eps"], ident, empty,
+             empty, None, True)
+    assert kernel_plan(*nargs)[0] == route
+    nq, nk = qk_norm_rope_kv(*nargs)
+    assert int(om.bf16_ulp_diff(nq, om.rms_forward(x["q"], x["q_w"], x["eps"])).max()) <= MAX_ULP
+    assert int(om.bf16_ulp_diff(nk, om.rms_forward(x["k"], x["k_w"], x["eps"])).max()) <= MAX_ULP
+    rq, rk = om.rotary(x["positions"], nq, nk, x["cos_sin"])
+    assert torch.equal(q_out, rq)
+    if write_k:
+        assert torch.equal(k_out, rk)
+    else:
+        assert k_out is None
+    if store:
+        check_kv_write(dict(x, cache=x["cache"]), dict(k_cache=cache[0], v_cache=cache[1], k_out=rk), hkv)
+    else:
+        assert torch.equal(cache, x["cache"])
+    assert _lib.status(cuda) == 0

@@ -51,12 +51,17 @@ def _args(out, q, kc, vc, sl, table, scale, causal):
     return a
 
 
+# The grid of a call is the smaller of the CTAs the SMs hold at once, the CTAs whose partial records fit in the array
+# (244 at 16 query rows per KV head) and U / 16, U = Hkv * sum_b ceil(L_b / 16) tiles (every CTA streams at least 16
+# tiles). The 8 x 8192-key call at 16 rows (U = 16384, U / 16 = 1024) is the one whose grid the array cuts to 244;
+# the others are cut by U / 16 or not at all.
 CALLS = [
     # B, n, hq, hkv, block_size, lens, causal, seed
     (32, 1, 16, 8, 256, [1024] * 32, True, 0),                    # decode-step shape: pairs split between CTAs
-    (6, 4, 16, 4, 64, [3000, 17, 2048, 1, 999, 4096], True, 1),   # 16 rows per KV head: the array-limited grid
-    (32, 1, 16, 8, 256, [1024] * 31 + [5], True, 2),              # the first shape again, after the second's leftovers
-    (1, 1, 8, 1, 256, [8192], False, 3),                          # one pair split over every CTA
+    (6, 4, 16, 4, 64, [3000, 17, 2048, 1, 999, 4096], True, 1),   # 16 rows per KV head, ragged lengths (U / 16 = 159)
+    (8, 4, 16, 4, 256, [8192] * 8, True, 5),                      # 16 rows per KV head, grid cut to what the array holds
+    (32, 1, 16, 8, 256, [1024] * 31 + [5], True, 2),              # the first shape again, after larger calls' leftovers
+    (1, 1, 8, 1, 256, [8192], False, 3),                          # one pair split over every CTA (U / 16 = 32)
 ]
 
 
