@@ -52,8 +52,9 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", default="fused8b", choices=["fused8b", "fused06b", "norm", "matmul", "gateup", "rowpar", "attn",
-                                                            "storekv", "decode"])
+    ap.add_argument("--workload", default="fused8b",
+                    choices=["fused8b", "fused06b", "norm", "rmsnorm", "addrmsnorm", "silu", "matmul", "gateup",
+                             "rowpar", "attn", "storekv", "decode"])
     ap.add_argument("--decode-worker", default=None, help=argparse.SUPPRESS)
     ap.add_argument("--decode-backends", default="b200,compile,triton_fused")
     ap.add_argument("--decode-batch", type=int, default=32)
@@ -61,6 +62,8 @@ def parse_args():
     ap.add_argument("--decode-tp", type=int, default=1, help="tensor-parallel ranks of the decode step (one GPU each)")
     ap.add_argument("--tokens", type=int, default=8192, help="tokens per step at N = 1")
     ap.add_argument("--scaling", choices=["weak", "strong"], default="weak")
+    ap.add_argument("--rank-shard-of", type=int, default=1,
+                    help="fused workloads on one GPU: run the shard one rank of this many GPUs would run")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-decode-step", action="store_true",
@@ -227,6 +230,11 @@ def fused_workload(args, rank, world, dev, hq_total, hkv_total, max_pos, num_blo
     from nanovllm_b200 import workloads
     from nanovllm_b200.kernels.qk_norm_rope_kv import qk_norm_rope_kv
 
+    if args.rank_shard_of > 1:
+        # One GPU runs the shard one rank of an N-GPU job would run (the weak-scaling batch of N x tokens, 8 / N kv
+        # heads): the per-rank kernel of config 3 at N GPUs, measured where a multi-GPU box is not at hand.
+        assert world == 1, "--rank-shard-of is a one-GPU option"
+        world = args.rank_shard_of
     T = args.tokens * (world if args.scaling == "weak" else 1)
     assert hkv_total % world == 0, "kv heads must divide across the GPUs"
     hq, hkv, d = hq_total // world, hkv_total // world, 128
@@ -305,25 +313,40 @@ def fused_workload(args, rank, world, dev, hq_total, hkv_total, max_pos, num_blo
                         "q_heads": hq_total, "kv_heads": hkv_total, "head_dim": d,
                         "kv_heads_per_gpu": hkv, "cache_blocks": blocks, "block_size": 256,
                         "max_position": max_pos, "skip_fraction": 0.05, "write_k": False,
-                        "parallelism": f"tp{world} (KV-head sharding, no collective)",
+                        "parallelism": f"tp{world} (KV-head sharding, no collective)" if args.rank_shard_of <= 1
+                        else f"one rank's shard of tp{world}, run alone on one GPU",
                         "l2": "flushed between timed steps (256 MiB write + 256 MiB read, outside the events)",
                         "bytes_formula": "T*((Hq+2Hkv)*D*2 read + 8 + 4 + D*4 + (Hq+2Hkv)*D*2 written) + 2*D*2"})
 
 
+NORM_OPS = {"norm": ("rms_norm", "add_rms_norm", "silu_and_mul"), "rmsnorm": ("rms_norm",),
+            "addrmsnorm": ("add_rms_norm",), "silu": ("silu_and_mul",)}
+
+
 def norm_workload(args, rank, world, dev):
+    """BASELINE config 2 at T = 8192 (hidden 1024, intermediate 3072): "norm" runs RMSNorm, Add+RMSNorm and SiLU x Mul
+    as one step (three launches); "rmsnorm", "addrmsnorm" and "silu" run one of them alone."""
     from nanovllm_b200 import workloads
     from nanovllm_b200.kernels.rms_norm import fused_add_rms_norm, rms_norm
     from nanovllm_b200.kernels.swiglu import silu_and_mul
+    ops = NORM_OPS[args.workload]
     T = args.tokens * (world if args.scaling == "weak" else 1)
     n, inter = 1024, 3072
     x = workloads.norm_inputs(T, n, seed=5, device=dev)
     gu = workloads.silu_inputs(T, inter, seed=6, device=dev)["x"]
-    units = (2 * T * n + n) * 2 + (4 * T * n + n) * 2 + 3 * T * inter * 2
+
+    def op_bytes(tokens):
+        b = {"rms_norm": (2 * tokens * n + n) * 2, "add_rms_norm": (4 * tokens * n + n) * 2,
+             "silu_and_mul": 3 * tokens * inter * 2}
+        return sum(b[o] for o in ops)
+
+    calls = {"rms_norm": lambda: rms_norm(x["x"], x["w"], x["eps"]),
+             "add_rms_norm": lambda: fused_add_rms_norm(x["x"], x["residual"], x["w"], x["eps"]),
+             "silu_and_mul": lambda: silu_and_mul(gu)}
 
     def launch():
-        rms_norm(x["x"], x["w"], x["eps"])
-        fused_add_rms_norm(x["x"], x["residual"], x["w"], x["eps"])
-        silu_and_mul(gu)
+        for o in ops:
+            calls[o]()
 
     xc = {}
 
@@ -331,16 +354,22 @@ def norm_workload(args, rank, world, dev):
         from oracle import reference_math as om
         if not xc:
             xc.update({k: (v.cpu() if torch.is_tensor(v) else v) for k, v in x.items()}, gu=gu.cpu())
-        om.rms_forward(xc["x"][:tokens], xc["w"], xc["eps"])
-        om.add_rms_forward(xc["x"][:tokens], xc["residual"][:tokens], xc["w"], xc["eps"])
-        om.silu_and_mul(xc["gu"][:tokens])
-        return (2 * tokens * n + n) * 2 + (4 * tokens * n + n) * 2 + 3 * tokens * inter * 2
+        if "rms_norm" in ops:
+            om.rms_forward(xc["x"][:tokens], xc["w"], xc["eps"])
+        if "add_rms_norm" in ops:
+            om.add_rms_forward(xc["x"][:tokens], xc["residual"][:tokens], xc["w"], xc["eps"])
+        if "silu_and_mul" in ops:
+            om.silu_and_mul(xc["gu"][:tokens])
+        return op_bytes(tokens)
 
-    return dict(launch=launch, units=units, e2e=None, cpu=cpu, unit="GB/s", scale=1e9, bound="hbm",
-                metric="rms_norm + add_rms_norm + silu_and_mul GB/s at T=8192", dtype="bf16", launches_per_step=3,
-                traffic_key="norm", config={"workload": "norm", "tokens_per_step": T, "hidden": n,
-                                            "intermediate": inter, "parallelism": f"replicas x{world}",
-                                            "l2": "flushed between timed steps"})
+    return dict(launch=launch, units=op_bytes(T), e2e=None, cpu=cpu, unit="GB/s", scale=1e9, bound="hbm",
+                metric=" + ".join(ops) + " GB/s at T=8192", dtype="bf16", launches_per_step=len(ops),
+                traffic_key=args.workload,
+                config={"workload": args.workload, "ops": list(ops), "tokens_per_step": T, "hidden": n,
+                        "intermediate": inter, "parallelism": f"replicas x{world}",
+                        "l2": "flushed between timed steps",
+                        "bytes_formula": "rms (2Tn+n)*2, add_rms (4Tn+n)*2, silu 3*T*inter*2 "
+                                         "(scripts/bench_norm_act.py:3-5)"})
 
 
 def matmul_workload(args, rank, world, dev):
@@ -566,7 +595,7 @@ def make_workload(args, rank, world, dev):
         return fused_workload(args, rank, world, dev, 32, 8, 32768, 1024, "fused8b")
     if args.workload == "fused06b":
         return fused_workload(args, rank, world, dev, 16, 8, 4096, 64, "fused06b")
-    if args.workload == "norm":
+    if args.workload in NORM_OPS:
         return norm_workload(args, rank, world, dev)
     if args.workload == "gateup":
         return gateup_workload(args, rank, world, dev)

@@ -72,34 +72,62 @@ NVB200_DEVICE uint32_t bf16x2_mul(uint32_t a, uint32_t b) {
 
 // SiLU x Mul on bf16, shared by the SiLU x Mul kernel and the gate_up GEMM epilogue.
 // Fast path: silu(g) rounded to bf16 depends only on the 16-bit g, so an estimate that lies close enough to
-// the exact fp32 value rounds the same way. __expf and __fdividef estimate g / (1 + exp(-g)) within a few tens of
-// fp32 ulps for |g| <= 16 (documented bounds: 2 + floor(1.173 |x|) ulps and 2 ulps); wherever the estimate's low
+// the exact fp32 value rounds the same way. The estimate g * rcp(1 + 2^(-g log2 e)) (the operations of __expf and
+// __fdividef, documented bounds 2 + floor(1.173 |x|) ulps and 2 ulps) lies within a few tens of fp32 ulps of the
+// exact value for |g| <= 16; wherever the estimate's low
 // 16 bits lie within kSiluMargin of the bf16 rounding midpoint 0x8000, or |g| > 16 (or g is not finite), the exact
-// expression is evaluated instead. Away from the midpoint, round-to-nearest-even is round-half-up on the bit
-// pattern. The exact path costs about twice the instructions (accurate expf, IEEE division) and kept the kernel
-// issue-bound below the memory roofline; the tests compare all 65,536 bf16 gate values with torch bit for bit.
+// expression is evaluated instead. Away from the midpoint the estimate and the exact value round to the same bf16.
+// The exact path costs about twice the instructions (accurate expf, IEEE division) and kept the kernel issue-bound
+// below the memory roofline; the tests compare all 65,536 bf16 gate values with torch bit for bit.
 constexpr float kSiluFastRange = 16.0f;
 constexpr uint32_t kSiluMargin = 64;
 
-NVB200_DEVICE uint32_t silu_bf16_bits(float g) {
-  const uint32_t b = __float_as_uint(__fdividef(g, 1.0f + __expf(-g)));
-  const uint32_t low = b & 0xFFFFu;
-  const uint32_t dist = low >= 0x8000u ? low - 0x8000u : 0x8000u - low;
-  if (fabsf(g) <= kSiluFastRange && dist > kSiluMargin) return (b + 0x8000u) >> 16;
-  return __bfloat16_as_ushort(__float2bfloat16_rn(g / (1.0f + expf(-g))));
+// 2^x and 1/x by the hardware approximations, flushing denormal inputs and results (never met by the fast path's
+// arguments: 2^(-g log2 e) and 1 + that lie in [1e-7, 1e7] for |g| <= 16). These are the operations __expf and
+// __fdividef are built on, minus their denormal handling.
+NVB200_DEVICE float ex2_approx_ftz(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+NVB200_DEVICE float rcp_approx_ftz(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// silu(g) rounded to bf16, as an fp32 value, by the exact expression (the fallback of the fast path).
+NVB200_DEVICE float silu_bf16_exact(float g) {
+  return bf16_lo(__bfloat16_as_ushort(__float2bfloat16_rn(g / (1.0f + expf(-g)))));
 }
 
 // Eight gate and eight up values (bf16) -> eight outputs: silu rounded to bf16, times up, rounded once
 // (mul.rn.bf16x2: the product of two bf16 values is exact in fp32, so this is torch's fp32 multiply then round).
+// The eight fast estimates are checked together: an estimate whose low 16 bits lie within kSiluMargin of 0x8000
+// (test: (b - (0x8000 - margin)) mod 2^16 <= 2 margin), or a gate outside the fast range, sends the thread through
+// the exact expression for the flagged elements only. Elsewhere the estimate rounds to the same bf16 as the exact
+// value under round-to-nearest-even (cvt.rn.bf16x2), since no exact tie lies outside the margin.
 NVB200_DEVICE uint4 silu_mul8_bf16(const uint4 &g, const uint4 &u) {
   const uint32_t gw[4] = {g.x, g.y, g.z, g.w}, uw[4] = {u.x, u.y, u.z, u.w};
+  float gf[8], est[8];
+  uint32_t flags = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    gf[i] = (i & 1) ? bf16_hi(gw[i >> 1]) : bf16_lo(gw[i >> 1]);
+    est[i] = gf[i] * rcp_approx_ftz(1.0f + ex2_approx_ftz(gf[i] * -1.4426950408889634f));  // g / (1 + e^-g)
+    const uint32_t b = __float_as_uint(est[i]);
+    const bool near_tie = ((b - (0x8000u - kSiluMargin)) & 0xFFFFu) <= 2 * kSiluMargin;
+    const bool out_of_range = !(fabsf(gf[i]) <= kSiluFastRange);
+    flags |= static_cast<uint32_t>(near_tie || out_of_range) << i;
+  }
+  if (flags != 0) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if (flags & (1u << i)) est[i] = silu_bf16_exact(gf[i]);
+  }
   uint32_t o[4];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const uint32_t lo = silu_bf16_bits(__uint_as_float(gw[i] << 16));
-    const uint32_t hi = silu_bf16_bits(__uint_as_float(gw[i] & 0xFFFF0000u));
-    o[i] = bf16x2_mul(lo | (hi << 16), uw[i]);
-  }
+  for (int i = 0; i < 4; ++i) o[i] = bf16x2_mul(pack_bf16x2(est[2 * i], est[2 * i + 1]), uw[i]);
   return make_uint4(o[0], o[1], o[2], o[3]);
 }
 

@@ -103,6 +103,16 @@ template <typename T> NVB200_DEVICE float norm_out(float v, float rstd, float w)
 
 template <typename T, int VEC> using RawVec = typename VecIO<T, VEC>::Raw;
 
+// Eight normalised bf16 outputs from fp32 values v, 1/rms and the raw bf16 weights: T(T(v * rstd) * w) as two
+// packed conversions and a bf16x2 multiply per pair (the bf16 x bf16 product is exact in fp32, so mul.rn.bf16x2
+// rounds it once, as torch's bf16 multiply does).
+NVB200_DEVICE uint4 norm8_bf16(const float (&v)[8], float rstd, const uint4 &w) {
+  return make_uint4(bf16x2_mul(pack_bf16x2(__fmul_rn(v[0], rstd), __fmul_rn(v[1], rstd)), w.x),
+                    bf16x2_mul(pack_bf16x2(__fmul_rn(v[2], rstd), __fmul_rn(v[3], rstd)), w.y),
+                    bf16x2_mul(pack_bf16x2(__fmul_rn(v[4], rstd), __fmul_rn(v[5], rstd)), w.z),
+                    bf16x2_mul(pack_bf16x2(__fmul_rn(v[6], rstd), __fmul_rn(v[7], rstd)), w.w));
+}
+
 // Loads this thread's vectors of one row (x, plus the residual for ADD, summed in fp32) and the matching weight
 // vectors (raw, issued with the row's loads so the store pass does not wait for them); returns the thread's
 // partial sum of squares.
@@ -136,12 +146,16 @@ NVB200_DEVICE void store_row(T *y, T *so, int n, int first, int step, float rstd
   for (int k = 0; k < kVecPerThread; ++k) {
     const int col = (first + k * step) * VEC;
     if (col < n) {
-      float wv[VEC], out[VEC];
-      VecIO<T, VEC>::unpack(wr[k], wv);
       if (ADD) VecIO<T, VEC>::store(so + col, v[k]);
+      if constexpr (std::is_same<T, __nv_bfloat16>::value && VEC == 8) {
+        *reinterpret_cast<uint4 *>(y + col) = norm8_bf16(v[k], rstd, wr[k]);
+      } else {
+        float wv[VEC], out[VEC];
+        VecIO<T, VEC>::unpack(wr[k], wv);
 #pragma unroll
-      for (int e = 0; e < VEC; ++e) out[e] = norm_out<T>(v[k][e], rstd, wv[e]);
-      VecIO<T, VEC>::store(y + col, out);
+        for (int e = 0; e < VEC; ++e) out[e] = norm_out<T>(v[k][e], rstd, wv[e]);
+        VecIO<T, VEC>::store(y + col, out);
+      }
     }
   }
 }
@@ -188,6 +202,110 @@ __global__ void __launch_bounds__(kMaxBlockThreads) block_row_norm_kernel(const 
   const float rstd = rsqrtf(tot / static_cast<float>(a.n) + a.eps);
   store_row<T, VEC, ADD>(static_cast<T *>(a.y) + row * a.n, ADD ? static_cast<T *>(a.res_out) + row * a.n : nullptr,
                          a.n, threadIdx.x, blockDim.x, rstd, v, wr);
+}
+
+// Large batches of short rows (up to 32 x kVecPerThread vectors, e.g. the 1024-element hidden of Qwen3-0.6B):
+// a persistent grid of as many CTAs as are resident at once, each warp taking rows (32 / L of them per step, L lanes
+// each) at a stride of the whole grid. A lane keeps its raw 16-byte vectors (x, and the residual for ADD) in
+// registers and issues the loads of its next row before it reduces and stores the current one, so every warp has
+// two rows in flight and no second wave waits for the first to drain (the one-row-per-warp kernel above ran 1.7
+// waves at 8192 rows). fp32 values are recomputed from the raw vectors in each pass instead of being held.
+template <typename T, int VEC, bool ADD>
+__global__ void __launch_bounds__(kRowThreads) row_norm_pipe_kernel(const __grid_constant__ RowArgs a) {
+  using Raw = RawVec<T, VEC>;
+  const int L = a.lanes;
+  const int lane = threadIdx.x & 31;
+  const int li = lane % L;
+  const int64_t step_rows = static_cast<int64_t>(gridDim.x) * (kRowThreads / L);
+  const int64_t warp_first = (static_cast<int64_t>(blockIdx.x) * (kRowThreads / 32) + (threadIdx.x >> 5)) * (32 / L);
+  const T *x = static_cast<const T *>(a.x);
+  const T *r = static_cast<const T *>(a.r);
+  const T *w = static_cast<const T *>(a.w);
+  Raw xc[kVecPerThread], rc[kVecPerThread], xn[kVecPerThread], rn[kVecPerThread];
+
+  auto load = [&](int64_t row, Raw (&xv)[kVecPerThread], Raw (&rv)[kVecPerThread]) {
+    if (row >= a.rows) return;
+    const T *xr = x + row_offset(a, row);
+    const T *rr = ADD ? r + row * a.r_row_stride : nullptr;
+#pragma unroll
+    for (int k = 0; k < kVecPerThread; ++k) {
+      const int col = (li + k * L) * VEC;
+      if (col < a.n) {
+        xv[k] = VecIO<T, VEC>::load_raw(xr + col);
+        if (ADD) rv[k] = VecIO<T, VEC>::load_raw(rr + col);
+      }
+    }
+  };
+  // Sum of x (+ residual) in fp32, as the unrounded value torch normalises.
+  auto value = [&](const Raw &xv, const Raw &rv, float (&v)[VEC]) {
+    VecIO<T, VEC>::unpack(xv, v);
+    if (ADD) {
+      float t[VEC];
+      VecIO<T, VEC>::unpack(rv, t);
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) v[e] = __fadd_rn(v[e], t[e]);
+    }
+  };
+
+  int64_t row = warp_first + lane / L;
+  load(row, xc, rc);
+  for (int64_t base = warp_first; base < a.rows; base += step_rows, row += step_rows) {
+    load(row + step_rows, xn, rn);
+    float ss = 0.f;
+    if (row < a.rows) {
+#pragma unroll
+      for (int k = 0; k < kVecPerThread; ++k) {
+        const int col = (li + k * L) * VEC;
+        if (col < a.n) {
+          float v[VEC];
+          value(xc[k], rc[k], v);
+          if (ADD) VecIO<T, VEC>::store(static_cast<T *>(a.res_out) + row * a.n + col, v);
+#pragma unroll
+          for (int e = 0; e < VEC; ++e) ss = fmaf(v[e], v[e], ss);
+        }
+      }
+    }
+    for (int o = L / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (row < a.rows) {
+      const float rstd = rsqrtf(ss / static_cast<float>(a.n) + a.eps);
+      T *y = static_cast<T *>(a.y) + row * a.n;
+#pragma unroll
+      for (int k = 0; k < kVecPerThread; ++k) {
+        const int col = (li + k * L) * VEC;
+        if (col < a.n) {
+          float v[VEC];
+          value(xc[k], rc[k], v);
+          if constexpr (std::is_same<T, __nv_bfloat16>::value && VEC == 8) {
+            *reinterpret_cast<uint4 *>(y + col) = norm8_bf16(v, rstd, __ldg(reinterpret_cast<const uint4 *>(w + col)));
+          } else {
+            float wv[VEC], out[VEC];
+            VecIO<T, VEC>::load(w + col, wv);
+#pragma unroll
+            for (int e = 0; e < VEC; ++e) out[e] = norm_out<T>(v[e], rstd, wv[e]);
+            VecIO<T, VEC>::store(y + col, out);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < kVecPerThread; ++k) {
+      xc[k] = xn[k];
+      if (ADD) rc[k] = rn[k];
+    }
+  }
+}
+
+// Resident CTAs per SM of a kernel with `threads` threads and no dynamic shared memory (cached per device).
+template <typename K> int resident_blocks(K kernel, int *cache, int threads = kRowThreads) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 1;
+  if (cache[dev] == 0) {
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, 0) != cudaSuccess || per_sm < 1)
+      per_sm = 1;
+    cache[dev] = per_sm;
+  }
+  return cache[dev];
 }
 
 // Rows longer than a CTA holds in registers: one CTA per row, sum of squares first, then a second pass.
@@ -243,6 +361,14 @@ template <typename T, int VEC, bool ADD> int launch_norm_vec(RowArgs &a, cudaStr
     const int64_t rows_per_block = kRowThreads / L;
     const int64_t blocks = (a.rows + rows_per_block - 1) / rows_per_block;
     if (blocks > 0x7fffffffLL) return NVB200_ERR_UNSUPPORTED;
+    static int resident[64] = {0};
+    const int64_t slots = static_cast<int64_t>(sm_count()) *
+                          resident_blocks(row_norm_pipe_kernel<T, VEC, ADD>, resident);
+    if (blocks > slots) {
+      // More rows than one wave holds: the persistent two-rows-in-flight kernel.
+      row_norm_pipe_kernel<T, VEC, ADD><<<static_cast<unsigned>(slots), kRowThreads, 0, stream>>>(a);
+      return launch_status();
+    }
     row_norm_kernel<T, VEC, ADD><<<static_cast<unsigned>(blocks), kRowThreads, 0, stream>>>(a);
     return launch_status();
   }
@@ -276,8 +402,7 @@ int elem_size(int dtype) { return dtype == NVB200_F32 ? 4 : 2; }
 
 // ---------------------------------------------------------------------------------------------------------------
 // SiLU x Mul: thread (x, y) owns vector column x of rows y, y + gridDim.y, ...: two 16-byte loads and one store per
-// step, no division on the index path. (Taking 4 rows per step, or prefetching the next row into registers,
-// measured no faster at 8192 rows.)
+// row (bf16: two rows per step), no division on the index path.
 
 template <typename T> NVB200_DEVICE float silu_mul(float g, float u) {
   // torch's silu: x / (1 + exp(-x)) in fp32, rounded to T; then T(silu * up) (exact product for 16-bit T).
@@ -294,7 +419,19 @@ __global__ void __launch_bounds__(kSiluThreads) silu_and_mul_kernel(T *out, cons
   const int cv = blockIdx.x * kSiluThreads + threadIdx.x;
   if (cv >= nv) return;
   const int col = cv * VEC;
-  for (int64_t r = blockIdx.y; r < rows; r += gridDim.y) {
+  int64_t r = blockIdx.y;
+  if constexpr (std::is_same<T, __nv_bfloat16>::value && VEC == 8) {
+    // Two rows per step: four 16-byte loads in flight per thread before the arithmetic.
+    const int64_t step = gridDim.y;
+    for (; r + step < rows; r += 2 * step) {
+      const T *s0 = x + r * x_row_stride + col, *s1 = s0 + step * x_row_stride;
+      const uint4 g0 = *reinterpret_cast<const uint4 *>(s0), u0 = *reinterpret_cast<const uint4 *>(s0 + n);
+      const uint4 g1 = *reinterpret_cast<const uint4 *>(s1), u1 = *reinterpret_cast<const uint4 *>(s1 + n);
+      *reinterpret_cast<uint4 *>(out + r * n + col) = silu_mul8_bf16(g0, u0);
+      *reinterpret_cast<uint4 *>(out + (r + step) * n + col) = silu_mul8_bf16(g1, u1);
+    }
+  }
+  for (; r < rows; r += gridDim.y) {
     const T *src = x + r * x_row_stride + col;
     if constexpr (std::is_same<T, __nv_bfloat16>::value && VEC == 8) {
       const uint4 g = *reinterpret_cast<const uint4 *>(src), u = *reinterpret_cast<const uint4 *>(src + n);
@@ -317,7 +454,11 @@ template <typename T> int launch_silu(void *out, const void *x, int64_t rows, in
   const int64_t nv = vec ? n / VEC : n;
   const int64_t gx = (nv + kSiluThreads - 1) / kSiluThreads;
   if (gx > 0x7fffffffLL) return NVB200_ERR_UNSUPPORTED;
-  const int64_t cap_y = std::max<int64_t>(1, static_cast<int64_t>(sm_count()) * 16 / gx);  // ~16 CTAs per SM
+  // As many CTAs as are resident at once (one wave), each column of CTAs striding over the rows.
+  static int resident[2][64] = {{0}};
+  const int per_sm = vec ? resident_blocks(silu_and_mul_kernel<T, VEC>, resident[0], kSiluThreads)
+                         : resident_blocks(silu_and_mul_kernel<T, 1>, resident[1], kSiluThreads);
+  const int64_t cap_y = std::max<int64_t>(1, static_cast<int64_t>(sm_count()) * per_sm / gx);
   const dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(std::min<int64_t>(std::min(rows, cap_y), 65535)));
   T *o = static_cast<T *>(out);
   const T *i = static_cast<const T *>(x);

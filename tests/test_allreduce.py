@@ -3,10 +3,13 @@ nanovllm_b200.parallel.RowParallelAllReduce) on two GPUs, one process each (NCCL
 the fp64 product of the full operands within bf16 tolerance, against the reference's path (matmul, then an NCCL
 all-reduce of the bf16 partials), and identical on both ranks; three calls per shape so both halves of the
 exchange buffers and increasing epochs are used; and three replays of a CUDA graph that captured one call, with
-new inputs each time. Needs two GPUs (skipped otherwise)."""
+new inputs each time; and a call that one rank skips, which must end on the other rank within its 1 s bound with
+NVB200_STATUS_WAIT_TIMEOUT set. Needs two GPUs (skipped otherwise)."""
+import datetime
 import math
 import os
 import socket
+import time
 
 import pytest
 import torch
@@ -94,3 +97,66 @@ def test_row_parallel_allreduce(tmp_path):
         scale = r["ref"].abs().max().item()
         torch.testing.assert_close(r["out"].double(), r["ref"], rtol=1.6e-2, atol=1e-2 * scale)
         torch.testing.assert_close(r["out"].double(), r["nccl"].double(), rtol=1.6e-2, atol=1e-2 * scale)
+
+
+def _skip_worker(rank, port, out_dir):
+    """Rank 1 skips the second of three calls. Rank 0's kernel then waits for a partial that never comes: its bounded
+    wait (1 s) must run out, set NVB200_STATUS_WAIT_TIMEOUT and return, so the host sees the failure and the context
+    stays usable. Both ranks then drop the exchange buffers (their epochs no longer agree) and set up new ones, and a
+    normal call must give the right result again. No rank leaves while a kernel or collective of its own is in
+    flight; NVLS is off (NCCL_NVLS_ENABLE=0) and the kernel exchanges data with plain peer stores and loads."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=WORLD, device_id=torch.device("cuda", rank),
+                            timeout=datetime.timedelta(seconds=60))
+    from nanovllm_b200 import _lib
+    from nanovllm_b200.parallel import RowParallelAllReduce
+    M, N, K = 32, 1024, 2048
+    k0, k1 = rank * K // WORLD, (rank + 1) * K // WORLD
+    g = torch.Generator(device="cuda").manual_seed(5)
+    a = (torch.randn(M, K, device="cuda", generator=g) / math.sqrt(K)).to(torch.bfloat16)
+    w = torch.randn(N, K, device="cuda", generator=g).to(torch.bfloat16)
+    a_r, b_r = a[:, k0:k1].contiguous(), w[:, k0:k1].t()
+    ref = (a.double() @ w.double().t()).cpu()
+    res = {}
+    _lib.status(clear=True)
+    ar = RowParallelAllReduce(max_n=N)
+    try:
+        out = ar(a_r, b_r)
+        torch.cuda.synchronize()
+        res["first"] = (out.cpu(), _lib.status(clear=True))
+        dist.barrier()
+        if rank == 0:
+            t0 = time.perf_counter()
+            out = ar(a_r, b_r)  # rank 1 never makes this call
+            torch.cuda.synchronize()
+            res["skipped"] = (_lib.status(clear=True), time.perf_counter() - t0)
+        dist.barrier()
+    finally:
+        ar.close()
+    dist.barrier()
+    ar = RowParallelAllReduce(max_n=N)
+    try:
+        out = ar(a_r, b_r)
+        torch.cuda.synchronize()
+        res["after"] = (out.cpu(), _lib.status(clear=True))
+    finally:
+        ar.close()
+        dist.barrier()
+        dist.destroy_process_group()
+    res["ref"] = ref
+    torch.save(res, os.path.join(out_dir, f"skip{rank}.pt"))
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < WORLD, reason="needs two GPUs")
+def test_missing_peer_times_out_and_the_group_recovers(tmp_path):
+    mp.start_processes(_skip_worker, args=(_free_port(), str(tmp_path)), nprocs=WORLD, start_method="spawn")
+    r0, r1 = (torch.load(tmp_path / f"skip{r}.pt") for r in range(WORLD))
+    scale = r0["ref"].abs().max().item()
+    for r in (r0, r1):
+        assert r["first"][1] == 0 and r["after"][1] == 0
+        torch.testing.assert_close(r["first"][0].double(), r["ref"], rtol=1.6e-2, atol=1e-2 * scale)
+        torch.testing.assert_close(r["after"][0].double(), r["ref"], rtol=1.6e-2, atol=1e-2 * scale)
+    status, seconds = r0["skipped"]
+    assert status & 4, status  # NVB200_STATUS_WAIT_TIMEOUT
+    assert 0.9 < seconds < 10, seconds  # the 1 s bound, then the call returned
