@@ -62,10 +62,16 @@ def parse_args():
     ap.add_argument("--decode-tp", type=int, default=1, help="tensor-parallel ranks of the decode step (one GPU each)")
     ap.add_argument("--tokens", type=int, default=8192, help="tokens per step at N = 1")
     ap.add_argument("--scaling", choices=["weak", "strong"], default="weak")
+    ap.add_argument("--attn-shape", default="32,1024,16,8",
+                    help="attn workload: sequences, keys per sequence, q heads, kv heads (default: the decode step)")
+    ap.add_argument("--attn-method", default="auto", choices=["auto", "cluster", "streamk"],
+                    help="attn workload: the drop-in's automatic choice, or one decode kernel")
     ap.add_argument("--rank-shard-of", type=int, default=1,
                     help="fused workloads on one GPU: run the shard one rank of this many GPUs would run")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-copy-reference", action="store_true",
+                    help="skip timing a torch copy of the same bytes beside an HBM-bound kernel")
     ap.add_argument("--no-decode-step", action="store_true",
                     help="skip the decode-step measurement the default (fused8b, one GPU) line carries")
     return ap.parse_args()
@@ -483,9 +489,10 @@ def attn_workload(args, rank, world, dev):
     previous one's keys in L2 even without the flush."""
     from nanovllm_b200.kernels.attention import flash_attn_with_kvcache
     from oracle import reference_math as om
-    B = 32 * (world if args.scaling == "weak" else 1)
-    hq, hkv, d, bs, ctx = 16 // world, 8 // world, 128, 256, 1024
-    pages = ctx // bs
+    B0, ctx, hq0, hkv0 = (int(v) for v in args.attn_shape.split(","))
+    B = B0 * (world if args.scaling == "weak" else 1)
+    hq, hkv, d, bs = hq0 // world, hkv0 // world, 128, 256
+    pages = (ctx + bs - 1) // bs
     nb = B * pages + 8
     g = torch.Generator(device=dev).manual_seed(17 + rank)
     copies = 4
@@ -498,10 +505,17 @@ def attn_workload(args, rank, world, dev):
     units = om.paged_decode_attention_bytes([ctx] * B, 1, hq, hkv, d, bs)
     step = [0]
 
+    from nanovllm_b200.kernels.attention import decode_attention
+
     def launch():
         kc, vc = caches[step[0] % copies]
         step[0] += 1
-        flash_attn_with_kvcache(q, kc, vc, cache_seqlens=seqlens, block_table=table, softmax_scale=scale, causal=True)
+        if args.attn_method == "auto":  # the drop-in, as the reference's Attention.forward calls it
+            flash_attn_with_kvcache(q, kc, vc, cache_seqlens=seqlens, block_table=table, softmax_scale=scale,
+                                    causal=True)
+        else:
+            decode_attention(q, kc, vc, seqlens, block_table=table, softmax_scale=scale, causal=True,
+                             method=args.attn_method)
 
     def library():
         import flash_attn
@@ -536,7 +550,7 @@ def attn_workload(args, rank, world, dev):
         return om.paged_decode_attention_bytes([ctx] * tokens, 1, hq, hkv, d, bs)
 
     return dict(launch=launch, units=units, e2e=e2e, cpu=cpu, unit="GB/s", scale=1e9, bound="hbm",
-                metric="paged decode attention GB/s (32 seqs x 1024 keys, Qwen3-0.6B heads)", dtype="bf16",
+                metric=f"paged decode attention GB/s ({B0} seqs x {ctx} keys, {hq0}/{hkv0} heads)", dtype="bf16",
                 launches_per_step=1, traffic_key="attn", library=("flash_attn.flash_attn_with_kvcache", library),
                 e2e_path="nanovllm_b200.kernels.attention.flash_attn_with_kvcache (public API) with pinned host q, "
                          "lengths and block table",
@@ -947,6 +961,31 @@ def main():
                            "note": "the kernel the reference itself runs for this op, same inputs, same L2 flush and "
                                    "step timing, this rank"}
 
+    if wl["bound"] == "hbm" and rank == 0 and not args.no_copy_reference:
+        # The same bytes moved by torch's copy (half read, half written), flushed and timed the same way: what a plain
+        # copy of this size achieves, launch and ramp-up included, beside the asymptotic copy peak of the roofline.
+        half = max(16, int(wl["units"]) // 2 // 16 * 16)
+        src = torch.empty(half, dtype=torch.uint8, device=dev).fill_(1)
+        dst = torch.empty_like(src)
+        cs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(50)]
+        with torch.inference_mode():
+            for _ in range(args.warmup):
+                flush_l2()
+                dst.copy_(src)
+            for a_, b_ in cs:
+                flush_l2()
+                a_.record(stream)
+                dst.copy_(src)
+                b_.record(stream)
+            torch.cuda.synchronize()
+        copy_s = sum(a_.elapsed_time(b_) for a_, b_ in cs) / 1e3 / len(cs)
+        ours_s = local_s / args.steps
+        copy_ref = {"us": 1e6 * copy_s, "gbs": 2 * half / copy_s / 1e9, "ours_frac_of_copy_rate": copy_s / ours_s,
+                    "note": "torch copy_ of the step's algorithmic bytes (half read, half written), same flush and "
+                            "event timing"}
+        del src, dst
+    else:
+        copy_ref = None
     if wl["bound"] == "hbm":
         peak = peaks["hbm_gbs"]
         roof_unit = "GB/s"
@@ -968,6 +1007,8 @@ def main():
         line["e2e"] = e2e
     if library is not None:
         line["library_comparison"] = library
+    if copy_ref is not None:
+        line["roofline"]["same_size_copy"] = copy_ref
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         torch.set_num_threads(os.cpu_count() or 1)
         full = wl["config"].get("tokens_per_step", wl["config"].get("M"))

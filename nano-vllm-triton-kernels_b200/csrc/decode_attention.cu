@@ -125,6 +125,11 @@ constexpr int smem_bytes(int R) { return kRingBytes + R * kHeadDim * 4 + kAttnWa
 constexpr int kSmemPerSm = 228 * 1024;
 constexpr int kFitBlocks = kSmemPerSm / (smem_bytes(kMaxRows) + 1024);
 constexpr int kMinBlocks = kFitBlocks > 0 ? kFitBlocks : 1;
+// CTAs per SM the cluster kernel's launch bounds ask for at R rows: as many as its shared memory allows, at most 3
+// (three at 1-8 rows, two at 16); the register budget per thread follows from it.
+constexpr int cluster_min_blocks(int R) {
+  return kSmemPerSm / (smem_bytes(R) + 1024) >= 3 ? 3 : (kSmemPerSm / (smem_bytes(R) + 1024) > 0 ? 2 : 1);
+}
 
 // Online-softmax state of one warp over R query rows (base 2, scores pre-scaled by scale * log2 e). Lane 2t + half
 // scores key t of a tile against half `half` of each query row; o[r][e] is output column 4 * lane + e of row r;
@@ -272,17 +277,175 @@ NVB200_DEVICE void merge_warp_records(const float *rec, int tid, float (&oc)[R],
   }
 }
 
+// ---------------------------------------------------------------------------------------------------------------
+// Tile fold on the tensor cores (the cluster kernel). Per 16-key tile a warp runs S = Q K^T and O += P V as warp-level
+// bf16 MMAs (m16n8k16, fp32 accumulation) with the query rows as the MMA's 16 rows (rows past R are zero), instead of
+// one FMA per key, dimension and row on the CUDA cores: about 130 instructions per tile instead of about 500, which is
+// what bounded the CUDA-core fold at the decode shape (few warps per SM, each issue-bound). The tiles are 16 x 16 and
+// 16 x 128, far below the 128-row tiles tcgen05.mma works on, and a warp owns its tile stream end to end, so the
+// warp-synchronous MMA fits here where a CTA-wide tcgen05 pipeline would not. K and V rows sit in shared memory with
+// the k_chunk swizzle, so the ldmatrix row addresses of each 8 x 8 matrix fall in distinct bank groups.
+// Fragment layout (lane = 4 g + t): A (16 x 16) a0 = (g, 2t..2t+1), a1 = (g + 8, 2t..), a2 = (g, 2t + 8..),
+// a3 = (g + 8, 2t + 8..); B (16 x 8) b0 = (2t..2t+1, g), b1 = (2t + 8.., g); C (16 x 8) c0, c1 = (g, 2t..2t+1),
+// c2, c3 = (g + 8, 2t..2t+1).
+
+NVB200_DEVICE void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+NVB200_DEVICE void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+NVB200_DEVICE void ldsm_x4_trans(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
+// One warp's online-softmax state for the MMA fold: lane 4 g + t holds rows g and g + 8 (index 0 and 1): running max
+// m (base 2, scaled scores), its share l of the row sums (the keys of its columns; summed over t at the end), and
+// o[n] = the C fragment of output columns 8 n .. 8 n + 7.
+struct MmaSoftmax {
+  float m[2], l[2], o[16][4];
+  NVB200_DEVICE void reset() {
+    m[0] = m[1] = -INFINITY, l[0] = l[1] = 0.f;
+#pragma unroll
+    for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+  }
+  NVB200_DEVICE void reduce_sums() {
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      l[i] += __shfl_xor_sync(0xffffffffu, l[i], 1);
+      l[i] += __shfl_xor_sync(0xffffffffu, l[i], 2);
+    }
+  }
+};
+
+// A fragments of the query block (rows r = i * group + gq, bf16 as stored, unscaled) for the 8 k-steps of head_dim
+// 128; rows at or past `rows` are zero.
+NVB200_DEVICE void load_q_frags(const AttnParams &p, int b, int h, int lane, uint32_t (&qa)[8][4]) {
+  const int g = lane >> 2, t = lane & 3;
+  const uint32_t *rowp[2] = {nullptr, nullptr};
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int r = g + 8 * i;
+    if (r < p.rows) {
+      const int qi = r / p.group, gq = r - qi * p.group;
+      rowp[i] = reinterpret_cast<const uint32_t *>(
+          p.q + static_cast<int64_t>(b) * p.q_batch_stride + static_cast<int64_t>(qi) * p.q_token_stride +
+          (static_cast<int64_t>(h) * p.group + gq) * p.q_head_stride);
+    }
+  }
+#pragma unroll
+  for (int ks = 0; ks < 8; ++ks) {
+    qa[ks][0] = rowp[0] ? __ldg(rowp[0] + 8 * ks + t) : 0u;
+    qa[ks][1] = rowp[1] ? __ldg(rowp[1] + 8 * ks + t) : 0u;
+    qa[ks][2] = rowp[0] ? __ldg(rowp[0] + 8 * ks + 4 + t) : 0u;
+    qa[ks][3] = rowp[1] ? __ldg(rowp[1] + 8 * ks + 4 + t) : 0u;
+  }
+}
+
+// Folds one 16-key tile (K tile at kt, V tile at kt + kTileBytes, both k_chunk-swizzled, landed and visible to the
+// warp) into the state. j0: index of the tile's first key; keys at or past je, or past a row's limit (lim0: row g,
+// lim1: row g + 8), get probability zero. scale: softmax_scale * log2(e). Ends with a __syncwarp, after which the
+// stage may be refilled.
+NVB200_DEVICE void fold_tile_mma(MmaSoftmax &st, uint32_t kt, const uint32_t (&qa)[8][4], int lane, int64_t j0,
+                                 int64_t je, int64_t lim0, int64_t lim1, float scale) {
+  const int t = lane & 3, mq = lane >> 3, rr = lane & 7;
+  // S = Q K^T: n-tile 0 holds keys 0-7, n-tile 1 keys 8-15. ldmatrix matrix mq: keys (mq >> 1) * 8 + rr, 16-byte
+  // chunk 2 ks + (mq & 1) of head_dim.
+  float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
+  const int kkey = (mq >> 1) * 8 + rr;
+  const uint32_t krow = kt + kkey * kRowBytes;
+#pragma unroll
+  for (int ks = 0; ks < 8; ++ks) {
+    uint32_t bk[4];
+    ldsm_x4(krow + k_chunk(kkey, 2 * ks + (mq & 1)) * 16, bk);
+    mma_16816(s0, qa[ks], bk[0], bk[1]);
+    mma_16816(s1, qa[ks], bk[2], bk[3]);
+  }
+  // sc[0..3]: row g at keys 2t, 2t + 1, 8 + 2t, 9 + 2t; sc[4..7]: row g + 8 at the same keys.
+  float sc[8] = {s0[0], s0[1], s1[0], s1[1], s0[2], s0[3], s1[2], s1[3]};
+  const int kj[4] = {2 * t, 2 * t + 1, 8 + 2 * t, 9 + 2 * t};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int64_t j = j0 + kj[i];
+    sc[i] = (j >= je || j > lim0) ? -INFINITY : sc[i] * scale;
+    sc[4 + i] = (j >= je || j > lim1) ? -INFINITY : sc[4 + i] * scale;
+  }
+  float alpha[2], pr[8];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    float mt = fmaxf(fmaxf(sc[4 * i], sc[4 * i + 1]), fmaxf(sc[4 * i + 2], sc[4 * i + 3]));
+    mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 1));
+    mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 2));
+    const float mn = fmaxf(st.m[i], mt);
+    const float mu = mn == -INFINITY ? 0.f : mn;  // no key seen yet: any finite reference keeps exp2 at 0
+    alpha[i] = exp2f(st.m[i] - mu);
+    st.m[i] = mn;
+    float sum = 0.f;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      pr[4 * i + e] = exp2f(sc[4 * i + e] - mu);
+      sum += pr[4 * i + e];
+    }
+    st.l[i] = fmaf(st.l[i], alpha[i], sum);
+  }
+  if (__any_sync(0xffffffffu, alpha[0] != 1.f || alpha[1] != 1.f)) {
+#pragma unroll
+    for (int n = 0; n < 16; ++n) {
+      st.o[n][0] *= alpha[0], st.o[n][1] *= alpha[0];
+      st.o[n][2] *= alpha[1], st.o[n][3] *= alpha[1];
+    }
+  }
+  // P as the A operand of O += P V (k = the tile's 16 keys): the C fragments of the two key n-tiles, in bf16.
+  const uint32_t pa[4] = {pack_bf16x2(pr[0], pr[1]), pack_bf16x2(pr[4], pr[5]), pack_bf16x2(pr[2], pr[3]),
+                          pack_bf16x2(pr[6], pr[7])};
+  // V as the B operand, transposed by ldmatrix: matrix mq holds keys (mq & 1) * 8 + rr, chunk 2 np + (mq >> 1).
+  const int vkey = (mq & 1) * 8 + rr;
+  const uint32_t vrow = kt + kTileBytes + vkey * kRowBytes;
+#pragma unroll
+  for (int np = 0; np < 8; ++np) {
+    uint32_t bv[4];
+    ldsm_x4_trans(vrow + k_chunk(vkey, 2 * np + (mq >> 1)) * 16, bv);
+    mma_16816(st.o[2 * np], pa, bv[0], bv[1]);
+    mma_16816(st.o[2 * np + 1], pa, bv[2], bv[3]);
+  }
+  __syncwarp();  // every lane is done with this stage before it is refilled
+}
+
+// Writes the warp's (o, m, l) for rows below R into records rec[warp][R][kStateStride] (after reduce_sums).
+template <int R> NVB200_DEVICE void store_warp_record_mma(const MmaSoftmax &st, float *rec, int warp, int lane) {
+  const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int r = g + 8 * i;
+    if (r >= R) continue;
+    float *w = rec + (warp * R + r) * kStateStride;
+#pragma unroll
+    for (int n = 0; n < 16; ++n)
+      *reinterpret_cast<float2 *>(w + 8 * n + 2 * t) = make_float2(st.o[n][2 * i], st.o[n][2 * i + 1]);
+    if (t == 0) w[kHeadDim] = st.m[i], w[kHeadDim + 1] = st.l[i];
+  }
+}
+
 template <int R>
-__global__ void __launch_bounds__(kAttnThreads, kMinBlocks) paged_decode_kernel(const __grid_constant__ AttnParams p) {
+__global__ void __launch_bounds__(kAttnThreads, cluster_min_blocks(R))
+    paged_decode_kernel(const __grid_constant__ AttnParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int h = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t rank = p.splits > 1 ? cta_rank_in_cluster() : 0u;  // == blockIdx.x: one cluster spans the x axis
-  float *q_s = reinterpret_cast<float *>(smem + kRingBytes);
-  float *p_w = q_s + R * kHeadDim + warp * kTileTokens * R;  // this warp's probabilities [kTileTokens][R]
-  const uint32_t q_addr = smem_addr(q_s), p_addr = smem_addr(p_w);
   const uint32_t wring = smem_addr(smem) + warp * (kStages * kStageBytes);
 
+  const int64_t bt_row = static_cast<int64_t>(b) * p.bt_stride;
+  int32_t bt_lane = 0;
+  if (p.splits == 1 && p.block_table && lane < p.max_pages) bt_lane = __ldg(p.block_table + bt_row + lane);
   // Keys of this sequence: [0, L), clamped to what its block-table row addresses.
   int64_t L = p.seqlens[b];
   const int64_t cap = static_cast<int64_t>(p.max_pages) * p.block_size;
@@ -295,15 +458,24 @@ __global__ void __launch_bounds__(kAttnThreads, kMinBlocks) paged_decode_kernel(
   const int64_t js = min(L, static_cast<int64_t>(rank) * per), je = min(L, js + per);
   const int ntiles = static_cast<int>((je - js + kTileTokens - 1) / kTileTokens);
   const int my_tiles = warp < ntiles ? (ntiles - warp + kAttnWarps - 1) / kAttnWarps : 0;
-  const int64_t bt_row = static_cast<int64_t>(b) * p.bt_stride;
+  // The block-table entries of the share's first 32 pages, one per lane, loaded once: a tile's copy then needs no
+  // table read of its own (which would put a round trip to L2 in front of every tile's copies). Without a split the
+  // share starts at key 0, so they were loaded above, together with the length.
+  const int64_t page0 = js / p.block_size;
+  if (p.splits > 1 && p.block_table && page0 + lane < p.max_pages)
+    bt_lane = __ldg(p.block_table + bt_row + page0 + lane);
 
   // Copies this warp's i-th tile (keys js + (warp + 4 i) * 16 + [0, 16)) into ring stage `stage`.
   auto issue = [&](int i, int stage) {
     const int64_t j = js + static_cast<int64_t>(warp + i * kAttnWarps) * kTileTokens + (lane & 15);
     int64_t off = -1;  // element offset of key j's row for head h; -1 = not read (zero-filled)
+    const int64_t page = j / p.block_size;
+    const int64_t rel = page - page0;
+    const int32_t cached = __shfl_sync(0xffffffffu, bt_lane, static_cast<int>(rel < 31 ? rel : 31));
     if (j < je) {
-      const int64_t page = j / p.block_size;
-      const int64_t blk = p.block_table ? static_cast<int64_t>(__ldg(p.block_table + bt_row + page)) : b;
+      const int64_t blk = !p.block_table ? b
+                          : rel < 32     ? static_cast<int64_t>(cached)
+                                         : static_cast<int64_t>(__ldg(p.block_table + bt_row + page));
       if (blk >= 0 && blk < p.num_blocks)
         off = blk * p.blk_stride + (j - page * p.block_size) * p.tok_stride + static_cast<int64_t>(h) * p.head_stride;
       else if (lane < 16)
@@ -316,7 +488,8 @@ __global__ void __launch_bounds__(kAttnThreads, kMinBlocks) paged_decode_kernel(
       const long long o = __shfl_sync(0xffffffffu, static_cast<long long>(off), row);
       const bool ok = o >= 0;
       cp_async16(dst + row * kRowBytes + k_chunk(row, c) * 16, p.k_cache + (ok ? o + c * 8 : 0), ok ? 16u : 0u);
-      cp_async16(dst + kTileBytes + row * kRowBytes + c * 16, p.v_cache + (ok ? o + c * 8 : 0), ok ? 16u : 0u);
+      cp_async16(dst + kTileBytes + row * kRowBytes + k_chunk(row, c) * 16, p.v_cache + (ok ? o + c * 8 : 0),
+                 ok ? 16u : 0u);
     }
   };
 #pragma unroll
@@ -325,23 +498,18 @@ __global__ void __launch_bounds__(kAttnThreads, kMinBlocks) paged_decode_kernel(
     cp_async_commit();
   }
 
-  // Query rows r = i * group + g (query i, q head h * group + g), fp32, scaled; rows past `rows` are zero.
-  for (int i = tid; i < R * kHeadDim; i += kAttnThreads) {
-    const int r = i / kHeadDim, d = i % kHeadDim;
-    float x = 0.f;
-    if (r < p.rows) {
-      const int qi = r / p.group, g = r - qi * p.group;
-      const int64_t at = static_cast<int64_t>(b) * p.q_batch_stride + static_cast<int64_t>(qi) * p.q_token_stride +
-                         (static_cast<int64_t>(h) * p.group + g) * p.q_head_stride + d;
-      x = __bfloat162float(p.q[at]) * p.scale_log2;
-    }
-    q_s[q_index(r, d)] = x;
+  // Query rows r = i * group + g (query i, q head h * group + g) as MMA A fragments; rows past `rows` are zero.
+  uint32_t qa[8][4];
+  load_q_frags(p, b, h, lane, qa);
+  // Key limits of this lane's two rows (g and g + 8).
+  int64_t lim[2];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int r = (lane >> 2) + 8 * i;
+    const int qi = r < p.rows ? r / p.group : p.sq - 1;
+    lim[i] = p.causal ? L - p.sq + qi : L - 1;
   }
-  __syncthreads();
-
-  int64_t lim[R];
-  row_limits<R>(lim, L, p.rows, p.group, p.sq, p.causal);
-  WarpSoftmax<R> st;
+  MmaSoftmax st;
   st.reset();
 
   for (int i = 0; i < my_tiles; ++i) {
@@ -349,16 +517,16 @@ __global__ void __launch_bounds__(kAttnThreads, kMinBlocks) paged_decode_kernel(
     cp_async_commit();
     cp_async_wait<kStages - 1>();  // this lane's copies of tile i have landed
     __syncwarp();                  // ... and every other lane's
-    fold_tile<R>(st, wring + (i % kStages) * kStageBytes, q_addr, p_w, p_addr, lane,
-                 js + static_cast<int64_t>(warp + i * kAttnWarps) * kTileTokens, je, lim);
+    fold_tile_mma(st, wring + (i % kStages) * kStageBytes, qa, lane,
+                  js + static_cast<int64_t>(warp + i * kAttnWarps) * kTileTokens, je, lim[0], lim[1], p.scale_log2);
   }
   cp_async_wait<0>();
   st.reduce_sums();
-  __syncthreads();  // every warp is done with its ring, queries and probabilities: the records below reuse them
+  __syncthreads();  // every warp is done with its ring: the records below reuse it
 
   // Merge the warps: record (o, m, l) per warp and row, then thread d combines column d.
   float *rec = reinterpret_cast<float *>(smem);  // [kAttnWarps][R][kStateStride]
-  store_warp_record<R>(st, rec, warp, lane);
+  store_warp_record_mma<R>(st, rec, warp, lane);
   __syncthreads();
   float oc[R], mc[R], lc[R];
   merge_warp_records<R>(rec, tid, oc, mc, lc);
