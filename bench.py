@@ -60,10 +60,14 @@ def parse_args():
     ap.add_argument("--decode-batch", type=int, default=32)
     ap.add_argument("--decode-ctx", type=int, default=1024)
     ap.add_argument("--decode-tp", type=int, default=1, help="tensor-parallel ranks of the decode step (one GPU each)")
+    ap.add_argument("--decode-profile", action="store_true",
+                    help="with --decode-worker: replay the decode graph once between cudaProfilerStart/Stop, untimed")
     ap.add_argument("--tokens", type=int, default=8192, help="tokens per step at N = 1")
     ap.add_argument("--scaling", choices=["weak", "strong"], default="weak")
     ap.add_argument("--attn-shape", default="32,1024,16,8",
                     help="attn workload: sequences, keys per sequence, q heads, kv heads (default: the decode step)")
+    ap.add_argument("--gateup-shape", default="4096,4096,12288",
+                    help="gateup workload: M, K, intermediate size (default: Qwen3-8B MLP at M = 4096)")
     ap.add_argument("--attn-method", default="auto", choices=["auto", "cluster", "streamk"],
                     help="attn workload: the drop-in's automatic choice, or one decode kernel")
     ap.add_argument("--rank-shard-of", type=int, default=1,
@@ -88,9 +92,12 @@ def load_peaks():
 def reference_kernel_module(name):
     """The reference's own Triton module nanovllm/kernels/<name>.py from its offline install (baseline/_ref), loaded
     by file so that the package's engine imports are not pulled in. Returns (module, None) or (None, why not)."""
-    path = os.path.join(ROOT, "baseline", "_ref", "nanovllm", "kernels", name + ".py")
+    ref = os.path.join(ROOT, "baseline", "_ref")
+    path = os.path.join(ref, "nanovllm", "kernels", name + ".py")
     if not os.path.exists(path):
         return None, "the reference is not installed in baseline/_ref"
+    if ref not in sys.path:  # some kernel modules import the package's own helpers
+        sys.path.append(ref)
     try:
         spec = importlib.util.spec_from_file_location(f"_reference_kernels_{name}", path)
         mod = importlib.util.module_from_spec(spec)
@@ -416,7 +423,7 @@ def gateup_workload(args, rank, world, dev):
     ([4096, 2 x 12288]) -> [4096, 12288], one kernel (nvb200_matmul_silu_and_mul). Column-parallel shards split the
     intermediate size (each rank its gate and up columns), as MergedColumnParallelLinear does."""
     from nanovllm_b200.kernels.matmul import matmul_silu_and_mul
-    M, K, inter = 4096, 4096, 12288
+    M, K, inter = (int(v) for v in args.gateup_shape.split(","))
     n_local = inter // world if args.scaling == "strong" else inter
     g = torch.Generator(device=dev).manual_seed(11)
     a = (torch.randn(M, K, device=dev, generator=g) / K ** 0.5).to(torch.bfloat16)
@@ -426,6 +433,15 @@ def gateup_workload(args, rank, world, dev):
 
     def launch():
         matmul_silu_and_mul(a, b)
+
+    # What the reference's Qwen3MLP runs (models/qwen3.py:133-137): the gate_up projection (F.linear: cuBLAS), then
+    # SiluAndMul (its Triton kernel, nanovllm/kernels/swiglu.py, under the triton backends).
+    mod, why = reference_kernel_module("swiglu")
+    if mod is None:
+        library = ("cuBLAS gate_up GEMM + reference Triton silu_and_mul", why)
+    else:
+        library = ("cuBLAS gate_up GEMM (torch.matmul) + reference Triton silu_and_mul (nanovllm/kernels/swiglu.py:"
+                   "34-43, baseline/_ref)", lambda: mod.silu_and_mul(a @ b))
 
     xc = {}
 
@@ -437,8 +453,8 @@ def gateup_workload(args, rank, world, dev):
         return 2 * tokens * 2 * n_local * K
 
     return dict(launch=launch, units=units, e2e=None, cpu=cpu, unit="TFLOP/s", scale=1e12, bound="tensor",
-                metric="gate_up GEMM + SiLU x Mul bf16 TFLOP/s (Qwen3-8B MLP, M=4096)", dtype="bf16",
-                launches_per_step=1, traffic_key="gateup",
+                metric=f"gate_up GEMM + SiLU x Mul bf16 TFLOP/s (M={M}, K={K}, intermediate {inter})", dtype="bf16",
+                launches_per_step=1, traffic_key="gateup", library=library,
                 config={"workload": "gateup", "M": M, "K": K, "intermediate": n_local,
                         "b_layout": "[gate | up] weight.t() (K-major)", "parallelism": f"column-parallel x{world}",
                         "l2": "flushed between timed steps"})
@@ -698,7 +714,7 @@ QWEN3_06B = {"architectures": ["Qwen3ForCausalLM"], "model_type": "qwen3", "hidd
              "hidden_act": "silu", "attention_bias": False}
 
 
-def decode_worker(backend: str, bs: int, ctx: int, tp: int = 1) -> dict:
+def decode_worker(backend: str, bs: int, ctx: int, tp: int = 1, profile_one: bool = False) -> dict:
     """One rank of the decode-step measurement (tp > 1: launched once per GPU by torch.distributed.run; the
     reference's ModelRunner then forms its own NCCL group, and every rank replays its graph in step with the others,
     as the reference's worker processes would)."""
@@ -759,6 +775,17 @@ def decode_worker(backend: str, bs: int, ctx: int, tp: int = 1) -> dict:
         gv["context_lens"].zero_()
         gv["context_lens"][:bs] = ctx + 1
         graph = runner.graphs[("target", 1, bs)]
+        if profile_one:
+            # One replay between cudaProfilerStart/Stop, for `ncu --profile-from-start off --graph-profiling node`:
+            # the launch list of one decode step, kernel by kernel.
+            for _ in range(3):
+                graph.replay()
+            torch.cuda.synchronize()
+            torch.cuda.cudart().cudaProfilerStart()
+            graph.replay()
+            torch.cuda.synchronize()
+            torch.cuda.cudart().cudaProfilerStop()
+            return {"backend": backend, "profiled_replays": 1}
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         if tp > 1:
             mr.dist.barrier()
@@ -862,7 +889,8 @@ def run_decode(args) -> None:
 def main():
     args = parse_args()
     if args.decode_worker:
-        res = decode_worker(args.decode_worker, args.decode_batch, args.decode_ctx, args.decode_tp)
+        res = decode_worker(args.decode_worker, args.decode_batch, args.decode_ctx, args.decode_tp,
+                            args.decode_profile)
         if res is not None:
             print(json.dumps(res), flush=True)
         return

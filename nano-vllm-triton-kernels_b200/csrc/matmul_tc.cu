@@ -818,6 +818,8 @@ struct SkinnyParams {
   uint32_t idesc;
   int elem_bytes;
   int c_is_f32;
+  int swiglu;       // 1: gate_up GEMM with the SiLU x Mul epilogue (B holds 2 N columns, gate | up; a tile is the 64
+                    // gate columns n0 .. n0 + 63 and the matching 64 up columns; C = silu(gate) * up, [M, N] bf16)
   int red_off;      // shared-memory offset of the partial slots [S][m_pad][128 / S] fp32 (S > 1, or all-reduce)
   int hdr_off;      // barriers and the TMEM slot
   int32_t *status;
@@ -856,14 +858,30 @@ NVB200_DEVICE void store_c(const SkinnyParams &p, int m, int n, float v) {
     static_cast<__nv_bfloat16 *>(p.c)[idx] = __float2bfloat16_rn(v);
 }
 
-// One stage of the skinny kernel: nsub consecutive K blocks from kb, each [B^T tile | A tile].
+// One stage of the skinny kernel: nsub consecutive K blocks from kb, each [B^T tile | A tile]. With up0 >= 0 (the
+// gate_up form) the B^T tile is two 64-row boxes: the gate rows from n0 and the up rows from up0.
 NVB200_DEVICE void skinny_load_stage(const CUtensorMap &map_w, const CUtensorMap &map_x, uint32_t full, uint32_t sw,
-                                     int kb, int nsub, uint32_t sub_bytes, uint32_t tile_w, int BK, int n0) {
+                                     int kb, int nsub, uint32_t sub_bytes, uint32_t tile_w, int BK, int n0, int up0) {
   mbar_arrive_expect_tx(full, nsub * sub_bytes);
   for (int u = 0; u < nsub; ++u) {
     tma_load_2d(sw + u * sub_bytes, &map_w, (kb + u) * BK, n0, full);
+    if (up0 >= 0) tma_load_2d(sw + u * sub_bytes + tile_w / 2, &map_w, (kb + u) * BK, up0, full);
     tma_load_2d(sw + u * sub_bytes + tile_w, &map_x, (kb + u) * BK, 0, full);
   }
+}
+
+// out[m, n] for the 4 consecutive columns n .. n + 3 of row m from gate and up sums in fp32: each rounded to bf16,
+// then the SiLU x Mul routine of the two-step form (so the result is bitwise that of the GEMM into bf16 followed by
+// nvb200_silu_and_mul). Columns at or past N are not stored.
+NVB200_DEVICE void store_swiglu4(const SkinnyParams &p, int m, int n, const float (&g)[4], const float (&u)[4]) {
+  const uint4 gv = make_uint4(pack_bf16x2(g[0], g[1]), pack_bf16x2(g[2], g[3]), 0u, 0u);
+  const uint4 uv = make_uint4(pack_bf16x2(u[0], u[1]), pack_bf16x2(u[2], u[3]), 0u, 0u);
+  const uint4 o = silu_mul8_bf16(gv, uv);
+  __nv_bfloat16 *c = static_cast<__nv_bfloat16 *>(p.c) + m * p.scm + n;
+  const uint32_t w[2] = {o.x, o.y};
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    if (n + i < p.N) c[i] = __ushort_as_bfloat16(static_cast<unsigned short>(i & 1 ? w[i >> 1] >> 16 : w[i >> 1] & 0xFFFFu));
 }
 
 template <bool TF32>
@@ -876,7 +894,10 @@ __global__ void __launch_bounds__(kSkinnyThreads)
   const int lane = threadIdx.x & 31;
   const uint32_t rank = cluster_rank();
   const int S = p.split;
-  const int n0 = (blockIdx.x / S) * BM;  // first row of B^T (column of C) of this tile
+  // First row of B^T (column of C) of this tile; the gate_up form's tiles are 64 gate rows and the 64 matching up
+  // rows, which start at up0.
+  const int n0 = (blockIdx.x / S) * (p.swiglu ? BM / 2 : BM);
+  const int up0 = p.swiglu ? p.N + n0 : -1;
   const int BK = 128 / p.elem_bytes;
   const uint32_t tile_w = BM * 128, tile_x = static_cast<uint32_t>(p.m_pad) * 128;
   const uint32_t sub_bytes = tile_w + tile_x;  // one K block: [B^T tile | A tile]
@@ -907,7 +928,7 @@ __global__ void __launch_bounds__(kSkinnyThreads)
     fence_mbar_init();
     for (int i = 0; pkb < kb_end && i < stages; ++i, pkb += kpb, pst = pst + 1 == stages ? 0 : pst + 1, pph ^= pst == 0)
       skinny_load_stage(map_w, map_x, bar_full + 8 * pst, stage0 + pst * stage_bytes, pkb, min(kpb, kb_end - pkb),
-                        sub_bytes, tile_w, BK, n0);
+                        sub_bytes, tile_w, BK, n0, up0);
   }
   if (warp == 1) tmem_alloc(smem_addr(tmem_slot), tmem_cols);
   tc_fence_before();
@@ -924,7 +945,7 @@ __global__ void __launch_bounds__(kSkinnyThreads)
         break;
       }
       skinny_load_stage(map_w, map_x, bar_full + 8 * pst, stage0 + pst * stage_bytes, pkb, min(kpb, kb_end - pkb),
-                        sub_bytes, tile_w, BK, n0);
+                        sub_bytes, tile_w, BK, n0, up0);
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
@@ -965,7 +986,40 @@ __global__ void __launch_bounds__(kSkinnyThreads)
   const int rows = BM / S;                          // rows of C^T this CTA finishes (its cluster slice)
   const int o0 = static_cast<int>(rank) * rows;      // first of them
   float *part = reinterpret_cast<float *>(smem + p.red_off);  // all-reduce: this CTA's partial, [m][rows]
-  if (S == 1) {
+  if (S == 1 && p.swiglu) {
+    // Lanes 64-127 (the up columns) hand their sums to lanes 0-63 (the gate columns) through shared memory, 32 rows
+    // at a time ([32][64] fp32); thread nt < 64 then finishes column n0 + nt of those rows, 4 rows per step.
+    float *xch = reinterpret_cast<float *>(smem + p.red_off);
+    const int n = n0 + nt;
+    for (int c0 = 0; c0 < p.m_pad; c0 += 32) {
+      float v[32];
+      tmem_ld32(taddr + c0, v);
+      if (nt >= BM / 2) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) xch[i * (BM / 2) + nt - BM / 2] = v[i];
+      }
+      __syncthreads();
+      if (nt < BM / 2 && n < p.N) {
+#pragma unroll
+        for (int i = 0; i < 32; i += 4) {
+          if (c0 + i >= p.M) break;
+          const uint4 gv = make_uint4(pack_bf16x2(v[i], v[i + 1]), pack_bf16x2(v[i + 2], v[i + 3]), 0u, 0u);
+          const uint4 uv = make_uint4(pack_bf16x2(xch[i * (BM / 2) + nt], xch[(i + 1) * (BM / 2) + nt]),
+                                      pack_bf16x2(xch[(i + 2) * (BM / 2) + nt], xch[(i + 3) * (BM / 2) + nt]), 0u, 0u);
+          const uint4 o = silu_mul8_bf16(gv, uv);
+          const uint32_t w[2] = {o.x, o.y};
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            if (c0 + i + e < p.M)
+              static_cast<__nv_bfloat16 *>(p.c)[(c0 + i + e) * p.scm + n] =
+                  __ushort_as_bfloat16(static_cast<unsigned short>(e & 1 ? w[e >> 1] >> 16 : w[e >> 1] & 0xFFFFu));
+        }
+      }
+      __syncthreads();  // the gate lanes are done with xch before the next 32 rows overwrite it
+    }
+    tc_fence_before();
+    __syncthreads();  // every TMEM read done before the columns are freed
+  } else if (S == 1) {
     const int n = n0 + nt;
     for (int c0 = 0; c0 < p.m_pad; c0 += 32) {
       float v[32];
@@ -983,10 +1037,15 @@ __global__ void __launch_bounds__(kSkinnyThreads)
     tc_fence_before();
     __syncthreads();  // every TMEM read done before the columns are freed (and the partial complete)
   } else {
-    // Push this CTA's partial of row nt to its owner: slot [rank][m][nt - owner * rows] of the owner's buffer.
-    const int owner = nt / rows;
+    // Push this CTA's partial of row nt to its owner: slot [rank][m][nt - owner * rows] of the owner's buffer. In
+    // the gate_up form, owner r takes the gate rows r * (64 / S) ... and the matching up rows: its slot row i is gate
+    // row r * (64 / S) + i for i < 64 / S, then up row 64 + r * (64 / S) + (i - 64 / S).
+    const int half = rows / 2;  // gate_up form: gate (and up) rows per owner
+    const int owner = p.swiglu ? (nt & (BM / 2 - 1)) / half : nt / rows;
+    const int local = p.swiglu ? (nt < BM / 2 ? nt - owner * half : half + (nt - BM / 2) - owner * half)
+                               : nt - owner * rows;
     const uint32_t dst = map_to_cta(smem_addr(smem + p.red_off), owner) +
-                         static_cast<uint32_t>((static_cast<int>(rank) * p.m_pad * rows + (nt - owner * rows)) * 4);
+                         static_cast<uint32_t>((static_cast<int>(rank) * p.m_pad * rows + local) * 4);
     for (int c0 = 0; c0 < p.m_pad; c0 += 32) {
       float v[32];
       tmem_ld32(taddr + c0, v);
@@ -1000,7 +1059,23 @@ __global__ void __launch_bounds__(kSkinnyThreads)
     // Sum the S slots of this CTA's rows, 4 consecutive rows (columns n of C) per step. With an all-reduce to
     // follow, the sum goes back into slot 0 (the same thread read it) as this GPU's partial.
     float *red = reinterpret_cast<float *>(smem + p.red_off);
-    const int qpr = rows / 4;
+    if (p.swiglu) {
+      // Owner: gate and up sums of its 64 / S columns n0 + rank * (64 / S) + [0, 64 / S), 4 columns per step.
+      const int qpg = half / 4;
+      for (int gi = threadIdx.x; gi < p.M * qpg; gi += kSkinnyThreads) {
+        const int m = gi / qpg, q = gi - m * qpg;
+        float g4[4] = {0.f, 0.f, 0.f, 0.f}, u4[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int r = 0; r < S; ++r) {
+          const float *row = red + (r * p.m_pad + m) * rows;
+          const float4 x = *reinterpret_cast<const float4 *>(row + 4 * q);
+          const float4 y = *reinterpret_cast<const float4 *>(row + half + 4 * q);
+          g4[0] += x.x, g4[1] += x.y, g4[2] += x.z, g4[3] += x.w;
+          u4[0] += y.x, u4[1] += y.y, u4[2] += y.z, u4[3] += y.w;
+        }
+        store_swiglu4(p, m, n0 + static_cast<int>(rank) * half + 4 * q, g4, u4);
+      }
+    }
+    const int qpr = p.swiglu ? 0 : rows / 4;
     for (int gi = threadIdx.x; gi < p.M * qpr; gi += kSkinnyThreads) {
       const int m = gi / qpr, q = gi - m * qpr;
       float acc[4] = {0.f, 0.f, 0.f, 0.f};
@@ -1110,8 +1185,9 @@ __global__ void __launch_bounds__(kSkinnyThreads)
 // NVB200_ERR_UNSUPPORTED otherwise.
 int launch_skinny(void *c, const void *a, const void *b, int64_t M, int64_t N, int64_t K, int64_t sam, int64_t sbn,
                   int64_t scm, int64_t scn, bool f32, int32_t *status, cudaStream_t stream,
-                  const nvb200_allreduce_group *ar = nullptr) {
+                  const nvb200_allreduce_group *ar = nullptr, bool swiglu = false) {
   if (M > kSkinnyMaxM || M <= 0) return NVB200_ERR_UNSUPPORTED;
+  if (swiglu && (f32 || ar != nullptr || scn != 1)) return NVB200_ERR_UNSUPPORTED;
   const int es = f32 ? 4 : 2;
   const int BK = 128 / es;
   SkinnyParams p{};
@@ -1120,7 +1196,9 @@ int launch_skinny(void *c, const void *a, const void *b, int64_t M, int64_t N, i
   p.m_pad = static_cast<int>((M + 15) / 16 * 16);
   p.k_blocks = static_cast<int>((K + BK - 1) / BK);
   p.elem_bytes = es, p.c_is_f32 = f32, p.status = status;
-  const int tiles = static_cast<int>((N + BM - 1) / BM);
+  p.swiglu = swiglu ? 1 : 0;
+  const int tile_cols = swiglu ? BM / 2 : BM;  // output columns per tile
+  const int tiles = static_cast<int>((N + tile_cols - 1) / tile_cols);
   const int sms = sm_count();
   int split = 1;
   while (split < 8 && static_cast<int64_t>(tiles) * split * 2 <= sms && split * 2 <= p.k_blocks) split *= 2;
@@ -1137,7 +1215,8 @@ int launch_skinny(void *c, const void *a, const void *b, int64_t M, int64_t N, i
     }
   }
   CUtensorMap map_w, map_x;
-  if (!make_map(&map_w, b, f32, K, N, sbn, BK, BM) || !make_map(&map_x, a, f32, K, M, sam, BK, p.m_pad))
+  if (!make_map(&map_w, b, f32, K, swiglu ? 2 * N : N, sbn, BK, swiglu ? BM / 2 : BM) ||
+      !make_map(&map_x, a, f32, K, M, sam, BK, p.m_pad))
     return NVB200_ERR_UNSUPPORTED;
   const uint32_t fmt = f32 ? 2u : 1u;
   p.idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | (static_cast<uint32_t>(p.m_pad >> 3) << 17) |
@@ -1152,7 +1231,8 @@ int launch_skinny(void *c, const void *a, const void *b, int64_t M, int64_t N, i
   const int ring_budget = split > 1 ? 160 * 1024 : 72 * 1024;
   p.stages = std::max(1, std::min({kSkinnyMaxStages, (blocks_per_cta + p.kpb - 1) / p.kpb, ring_budget / stage_bytes}));
   p.red_off = p.stages * stage_bytes;
-  p.hdr_off = p.red_off + (split > 1 || p.ar_world > 1 ? p.m_pad * BM * 4 : 0);
+  // Partial slots (K split, all-reduce) or the gate_up form's exchange of 32 rows of up sums.
+  p.hdr_off = p.red_off + (split > 1 || p.ar_world > 1 ? p.m_pad * BM * 4 : (swiglu ? 32 * (BM / 2) * 4 : 0));
   const int smem = 1024 + p.hdr_off + 256;
   const int rc = f32 ? configure_once(matmul_skinny_kernel<true>, smem, 2) : configure_once(matmul_skinny_kernel<false>, smem, 3);
   if (rc) return rc;
@@ -1197,8 +1277,8 @@ int tc_launch(void *c, const void *a, const void *b, int64_t M, int64_t N, int64
   else if (sbn == 1 && (sbk * es) % 16 == 0) b_mn = true;
   else return NVB200_ERR_UNSUPPORTED;
   if (!aligned16(a) || !aligned16(b)) return NVB200_ERR_UNSUPPORTED;
-  if (M <= kSkinnyMaxM && !a_mn && !b_mn && !swiglu) {
-    const int rc = launch_skinny(c, a, b, M, N, K, sam, sbn, scm, scn, f32, status, stream);
+  if (M <= kSkinnyMaxM && !a_mn && !b_mn) {
+    const int rc = launch_skinny(c, a, b, M, N, K, sam, sbn, scm, scn, f32, status, stream, nullptr, swiglu);
     if (rc != NVB200_ERR_UNSUPPORTED) return rc;
   }
 

@@ -21,7 +21,10 @@ The reference selects its kernels with the module-global string `nanovllm.kernel
    models whose q/k are normalised before the layer) and its decode attention (the flash_attn_with_kvcache call of
    Attention.forward, :84-91) run the b200 kernels while the backend is "b200". Decode calls outside what the b200
    kernel takes (`nanovllm_b200.kernels.attention.supports`: bf16, head_dim 128, at most 16 query rows per KV head)
-   keep flash-attn's; prefill attention (flash_attn_varlen_func, :79-83) stays flash-attn's.
+   keep flash-attn's; prefill attention (flash_attn_varlen_func, :79-83) stays flash-attn's;
+7. makes Qwen3MLP (nanovllm/models/qwen3.py:133-137) run its gate_up projection and SiLU x Mul as one kernel
+   (nanovllm_b200.kernels.matmul.matmul_silu_and_mul) for the batches `fused_gate_up_applies` admits (decode-sized
+   batches, where it was measured faster than the projection followed by the SiLU x Mul kernel).
 
 Call it once, before constructing `LLM(..., kernel_backend="b200")`.
 """
@@ -143,6 +146,26 @@ def install() -> None:
         return op(x, self.weight.t())
     linear_mod.RowParallelLinear.__init__ = row_parallel_init
     linear_mod.RowParallelLinear.forward = row_parallel_forward
+
+    # 7. Qwen3MLP (models/qwen3.py:133-137) of a b200 model: the gate_up projection and SiLU x Mul as one kernel
+    # (nvb200_matmul_silu_and_mul) for the batch sizes where it was measured faster than the projection followed by
+    # the SiLU x Mul kernel; the down projection is unchanged (step 5 applies to it under tensor parallelism).
+    mlp_init, mlp_forward = qwen3_mod.Qwen3MLP.__init__, qwen3_mod.Qwen3MLP.forward
+
+    @functools.wraps(mlp_init)
+    def qwen3_mlp_init(self, *args, **kwargs):
+        mlp_init(self, *args, **kwargs)
+        self._b200_fused = kernels_mod.backend == BACKEND
+
+    @functools.wraps(mlp_forward)
+    def qwen3_mlp_forward(self, x):
+        w = self.gate_up_proj.weight
+        if (not getattr(self, "_b200_fused", False) or getattr(self.gate_up_proj, "bias", None) is not None
+                or not b200_matmul.fused_gate_up_applies(x, w)):
+            return mlp_forward(self, x)
+        return self.down_proj(b200_matmul.matmul_silu_and_mul(x, w.t()))
+    qwen3_mod.Qwen3MLP.__init__ = qwen3_mlp_init
+    qwen3_mod.Qwen3MLP.forward = qwen3_mlp_forward
     _installed = True
 
 

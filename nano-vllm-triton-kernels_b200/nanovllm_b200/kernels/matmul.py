@@ -56,3 +56,18 @@ def matmul_silu_and_mul(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
             return silu_and_mul(matmul(a, b))
         _lib.check(rc, "matmul_silu_and_mul")
     return out
+
+
+# Largest batch for which the model's MLP (nanovllm_b200.install(), step 7) runs matmul_silu_and_mul in place of the
+# gate_up projection (cuBLAS) followed by the SiLU x Mul kernel. 0: never, as measured on B200 at the Qwen3-0.6B
+# decode step (32 rows, weights streamed from HBM): the skinny kernel's gate_up form took 13.7 us per layer against
+# 10.4 us for cuBLAS's projection and the SiLU x Mul kernel (ncu launch list), and the step rose from 1657 to 1780 us;
+# at K = 1024 the projection alone also runs faster on cuBLAS than the fused tiled kernel for large batches.
+FUSED_GATE_UP_MAX_ROWS = 0
+
+
+def fused_gate_up_applies(x: torch.Tensor, weight: torch.Tensor) -> bool:
+    """Whether Qwen3MLP under kernel_backend="b200" runs x through matmul_silu_and_mul(x, weight.t())."""
+    return (x.dim() == 2 and 0 < x.shape[0] <= FUSED_GATE_UP_MAX_ROWS and x.dtype == weight.dtype == torch.bfloat16
+            and weight.dim() == 2 and weight.shape[1] == x.shape[1] and weight.shape[0] % 2 == 0
+            and x.stride(1) == 1 and weight.stride(1) == 1)

@@ -134,7 +134,9 @@ def test_skinny_row_view(cuda):
 # where both run the tiled kernels, M > 64; the skinny kernel sums in another order) and against the oracle (fp64 product rounded to bf16, then the torch
 # SiLU x Mul) within bf16 tolerance.
 GATE_UP = [(100, 3072, 1024), (300, 1000, 104), (2048, 3072, 1024), (4096, 3072, 1024), (1000, 128, 256),
-           (257, 200, 512), (32, 3072, 1024), (7, 384, 64)]
+           (257, 200, 512), (32, 3072, 1024), (7, 384, 64),
+           # decode-sized rows (the skinny kernel's gate_up form): one row, ragged N, K splits 1-8, 64 rows
+           (1, 3072, 1024), (16, 200, 512), (33, 1000, 4096), (64, 1536, 1024), (32, 12288, 4096), (48, 96, 2048)]
 
 
 @pytest.mark.parametrize("M,N,K", GATE_UP)
