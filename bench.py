@@ -66,6 +66,10 @@ def parse_args():
     ap.add_argument("--scaling", choices=["weak", "strong"], default="weak")
     ap.add_argument("--attn-shape", default="32,1024,16,8",
                     help="attn workload: sequences, keys per sequence, q heads, kv heads (default: the decode step)")
+    ap.add_argument("--matmul-shape", default="4096,4096,4096", help="matmul workload: M, N, K (B = weight.t())")
+    ap.add_argument("--cublas", action="store_true",
+                    help="matmul / gateup workloads: time torch.matmul (cuBLAS) beside ours instead of the reference's "
+                         "Triton kernel")
     ap.add_argument("--gateup-shape", default="4096,4096,12288",
                     help="gateup workload: M, K, intermediate size (default: Qwen3-8B MLP at M = 4096)")
     ap.add_argument("--attn-method", default="auto", choices=["auto", "cluster", "streamk"],
@@ -388,7 +392,7 @@ def norm_workload(args, rank, world, dev):
 def matmul_workload(args, rank, world, dev):
     from nanovllm_b200 import workloads
     from nanovllm_b200.kernels.matmul import matmul
-    M = K = N = 4096
+    M, N, K = (int(v) for v in args.matmul_shape.split(","))
     n_local = N // world if args.scaling == "strong" else N
     x = workloads.matmul_inputs(M, n_local, K, dtype=torch.bfloat16, seed=7, device=dev)
     units = 2 * M * n_local * K
@@ -405,14 +409,17 @@ def matmul_workload(args, rank, world, dev):
         return 2 * tokens * n_local * K
 
     mod, why = reference_kernel_module("matmul")
-    if mod is None:
+    if args.cublas:
+        library = ("cuBLAS (torch.matmul), the GEMM the reference's linear layers run", lambda: x["a"] @ x["b"])
+    elif mod is None:
         library = ("reference Triton matmul", why)
     else:
         library = ("reference Triton kernel nanovllm/kernels/matmul.py:84-99 (baseline/_ref, autotuned and "
                    "JIT-compiled on this GPU)", lambda: mod.matmul(x["a"], x["b"]))
 
     return dict(launch=launch, units=units, e2e=None, cpu=cpu, unit="TFLOP/s", scale=1e12, bound="tensor",
-                metric="matmul bf16 TFLOP/s at M=K=N=4096", dtype="bf16", launches_per_step=1, traffic_key="matmul",
+                metric=f"matmul bf16 TFLOP/s at M={M}, N={N}, K={K}", dtype="bf16", launches_per_step=1,
+                traffic_key="matmul",
                 library=library,
                 config={"workload": "matmul", "M": M, "N": n_local, "K": K, "b_layout": "weight.t() (K-major)",
                         "parallelism": f"column-parallel x{world}", "l2": "flushed between timed steps"})
