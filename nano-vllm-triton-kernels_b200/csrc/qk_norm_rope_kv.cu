@@ -552,7 +552,10 @@ __global__ void __launch_bounds__(32 * (1 + W), CTAS) qknr_multi_kernel(const __
 // requirements as the bulk kernel.
 
 constexpr int kDirectWarps = 4;
-constexpr int64_t kDirectMaxTokens = 512;
+#ifndef NVB200_QKNR_DIRECT_MAX_TOKENS
+#define NVB200_QKNR_DIRECT_MAX_TOKENS 512
+#endif
+constexpr int64_t kDirectMaxTokens = NVB200_QKNR_DIRECT_MAX_TOKENS;
 
 template <int D>
 __global__ void __launch_bounds__(32 * kDirectWarps) qknr_direct_kernel(const __grid_constant__ QknrParams p) {
