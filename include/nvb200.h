@@ -99,7 +99,7 @@ NVB200_API int nvb200_qk_norm_rope_kv(const nvb200_qk_norm_rope_kv_args *args, n
 enum {
   NVB200_QKNR_KERNEL_NONE = 0,    /* T = 0: no launch                                                        */
   NVB200_QKNR_KERNEL_GENERIC = 1, /* rows not 16-byte aligned or D outside {64, 128, 256}: one warp per head  */
-  NVB200_QKNR_KERNEL_DIRECT = 2,  /* T <= 512: direct loads and stores, no staging                            */
+  NVB200_QKNR_KERNEL_DIRECT = 2,  /* T <= 512, or q/k/v rows of at most 40 MB: direct loads and stores       */
   NVB200_QKNR_KERNEL_MULTI = 3,   /* small tokens in a rank's qkv_proj layout: units of 4-16 tokens, bulk copies */
   NVB200_QKNR_KERNEL_BULK = 4     /* one token (or a head group of one) per unit, bulk-copy pipeline          */
 };

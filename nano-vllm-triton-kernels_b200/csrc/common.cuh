@@ -96,6 +96,29 @@ NVB200_DEVICE float rcp_approx_ftz(float x) {
   return y;
 }
 
+// Two fp32 values in one 64-bit register pair, for sm_100's packed fp32 arithmetic (add / mul .f32x2: one
+// instruction for both lanes, each rounded as its scalar form is).
+NVB200_DEVICE uint64_t f32x2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+NVB200_DEVICE float2 f32x2_unpack(uint64_t v) {
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+  return r;
+}
+NVB200_DEVICE uint64_t f32x2_mul(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+NVB200_DEVICE uint64_t f32x2_add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+
 // silu(g) rounded to bf16, as an fp32 value, by the exact expression (the fallback of the fast path).
 NVB200_DEVICE float silu_bf16_exact(float g) {
   return bf16_lo(__bfloat16_as_ushort(__float2bfloat16_rn(g / (1.0f + expf(-g)))));
@@ -104,21 +127,34 @@ NVB200_DEVICE float silu_bf16_exact(float g) {
 // Eight gate and eight up values (bf16) -> eight outputs: silu rounded to bf16, times up, rounded once
 // (mul.rn.bf16x2: the product of two bf16 values is exact in fp32, so this is torch's fp32 multiply then round).
 // The eight fast estimates are checked together: an estimate whose low 16 bits lie within kSiluMargin of 0x8000
-// (test: (b - (0x8000 - margin)) mod 2^16 <= 2 margin), or a gate outside the fast range, sends the thread through
-// the exact expression for the flagged elements only. Elsewhere the estimate rounds to the same bf16 as the exact
-// value under round-to-nearest-even (cvt.rn.bf16x2), since no exact tie lies outside the margin.
+// (test: (b - (0x8000 - margin)) mod 2^16 <= 2 margin) sends the thread through the exact expression for the flagged
+// elements, and a gate outside the fast range for all eight. Elsewhere the estimate rounds to the same bf16 as the
+// exact value under round-to-nearest-even (cvt.rn.bf16x2), since no exact tie lies outside the margin.
 NVB200_DEVICE uint4 silu_mul8_bf16(const uint4 &g, const uint4 &u) {
   const uint32_t gw[4] = {g.x, g.y, g.z, g.w}, uw[4] = {u.x, u.y, u.z, u.w};
+  // A gate outside the fast range (|g| > 16, or not finite) sends all eight through the check below: for each bf16
+  // half h of a word, (h & 0x7fff) > 0x4180 (16.0) exactly when (h & 0x7fff) + 0x3e7f sets bit 15 (no carry crosses
+  // into the other half: both terms are below 0x8000).
+  uint32_t wide = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) wide |= ((gw[i] & 0x7FFF7FFFu) + 0x3E7F3E7Fu) & 0x80008000u;
   float gf[8], est[8];
-  uint32_t flags = 0;
+  uint32_t flags = wide ? 0xFFu : 0u;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    // Pairs in packed fp32 (f32x2) arithmetic: est = g * rcp(1 + 2^(-g log2 e)), two elements per instruction.
+    gf[2 * i] = bf16_lo(gw[i]), gf[2 * i + 1] = bf16_hi(gw[i]);
+    const uint64_t x = f32x2_pack(gf[2 * i], gf[2 * i + 1]);
+    const float2 t = f32x2_unpack(f32x2_mul(x, f32x2_pack(-1.4426950408889634f, -1.4426950408889634f)));
+    const uint64_t d = f32x2_add(f32x2_pack(ex2_approx_ftz(t.x), ex2_approx_ftz(t.y)), f32x2_pack(1.0f, 1.0f));
+    const float2 dd = f32x2_unpack(d);
+    const float2 e = f32x2_unpack(f32x2_mul(x, f32x2_pack(rcp_approx_ftz(dd.x), rcp_approx_ftz(dd.y))));
+    est[2 * i] = e.x, est[2 * i + 1] = e.y;
+  }
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
-    gf[i] = (i & 1) ? bf16_hi(gw[i >> 1]) : bf16_lo(gw[i >> 1]);
-    est[i] = gf[i] * rcp_approx_ftz(1.0f + ex2_approx_ftz(gf[i] * -1.4426950408889634f));  // g / (1 + e^-g)
     const uint32_t b = __float_as_uint(est[i]);
-    const bool near_tie = ((b - (0x8000u - kSiluMargin)) & 0xFFFFu) <= 2 * kSiluMargin;
-    const bool out_of_range = !(fabsf(gf[i]) <= kSiluFastRange);
-    flags |= static_cast<uint32_t>(near_tie || out_of_range) << i;
+    flags |= static_cast<uint32_t>(((b - (0x8000u - kSiluMargin)) & 0xFFFFu) <= 2 * kSiluMargin) << i;
   }
   if (flags != 0) {
 #pragma unroll

@@ -411,6 +411,9 @@ template <typename T> NVB200_DEVICE float silu_mul(float g, float u) {
 }
 
 constexpr int kSiluThreads = 128;
+#ifndef NVB200_SILU_PIPE
+#define NVB200_SILU_PIPE 1
+#endif
 
 template <typename T, int VEC>
 __global__ void __launch_bounds__(kSiluThreads) silu_and_mul_kernel(T *out, const T *x, int64_t rows, int n,
@@ -421,6 +424,28 @@ __global__ void __launch_bounds__(kSiluThreads) silu_and_mul_kernel(T *out, cons
   const int col = cv * VEC;
   int64_t r = blockIdx.y;
   if constexpr (std::is_same<T, __nv_bfloat16>::value && VEC == 8) {
+#if NVB200_SILU_PIPE
+    // Two rows per step, and the next step's four 16-byte loads issued before this step's arithmetic, so the loads
+    // of one step overlap the SiLU arithmetic of the previous one.
+    const int64_t step = gridDim.y;
+    auto ld = [&](int64_t row, uint4 &g, uint4 &u) {
+      if (row < rows) {
+        const T *s0 = x + row * x_row_stride + col;
+        g = *reinterpret_cast<const uint4 *>(s0), u = *reinterpret_cast<const uint4 *>(s0 + n);
+      }
+    };
+    uint4 g0{}, u0{}, g1{}, u1{}, h0{}, v0{}, h1{}, v1{};
+    ld(r, g0, u0);
+    ld(r + step, g1, u1);
+    for (; r < rows; r += 2 * step) {
+      ld(r + 2 * step, h0, v0);
+      ld(r + 3 * step, h1, v1);
+      *reinterpret_cast<uint4 *>(out + r * n + col) = silu_mul8_bf16(g0, u0);
+      if (r + step < rows) *reinterpret_cast<uint4 *>(out + (r + step) * n + col) = silu_mul8_bf16(g1, u1);
+      g0 = h0, u0 = v0, g1 = h1, u1 = v1;
+    }
+    return;
+#else
     // Two rows per step: four 16-byte loads in flight per thread before the arithmetic.
     const int64_t step = gridDim.y;
     for (; r + step < rows; r += 2 * step) {
@@ -430,6 +455,7 @@ __global__ void __launch_bounds__(kSiluThreads) silu_and_mul_kernel(T *out, cons
       *reinterpret_cast<uint4 *>(out + r * n + col) = silu_mul8_bf16(g0, u0);
       *reinterpret_cast<uint4 *>(out + (r + step) * n + col) = silu_mul8_bf16(g1, u1);
     }
+#endif
   }
   for (; r < rows; r += gridDim.y) {
     const T *src = x + r * x_row_stride + col;

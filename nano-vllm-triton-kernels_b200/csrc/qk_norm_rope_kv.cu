@@ -556,6 +556,14 @@ constexpr int kDirectWarps = 4;
 #define NVB200_QKNR_DIRECT_MAX_TOKENS 512
 #endif
 constexpr int64_t kDirectMaxTokens = NVB200_QKNR_DIRECT_MAX_TOKENS;
+// Batches whose q/k/v rows total at most this many bytes also take the direct kernel when the multi-token kernel does
+// not apply. Measured on B200 (L2 flushed): Qwen3-8B shape T = 1024 / 2048: 11.9 / 15.3 us direct vs 13.6 / 16.2 us
+// bulk; T = 4096 (50 MB): 23.7 vs 22.5 us; Qwen3-0.6B shape T = 4096 (34 MB): 17.5 vs 18.3 us, T = 8192: 28.9 vs
+// 26.0 us. Beyond a few tens of MB the persistent bulk pipeline keeps more bytes in flight than one-shot CTAs do.
+#ifndef NVB200_QKNR_DIRECT_MAX_BYTES
+#define NVB200_QKNR_DIRECT_MAX_BYTES (40LL << 20)
+#endif
+constexpr int64_t kDirectMaxBytes = NVB200_QKNR_DIRECT_MAX_BYTES;
 
 template <int D>
 __global__ void __launch_bounds__(32 * kDirectWarps) qknr_direct_kernel(const __grid_constant__ QknrParams p) {
@@ -904,6 +912,17 @@ int qk_norm_rope_kv_launch(const nvb200_qk_norm_rope_kv_args *a, cudaStream_t st
     }
   }
   p.tpu = 1;
+  if (T * static_cast<int64_t>(hq + 2 * hkv) * D * 2 <= kDirectMaxBytes && T <= 0x7fffffffLL) {
+    if (plan) {
+      plan[0] = NVB200_QKNR_KERNEL_DIRECT, plan[1] = 1;
+      return NVB200_OK;
+    }
+    switch (D) {
+      case 64: return launch_direct<64>(p, stream);
+      case 128: return launch_direct<128>(p, stream);
+      default: return launch_direct<256>(p, stream);
+    }
+  }
 
   // Heads per unit: as many as possible while the units still cover every SM once.
   int splits = hkv;

@@ -336,8 +336,8 @@ def rank_inputs(dev, T, world, rank, seed=11):
 
 
 # (world, T): the multi-token route needs ceil(T / B) >= 2 x SMs units (B = 4 at 4 ranks, 8 at 8 ranks); T = 1024
-# is below that and runs the one-token kernel (checked for parity all the same); 8193 leaves a last unit of one
-# token, 8190 one of 2 (B = 4) / 6 (B = 8) tokens.
+# is below that and runs a one-token-per-unit kernel (checked for parity all the same); 8193 leaves a last unit of
+# one token, 8190 one of 2 (B = 4) / 6 (B = 8) tokens.
 MULTI_CASES = [(w, t) for w in (4, 8) for t in (1024, 8192, 8193, 8190)]
 
 
@@ -358,8 +358,8 @@ def test_rank_qkv_layout_multi_token_kernel(cuda, world, tokens, store, write_k)
     B = 4 if world == 4 else 8
     if (tokens + B - 1) // B >= 2 * sms:
         assert (route, tpu) == ("multi", B), (route, tpu)
-    else:
-        assert route == "bulk", route
+    else:  # the one-token-per-unit kernels: direct for batches of up to 40 MB of q/k/v rows, else bulk
+        assert route in ("direct", "bulk"), route
     _lib.status(cuda, clear=True)
     q_out, k_out = qk_norm_rope_kv(*args)
     # The normed heads: the same layout through an identity rotation (cos 1, sin 0 at position 0), k_out on.
