@@ -42,6 +42,7 @@ sys.path.insert(0, ROOT)
 import torch  # noqa: E402
 
 L2_FLUSH_BYTES = 256 << 20
+E2E_CHUNK = 1024  # tokens per chunk of the fused op's end-to-end leg (copies of one chunk overlap another's kernel)
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 METRIC_FUSED = "qk-norm+RoPE+KV-write GB/s (% HBM peak) at T=8192"
 
@@ -274,20 +275,48 @@ def fused_workload(args, rank, world, dev, hq_total, hkv_total, max_pos, num_blo
     host = {}
 
     def e2e():
+        """One step through the public API from pinned host memory, in chunks of E2E_CHUNK tokens on three streams:
+        the host-to-device copy of chunk c + 1 and the device-to-host copy of chunk c - 1 run while chunk c computes
+        (PCIe carries both directions at once, and the op is token-parallel). The streams start after, and the
+        current stream waits for, all of a step's work, so steps do not overlap one another."""
         if not host:  # pinned host copies of the step's inputs, and the device buffers they are copied into
             host.update(qkv=x["qkv"].cpu().pin_memory(), positions=x["positions"].cpu().pin_memory(),
                         slots=x["slots"].cpu().pin_memory(),
                         q_out=torch.empty(T, hq, d, dtype=torch.bfloat16).pin_memory(),
                         dqkv=torch.empty_like(x["qkv"]), dpos=torch.empty_like(x["positions"]),
-                        dslots=torch.empty_like(x["slots"]))
+                        dslots=torch.empty_like(x["slots"]),
+                        streams=[torch.cuda.Stream(dev) for _ in range(3)])
         dqkv, dpos, dslots = host["dqkv"], host["dpos"], host["dslots"]
-        dqkv.copy_(host["qkv"], non_blocking=True)
-        dpos.copy_(host["positions"], non_blocking=True)
-        dslots.copy_(host["slots"], non_blocking=True)
         q, k, v = dqkv.split([hq * d, hkv * d, hkv * d], dim=-1)
-        q_out, _ = qk_norm_rope_kv(q.view(T, hq, d), k.view(T, hkv, d), v.view(T, hkv, d), dpos, x["q_w"],
-                                   x["k_w"], x["eps"], x["cos_sin"], x["k_cache"], x["v_cache"], dslots, False)
-        host["q_out"].copy_(q_out, non_blocking=True)
+        q, k, v = q.view(T, hq, d), k.view(T, hkv, d), v.view(T, hkv, d)
+        s_in, s_cmp, s_out = host["streams"]
+        main = torch.cuda.current_stream(dev)
+        begin = torch.cuda.Event()
+        begin.record(main)
+        for s_ in (s_in, s_cmp, s_out):
+            s_.wait_event(begin)
+        for t0 in range(0, T, E2E_CHUNK):
+            t1 = min(T, t0 + E2E_CHUNK)
+            with torch.cuda.stream(s_in):
+                dqkv[t0:t1].copy_(host["qkv"][t0:t1], non_blocking=True)
+                dpos[t0:t1].copy_(host["positions"][t0:t1], non_blocking=True)
+                dslots[t0:t1].copy_(host["slots"][t0:t1], non_blocking=True)
+                landed = torch.cuda.Event()
+                landed.record(s_in)
+            s_cmp.wait_event(landed)
+            with torch.cuda.stream(s_cmp):
+                q_out, _ = qk_norm_rope_kv(q[t0:t1], k[t0:t1], v[t0:t1], dpos[t0:t1], x["q_w"], x["k_w"], x["eps"],
+                                           x["cos_sin"], x["k_cache"], x["v_cache"], dslots[t0:t1], False)
+                computed = torch.cuda.Event()
+                computed.record(s_cmp)
+            s_out.wait_event(computed)
+            with torch.cuda.stream(s_out):
+                host["q_out"][t0:t1].copy_(q_out, non_blocking=True)
+                q_out.record_stream(s_out)
+        for s_ in (s_in, s_cmp, s_out):
+            done = torch.cuda.Event()
+            done.record(s_)
+            main.wait_event(done)
         h2d = host["qkv"].numel() * 2 + host["positions"].numel() * 8 + host["slots"].numel() * 4
         return h2d, host["q_out"].numel() * 2
 
@@ -963,8 +992,9 @@ def main():
             e_s = max_over_ranks(e_start.elapsed_time(e_end) / 1e3, world)
             e2e = {"value": all_units / e_s / wl["scale"], "unit": wl["unit"], "h2d_bytes_per_step": h2d,
                    "d2h_bytes_per_step": d2h,
-                   "path": wl.get("e2e_path", "nanovllm_b200.kernels.qk_norm_rope_kv (public API) with pinned "
-                                                      "host inputs/outputs")}
+                   "path": wl.get("e2e_path", f"nanovllm_b200.kernels.qk_norm_rope_kv (public API) with pinned "
+                                              f"host inputs/outputs, in chunks of {E2E_CHUNK} tokens whose copies "
+                                              f"in both directions overlap the other chunks' kernels (three streams)")}
 
         library = None
         if wl.get("library") is not None:
