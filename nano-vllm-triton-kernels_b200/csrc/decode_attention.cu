@@ -123,8 +123,6 @@ NVB200_DEVICE int q_index(int r, int d) { return (r * 8 + ((d >> 3) & 7)) * 16 +
 constexpr int smem_bytes(int R) { return kRingBytes + R * kHeadDim * 4 + kAttnWarps * kTileTokens * R * 4; }
 // CTAs per SM at the largest row count (228 KB of shared memory per SM, 1 KB reserved per CTA).
 constexpr int kSmemPerSm = 228 * 1024;
-constexpr int kFitBlocks = kSmemPerSm / (smem_bytes(kMaxRows) + 1024);
-constexpr int kMinBlocks = kFitBlocks > 0 ? kFitBlocks : 1;
 // CTAs per SM the cluster kernel's launch bounds ask for at R rows: as many as its shared memory allows, at most 3
 // (three at 1-8 rows, two at 16); the register budget per thread follows from it.
 constexpr int cluster_min_blocks(int R) {

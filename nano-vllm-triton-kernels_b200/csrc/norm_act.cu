@@ -444,7 +444,7 @@ __global__ void __launch_bounds__(kSiluThreads) silu_and_mul_kernel(T *out, cons
       if (r + step < rows) *reinterpret_cast<uint4 *>(out + (r + step) * n + col) = silu_mul8_bf16(g1, u1);
       g0 = h0, u0 = v0, g1 = h1, u1 = v1;
     }
-    return;
+    r = rows;  // every row done: the loop below has nothing left
 #else
     // Two rows per step: four 16-byte loads in flight per thread before the arithmetic.
     const int64_t step = gridDim.y;

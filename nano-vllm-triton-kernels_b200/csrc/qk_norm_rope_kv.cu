@@ -523,24 +523,25 @@ __global__ void __launch_bounds__(32 * (1 + W), CTAS) qknr_multi_kernel(const __
     }
     fence_proxy_async_smem();
     __syncwarp();
-    if (lane == 0) {
-      for (int i = 0; i < nt; ++i) {
-        const int64_t t = t0 + i;
-        const uint32_t sq = sb + i * row_stage;
-        bulk_s2g(p.q_out + t * p.hq * D, sq, qb);
-        if (p.k_out) bulk_s2g(p.k_out + t * p.hkv * D, sq + qb, kb);
-        const int32_t slot = meta[st * kMultiMaxTpu + i];
-        if (slot >= 0) {
-          const int64_t off = static_cast<int64_t>(slot) * p.hkv * D;
-          bulk_s2g(p.k_cache + off, sq + qb, kb);
-          bulk_s2g(p.v_cache + off, sq + qb + kb, kb);
-        }
+    // Lane i issues token i's stores (q_out, k_out, the k and v cache rows), so the unit's bulk stores go out in
+    // parallel rather than one after another from one lane; each lane then waits until its stores have read the
+    // stage, and lane 0 hands the stage back once every lane has.
+    if (lane < nt) {
+      const int64_t t = t0 + lane;
+      const uint32_t sq = sb + lane * row_stage;
+      bulk_s2g(p.q_out + t * p.hq * D, sq, qb);
+      if (p.k_out) bulk_s2g(p.k_out + t * p.hkv * D, sq + qb, kb);
+      const int32_t slot = meta[st * kMultiMaxTpu + lane];
+      if (slot >= 0) {
+        const int64_t off = static_cast<int64_t>(slot) * p.hkv * D;
+        bulk_s2g(p.k_cache + off, sq + qb, kb);
+        bulk_s2g(p.v_cache + off, sq + qb + kb, kb);
       }
       bulk_commit();
-      bulk_wait_read<0>();  // the stores have read the stage: hand it back to the producer
-      mbar_arrive(empty);
+      bulk_wait_read<0>();
     }
     __syncwarp();
+    if (lane == 0) mbar_arrive(empty);  // every lane's stores have read the stage: hand it back to the producer
   }
 }
 
