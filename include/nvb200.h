@@ -156,6 +156,22 @@ NVB200_API int nvb200_matmul_silu_and_mul(void *out, const void *a, const void *
                                int64_t sam, int64_t sak, int64_t sbk, int64_t sbn, int64_t scm, int32_t *status,
                                nvb200_stream_t stream);
 
+/* y[M, N] = x[M, K] @ weight[N, K]^T for decode-sized batches (bf16, 1 <= M <= 64): a linear layer's projection
+ * with the layer's weight read as it is stored (nn.Linear layout, K-major rows). The caller guarantees that no
+ * kernel still in flight on the stream writes `weight` (model parameters), which lets the launch start the weight
+ * loads while the preceding kernel finishes (programmatic dependent launch; x is read only after it completes).
+ * swiglu = 1: weight holds 2N rows, the N gate rows then the N up rows (MergedColumnParallelLinear's gate_up
+ * layout), and y = silu(x gate^T).to(bf16) * (x up^T).to(bf16), the SiLU x Mul of the two-step form.
+ * Replaces: F.linear in ColumnParallelLinear.forward / RowParallelLinear.forward (nanovllm/layers/linear.py:72-73,
+ * :152-153; the projections of models/qwen3.py) at decode-sized batches, and for swiglu = 1 the gate_up projection
+ * with SiluAndMul (models/qwen3.py:133-137, kernels/swiglu.py:34-43).
+ * x and weight with unit last strides (row pitches sx, sw, 16-byte multiples, bases 16-byte aligned), y row-major with
+ * row pitch sy. Returns NVB200_ERR_UNSUPPORTED for shapes or layouts it does not take (M > 64, K = 0 included): the
+ * caller then runs F.linear / nvb200_matmul. */
+NVB200_API int nvb200_linear_decode(void *y, const void *x, const void *weight, int64_t M, int64_t N, int64_t K,
+                                    int64_t sx, int64_t sw, int64_t sy, int swiglu, int32_t *status,
+                                    nvb200_stream_t stream);
+
 /* Row-parallel GEMM fused with its all-reduce over NVLink (decode-sized rows), for tensor parallelism: rank r
  * holds A_r [M, K_r] and B_r [K_r, N] (its K shard); every rank receives out[M, N] = sum over ranks of A_r @ B_r in
  * bf16, summed in fp32 in rank order (so every rank gets the same bits). One kernel per rank computes its partial

@@ -282,28 +282,8 @@ NVB200_DEVICE void merge_warp_records(const float *rec, int tid, float (&oc)[R],
 // what bounded the CUDA-core fold at the decode shape (few warps per SM, each issue-bound). The tiles are 16 x 16 and
 // 16 x 128, far below the 128-row tiles tcgen05.mma works on, and a warp owns its tile stream end to end, so the
 // warp-synchronous MMA fits here where a CTA-wide tcgen05 pipeline would not. K and V rows sit in shared memory with
-// the k_chunk swizzle, so the ldmatrix row addresses of each 8 x 8 matrix fall in distinct bank groups.
-// Fragment layout (lane = 4 g + t): A (16 x 16) a0 = (g, 2t..2t+1), a1 = (g + 8, 2t..), a2 = (g, 2t + 8..),
-// a3 = (g + 8, 2t + 8..); B (16 x 8) b0 = (2t..2t+1, g), b1 = (2t + 8.., g); C (16 x 8) c0, c1 = (g, 2t..2t+1),
-// c2, c3 = (g + 8, 2t..2t+1).
-
-NVB200_DEVICE void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
-      "{%0, %1, %2, %3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-NVB200_DEVICE void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(addr));
-}
-NVB200_DEVICE void ldsm_x4_trans(uint32_t addr, uint32_t (&r)[4]) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-               : "r"(addr));
-}
+// the k_chunk swizzle, so the ldmatrix row addresses of each 8 x 8 matrix fall in distinct bank groups. (The MMA
+// and ldmatrix wrappers and the fragment layout are in common.cuh.)
 
 // One warp's online-softmax state for the MMA fold: lane 4 g + t holds rows g and g + 8 (index 0 and 1): running max
 // m (base 2, scaled scores), its share l of the row sums (the keys of its columns; summed over t at the end), and
@@ -435,6 +415,7 @@ template <int R> NVB200_DEVICE void store_warp_record_mma(const MmaSoftmax &st, 
 template <int R>
 __global__ void __launch_bounds__(kAttnThreads, cluster_min_blocks(R))
     paged_decode_kernel(const __grid_constant__ AttnParams p) {
+  launch_dependents();  // a dependent launched early waits for this grid before reading its output
   extern __shared__ __align__(128) uint8_t smem[];
   const int h = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -687,6 +668,7 @@ NVB200_DEVICE long long warp_inclusive_scan_i64(long long x, int lane) {
 template <int R>
 __global__ void __launch_bounds__(kAttnThreads, streamk_min_blocks(R))
     paged_decode_streamk_kernel(const __grid_constant__ AttnParams p, const __grid_constant__ StreamKParams sk) {
+  launch_dependents();  // a dependent launched early waits for this grid before reading its output
   extern __shared__ __align__(128) uint8_t smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   float *q_s = reinterpret_cast<float *>(smem + kRingBytes);

@@ -19,6 +19,8 @@ namespace nvb200 {
 // Implemented in matmul_tc.cu. Return NVB200_ERR_UNSUPPORTED when the layout is not TMA-readable.
 int matmul_swiglu_launch(void *c, const void *a, const void *b, int64_t M, int64_t N, int64_t K, int64_t sam,
                          int64_t sak, int64_t sbk, int64_t sbn, int64_t scm, int32_t *status, cudaStream_t stream);
+int linear_decode_launch(void *y, const void *x, const void *w, int64_t M, int64_t N, int64_t K, int64_t sx,
+                         int64_t sw, int64_t sy, bool swiglu, int32_t *status, cudaStream_t stream);
 int64_t allreduce_buffer_bytes(int64_t max_n);
 int matmul_allreduce_launch(void *c, const void *a, const void *b, int64_t M, int64_t N, int64_t K, int64_t sam,
                             int64_t sak, int64_t sbk, int64_t sbn, int64_t scm, const nvb200_allreduce_group *g,
@@ -195,6 +197,18 @@ extern "C" int nvb200_matmul_silu_and_mul(void *c, const void *a, const void *b,
   if (!c || !a || !b) return NVB200_ERR_ARG;
   if (int rc = check_device()) return rc;
   return matmul_swiglu_launch(c, a, b, M, N, K, sam, sak, sbk, sbn, scm, status, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int nvb200_linear_decode(void *y, const void *x, const void *weight, int64_t M, int64_t N, int64_t K,
+                                    int64_t sx, int64_t sw, int64_t sy, int swiglu, int32_t *status,
+                                    nvb200_stream_t stream) {
+  if (M < 0 || N < 0 || K < 0 || (swiglu != 0 && swiglu != 1)) return NVB200_ERR_ARG;
+  if (M == 0 || N == 0) return NVB200_OK;
+  if (K == 0) return NVB200_ERR_UNSUPPORTED;
+  if (!y || !x || !weight) return NVB200_ERR_ARG;
+  if (int rc = check_device()) return rc;
+  return linear_decode_launch(y, x, weight, M, N, K, sx, sw, sy, swiglu != 0, status,
+                              reinterpret_cast<cudaStream_t>(stream));
 }
 
 extern "C" int64_t nvb200_allreduce_buffer_bytes(int64_t max_n) {

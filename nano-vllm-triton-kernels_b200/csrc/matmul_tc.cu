@@ -772,8 +772,11 @@ bool make_map_c(CUtensorMap *map, void *base, bool f32, int64_t M, int64_t N, in
 
 constexpr int kMaxDynamicSmem = 227 * 1024;
 
+// Raises `kernel`'s dynamic shared-memory limit to at least smem bytes, once per device and size; `slot` identifies
+// the kernel (each kernel instantiation has its own slot: the limit is an attribute of the function).
+constexpr int kConfigureSlots = 8;
 template <typename Kernel> int configure_once(Kernel kernel, int smem, int slot) {
-  static int configured[4][64] = {{0}};
+  static int configured[kConfigureSlots][64] = {{0}};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 64 && configured[slot][dev] >= smem) return NVB200_OK;
@@ -1181,6 +1184,399 @@ __global__ void __launch_bounds__(kSkinnyThreads)
   }
 }
 
+// ---------------------------------------------------------------------------------------------------------------
+// Weight-streaming GEMM for decode-sized rows (bf16, M <= 64, A row-major, B = weight.t(): both K-major). A decode
+// step's linear layers stream each layer's weights from HBM once (tens of MB per layer, gone from L2 by the next
+// step) against 1-64 activation rows: the time is the weight stream, the fixed cost of a launch and the wait for
+// the preceding kernel, not arithmetic. So:
+//   * a CTA owns a slice of NS = 8 NT weight rows (output columns) and a share of K; a thread-block cluster of S CTAs
+//     splits K, their fp32 partials are summed through distributed shared memory. NT and S are chosen so that the
+//     grid covers the SMs with the least data per SM (weights from HBM plus the A rows each CTA re-reads from L2);
+//   * the weights do not depend on the preceding kernel, the A rows do. The kernel is launched with programmatic
+//     stream serialization: its producer issues the weight loads of the first ring stages, then waits for the
+//     preceding grid (griddepcontrol.wait), then loads A. When the preceding kernel lets its dependents start early
+//     (griddepcontrol.launch_dependents, as this library's norm, SiLU x Mul and decode-attention kernels do), the
+//     weight stream overlaps it;
+//   * TMA moves 128-element K chunks (two 64-element boxes per operand, 128-byte swizzle) through a ring; 8 consumer
+//     warps each take one 16-element k-step of every chunk on warp-level bf16 MMAs (the slice is 8-64 rows wide, below
+//     the 64/128-row tiles of tcgen05.mma) and one pass through shared memory sums the 8 warps' shares.
+// The gate_up form takes NS / 2 gate rows and the matching NS / 2 up rows and finishes with the SiLU x Mul routine of
+// the two-step form.
+
+constexpr int kStreamKc = 128;  // K elements per stage: two 64-element (128-byte) TMA boxes per operand
+constexpr int kStreamConsumers = 8;
+constexpr int kStreamThreads = 32 * (kStreamConsumers + 1);  // the consumer warps, then the producer warp
+constexpr int kStreamMaxStages = 8;
+// Ring bytes per CTA (one CTA per SM; it still fits beside the CTAs of this library's norm and SiLU x Mul kernels,
+// which use no shared memory).
+constexpr uint32_t kStreamRingBytes = 192 * 1024;
+
+struct StreamParams {
+  __nv_bfloat16 *c;
+  int64_t scm;
+  int M, N, K;
+  int chunks;         // ceil(K / kStreamKc)
+  int split;          // S: CTAs of a cluster (consecutive blockIdx.x) sharing one slice, each a range of the chunks
+  int stages;
+  int swiglu;         // 1: rows n0 .. n0 + ns/2 - 1 are gate rows, their up rows start at N + n0; C = silu(g) * u
+  uint32_t a_bytes;   // one stage's A tile: 2 boxes of m_pad rows x 128 bytes
+  uint32_t w_bytes;   // one stage's weight tile: 2 boxes of ns rows x 128 bytes (each box two half-boxes for swiglu)
+  uint32_t slot_off;  // the partials other CTAs of the cluster send (after the ring, which the sums reuse)
+  uint32_t hdr_off;   // barriers
+  int32_t *status;
+};
+
+// Address of the 16-byte chunk `ch` (0..7) of row `row` in a 128-byte-swizzled TMA tile at `tile` (rows of 128 bytes;
+// TMA's SWIZZLE_128B stores chunk ch of row r at position ch ^ (r & 7), the tile 1024-byte aligned).
+NVB200_DEVICE uint32_t sw128(uint32_t tile, int row, int ch) {
+  return tile + row * 128 + ((ch ^ (row & 7)) << 4);
+}
+
+NVB200_DEVICE float ld_cluster_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+
+template <int MT, int NT>
+__global__ void __launch_bounds__(kStreamThreads, 1)
+    matmul_stream_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w,
+                         const __grid_constant__ StreamParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  constexpr int NS = 8 * NT;
+  constexpr int G = MT * NT * 32;  // fragment groups: (m tile, n tile, lane), four fp32 values each
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int S = p.split, stages = p.stages;
+  const int rank = static_cast<int>(blockIdx.x) % S, tile = static_cast<int>(blockIdx.x) / S;
+  // This CTA's chunks: an even share of the K chunks (S <= chunks, so every share holds at least one).
+  const int c_begin = rank * p.chunks / S, nch = (rank + 1) * p.chunks / S - c_begin;
+  const uint32_t base = smem_addr(smem);
+  const uint32_t stage_bytes = p.a_bytes + p.w_bytes;
+  const uint32_t bar_full = base + p.hdr_off, bar_empty = bar_full + 8 * kStreamMaxStages;
+  const int n0 = tile * (p.swiglu ? NS / 2 : NS);  // first weight row (gate row) of the slice
+  launch_dependents();
+  // Distributed shared memory may be written only once every CTA of the cluster runs: arrive now, wait before the
+  // first remote store.
+  if (S > 1) asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+
+  // The producer lane sets up the barriers and starts the weight loads of the first stages (they do not depend on
+  // the preceding kernel) before the CTA's first barrier, so the loads start as early as possible.
+  const bool producer = warp == kStreamConsumers && lane == 0;
+  const int pre = min(nch, stages);
+  auto load_w = [&](int i) {
+    const uint32_t sw = base + (i % stages) * stage_bytes + p.a_bytes, full = bar_full + 8 * (i % stages);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int k = (c_begin + i) * kStreamKc + h * 64;
+      tma_load_2d(sw + h * (p.w_bytes / 2), &map_w, k, n0, full);
+      if (p.swiglu) tma_load_2d(sw + h * (p.w_bytes / 2) + p.w_bytes / 4, &map_w, k, p.N + n0, full);
+    }
+  };
+  auto load_a = [&](int i) {
+    const uint32_t sa = base + (i % stages) * stage_bytes, full = bar_full + 8 * (i % stages);
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+      tma_load_2d(sa + h * (p.a_bytes / 2), &map_a, (c_begin + i) * kStreamKc + h * 64, 0, full);
+  };
+  if (producer) {
+    prefetch_tmap(&map_w);
+    prefetch_tmap(&map_a);
+    for (int i = 0; i < stages; ++i) {
+      mbar_init(bar_full + 8 * i, 1);
+      mbar_init(bar_empty + 8 * i, kStreamConsumers);
+    }
+    fence_mbar_init();
+    for (int i = 0; i < pre; ++i) {
+      mbar_arrive_expect_tx(bar_full + 8 * i, stage_bytes);
+      load_w(i);
+    }
+  }
+  __syncthreads();
+
+  float acc[MT][NT][4];
+#pragma unroll
+  for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) acc[mt][nt][0] = acc[mt][nt][1] = acc[mt][nt][2] = acc[mt][nt][3] = 0.f;
+
+  if (warp == kStreamConsumers) {
+    // ------------------------------------------------------------------ producer (one lane): A, then the rest
+    if (lane == 0) {
+      grid_dependency_wait();
+      for (int i = 0; i < pre; ++i) load_a(i);
+      for (int i = pre; i < nch; ++i) {
+        const int st = i % stages;
+        if (!mbar_wait_bounded(bar_empty + 8 * st, ((i / stages) & 1) ^ 1)) {
+          set_status(p.status, NVB200_STATUS_WAIT_TIMEOUT);
+          break;
+        }
+        mbar_arrive_expect_tx(bar_full + 8 * st, stage_bytes);
+        load_w(i);
+        load_a(i);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------ consumers: k-step `warp` of every chunk
+    const int h = warp >> 2;            // which 64-element box of the chunk
+    const int ch0 = (warp & 3) * 2;     // first 16-byte chunk of the k-step in the box's 128-byte rows
+    const int arow = (lane & 7) + ((lane >> 3) & 1) * 8, ach = ch0 + (lane >> 4);
+    const int wrow = ((lane >> 4) << 3) + (lane & 7), wch = ch0 + ((lane >> 3) & 1);
+    for (int i = 0; i < nch; ++i) {
+      const int st = i % stages;
+      if (!mbar_wait_bounded(bar_full + 8 * st, (i / stages) & 1)) {
+        if (lane == 0) set_status(p.status, NVB200_STATUS_WAIT_TIMEOUT);
+        break;
+      }
+      const uint32_t abox = base + st * stage_bytes + h * (p.a_bytes / 2);
+      const uint32_t wbox = base + st * stage_bytes + p.a_bytes + h * (p.w_bytes / 2);
+      uint32_t af[MT][4];
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt) ldsm_x4(sw128(abox, mt * 16 + arow, ach), af[mt]);
+#pragma unroll
+      for (int np = 0; np < NT / 2; ++np) {
+        uint32_t bw[4];
+        ldsm_x4(sw128(wbox, np * 16 + wrow, wch), bw);
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) {
+          mma_16816(acc[mt][2 * np], af[mt], bw[0], bw[1]);
+          mma_16816(acc[mt][2 * np + 1], af[mt], bw[2], bw[3]);
+        }
+      }
+      if constexpr (NT % 2 == 1) {
+        uint32_t bw[2];
+        ldsm_x2(sw128(wbox, (NT - 1) * 8 + (lane & 7), ch0 + ((lane >> 3) & 1)), bw);
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) mma_16816(acc[mt][NT - 1], af[mt], bw[0], bw[1]);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_empty + 8 * st);  // this warp is done with the stage
+    }
+  }
+
+  // -------------------------------------------------------------------- sums
+  // Every chunk was consumed, so no copy is in flight and the ring is free: the warps' shares go there in fragment
+  // order (group j = (mt NT + nt) 32 + lane, a float4 per group and warp: conflict-free), each thread then sums the
+  // eight shares of its groups. With a split, the sum of group j goes to the shared memory of the CTA that finishes
+  // it (rank j % S, slot [this rank][j / S]); one cluster barrier later each CTA adds the S partials of its groups.
+  __syncthreads();
+  float4 *red = reinterpret_cast<float4 *>(smem);  // [warp][G]
+  if (warp < kStreamConsumers) {
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+        red[warp * G + (mt * NT + nt) * 32 + lane] =
+            make_float4(acc[mt][nt][0], acc[mt][nt][1], acc[mt][nt][2], acc[mt][nt][3]);
+  }
+  __syncthreads();
+  const int per_owner = (G + S - 1) / S;
+  const uint32_t slots = base + p.slot_off;  // [S][per_owner] float4
+  if (S > 1) asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
+  for (int j = threadIdx.x; j < G; j += kStreamThreads) {
+    float4 v = red[j];
+#pragma unroll
+    for (int w = 1; w < kStreamConsumers; ++w) {
+      const float4 x = red[w * G + j];
+      v.x += x.x, v.y += x.y, v.z += x.z, v.w += x.w;
+    }
+    if (S == 1) {
+      red[j] = v;  // this thread's element alone
+    } else {
+      const uint32_t dst = map_to_cta(slots + (rank * per_owner + j / S) * 16, j % S);
+      asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "f"(v.x), "f"(v.y), "f"(v.z),
+                   "f"(v.w)
+                   : "memory");
+    }
+  }
+  if (S > 1) cluster_sync();
+  else __syncthreads();
+  // Group j's finished values: c0, c1 at (row mt 16 + g, columns nt 8 + 2t, + 1), c2, c3 eight rows below.
+  auto group_sum = [&](int j) {
+    if (S == 1) return red[j];
+    const float4 *sl = reinterpret_cast<const float4 *>(smem + p.slot_off);
+    const int li = j / S;
+    float4 v = sl[li];
+    for (int q = 1; q < S; ++q) {
+      const float4 x = sl[q * per_owner + li];
+      v.x += x.x, v.y += x.y, v.z += x.z, v.w += x.w;
+    }
+    return v;
+  };
+  auto store = [&](int row, int col, uint32_t packed) {
+    if (row >= p.M) return;
+    __nv_bfloat16 *dst = p.c + row * p.scm + col;
+    if (col < p.N) dst[0] = __ushort_as_bfloat16(static_cast<unsigned short>(packed & 0xFFFFu));
+    if (col + 1 < p.N) dst[1] = __ushort_as_bfloat16(static_cast<unsigned short>(packed >> 16));
+  };
+  // Groups finished here: j = rank + S li (all of them when S == 1); for swiglu only the gate tiles (nt < NT / 2),
+  // whose up partner j + 16 NT has the same owner (16 NT is a multiple of S).
+  const int tiles_done = p.swiglu ? MT * (NT / 2) : MT * NT;
+  for (int e = threadIdx.x; e < tiles_done * 32; e += kStreamThreads) {
+    const int ln = e & 31, t = e >> 5;
+    const int mt = p.swiglu ? t / (NT / 2) : t / NT, nt = p.swiglu ? t % (NT / 2) : t % NT;
+    const int j = (mt * NT + nt) * 32 + ln;
+    if (j % S != rank) continue;
+    const int row = mt * 16 + (ln >> 2), col = nt * 8 + 2 * (ln & 3);
+    const float4 v = group_sum(j);
+    if (!p.swiglu) {
+      store(row, n0 + col, pack_bf16x2(v.x, v.y));
+      store(row + 8, n0 + col, pack_bf16x2(v.z, v.w));
+    } else {
+      const float4 u = group_sum(j + 16 * NT);
+      const uint4 o = silu_mul8_bf16(make_uint4(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w), 0u, 0u),
+                                     make_uint4(pack_bf16x2(u.x, u.y), pack_bf16x2(u.z, u.w), 0u, 0u));
+      store(row, n0 + col, o.x);
+      store(row + 8, n0 + col, o.y);
+    }
+  }
+}
+
+#ifndef NVB200_MM_STREAM
+#define NVB200_MM_STREAM 1
+#endif
+// 1: launch with programmatic stream serialization (the weight loads of the first stages overlap the preceding
+// kernel); 0: plain stream order.
+#ifndef NVB200_MM_STREAM_PDL
+#define NVB200_MM_STREAM_PDL 1
+#endif
+
+template <int MT, int NT> int launch_stream_mt_nt(const CUtensorMap &map_a, const CUtensorMap &map_w,
+                                                  const StreamParams &p, int grid, int smem, bool early_weights,
+                                                  cudaStream_t stream) {
+  static int configured[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && configured[dev] < smem) {
+    if (cudaFuncSetAttribute(matmul_stream_kernel<MT, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+        cudaSuccess)
+      return NVB200_ERR_CUDA;
+    configured[dev] = smem;
+  }
+  static int carve[64];
+  prefer_carveout_once(matmul_stream_kernel<MT, NT>, carve);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kStreamThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  if (p.split > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = p.split, attr[n].val.clusterDim.y = 1, attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  if (NVB200_MM_STREAM_PDL && early_weights) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, matmul_stream_kernel<MT, NT>, map_a, map_w, p) == cudaSuccess ? NVB200_OK
+                                                                                              : NVB200_ERR_CUDA;
+}
+
+template <int MT> int launch_stream_mt(int nt, const CUtensorMap &map_a, const CUtensorMap &map_w,
+                                       const StreamParams &p, int grid, int smem, bool early_weights,
+                                       cudaStream_t stream) {
+  // MT x NT <= 16 (accumulator registers); the selection never asks for more.
+  switch (nt) {
+    case 1: return launch_stream_mt_nt<MT, 1>(map_a, map_w, p, grid, smem, early_weights, stream);
+    case 2: return launch_stream_mt_nt<MT, 2>(map_a, map_w, p, grid, smem, early_weights, stream);
+    case 3: return launch_stream_mt_nt<MT, 3>(map_a, map_w, p, grid, smem, early_weights, stream);
+    case 4: return launch_stream_mt_nt<MT, 4>(map_a, map_w, p, grid, smem, early_weights, stream);
+    case 5: return launch_stream_mt_nt<MT, (MT <= 2 ? 5 : 4)>(map_a, map_w, p, grid, smem, early_weights, stream);
+    case 6: return launch_stream_mt_nt<MT, (MT <= 2 ? 6 : 4)>(map_a, map_w, p, grid, smem, early_weights, stream);
+    case 7: return launch_stream_mt_nt<MT, (MT <= 2 ? 7 : 4)>(map_a, map_w, p, grid, smem, early_weights, stream);
+    default: return launch_stream_mt_nt<MT, (MT <= 2 ? 8 : 4)>(map_a, map_w, p, grid, smem, early_weights, stream);
+  }
+}
+
+// Slice width (NT 8-column tiles) and K split S for a decode-sized GEMM. A CTA's time is about the bytes it moves
+// (its weight rows and the A rows it re-reads, over its share of K) plus a fixed start-up cost, and with a split the
+// cluster reduction; the kernel's time is a CTA's times the waves of CTAs. So: the pair with the least
+//   waves x (bytes per CTA + 40 KB) + (S > 1: 40 KB + 8 KB x S),
+// at least 4 tiles per slice (narrower slices re-read A for too few weight rows); ties go to more CTAs. On B200 this
+// picks, at the Qwen3-0.6B and -8B decode projections with 1, 32 and 64 rows, the (NT, S) that a sweep of every pair
+// measured fastest or within a few percent of it (32 rows: o_proj and down_proj 4 x 4, gate_up with SiLU x Mul 6 x 1,
+// 8B o_proj and down_proj 7 x 2).
+struct StreamPlan {
+  int nt, split;
+};
+
+#ifndef NVB200_STREAM_FORCE_NT
+#define NVB200_STREAM_FORCE_NT 0
+#endif
+#ifndef NVB200_STREAM_FORCE_SPLIT
+#define NVB200_STREAM_FORCE_SPLIT 0
+#endif
+
+StreamPlan stream_plan(int64_t M, int64_t N, int64_t K, bool swiglu, int sms) {
+  const int MT = M <= 16 ? 1 : (M <= 32 ? 2 : 4);
+  const int64_t chunks = (K + kStreamKc - 1) / kStreamKc;
+  StreamPlan best{0, 0};
+  int64_t best_cost = 0, best_ctas = 0;
+  for (int nt = 4; nt <= 8; ++nt) {
+    if (MT * nt > 16 || (swiglu && nt % 2)) continue;
+    if (NVB200_STREAM_FORCE_NT && nt != NVB200_STREAM_FORCE_NT) continue;
+    const int64_t cols = swiglu ? 4 * nt : 8 * nt;
+    const int64_t tiles = (N + cols - 1) / cols;
+    for (int s = 1; s <= 8; s *= 2) {
+      if (s > chunks || (NVB200_STREAM_FORCE_SPLIT && s != NVB200_STREAM_FORCE_SPLIT)) continue;
+      const int64_t ctas = tiles * s, cpc = (chunks + s - 1) / s, waves = (ctas + sms - 1) / sms;
+      const int64_t cost = waves * (cpc * (4096LL * MT + 2048LL * nt) + 40960) + (s > 1 ? 40960 + 8192LL * s : 0);
+      if (best.nt == 0 || cost < best_cost || (cost == best_cost && ctas > best_ctas))
+        best = {nt, s}, best_cost = cost, best_ctas = ctas;
+    }
+  }
+  return best;
+}
+
+// Launches the weight-streaming kernel for bf16, M <= 64, K-major A and B (16-byte aligned rows), C row-major
+// (scn == 1); returns NVB200_ERR_UNSUPPORTED otherwise. early_weights: the caller guarantees that no kernel in
+// flight writes B (model weights), so the launch may let the weight loads overlap the preceding kernel.
+int launch_stream(void *c, const void *a, const void *b, int64_t M, int64_t N, int64_t K, int64_t sam, int64_t sbn,
+                  int64_t scm, int64_t scn, bool swiglu, bool early_weights, int32_t *status, cudaStream_t stream) {
+  if (!NVB200_MM_STREAM || M <= 0 || M > 64 || N <= 0 || scn != 1 || K <= 0 || (sam * 2) % 16 != 0 ||
+      (sbn * 2) % 16 != 0 || N > 0x3fffffffLL || K > 0x3fffffffLL)
+    return NVB200_ERR_UNSUPPORTED;
+  const int MT = M <= 16 ? 1 : (M <= 32 ? 2 : 4);
+  const StreamPlan plan = stream_plan(M, N, K, swiglu, sm_count());
+  if (plan.nt == 0) return NVB200_ERR_UNSUPPORTED;
+  const int nt = plan.nt, NS = 8 * nt;
+  const int64_t cols = swiglu ? NS / 2 : NS;  // output columns per slice
+  const int64_t grid = (N + cols - 1) / cols * plan.split;
+  if (grid > 0x7fffffffLL) return NVB200_ERR_UNSUPPORTED;
+  StreamParams p{};
+  p.c = static_cast<__nv_bfloat16 *>(c), p.scm = scm;
+  p.M = static_cast<int>(M), p.N = static_cast<int>(N), p.K = static_cast<int>(K);
+  p.chunks = static_cast<int>((K + kStreamKc - 1) / kStreamKc);
+  p.split = plan.split;
+  p.swiglu = swiglu ? 1 : 0;
+  p.a_bytes = 2u * (16u * MT) * 128u;
+  p.w_bytes = 2u * static_cast<uint32_t>(NS) * 128u;
+  const uint32_t stage_bytes = p.a_bytes + p.w_bytes;
+  const int cpc = (p.chunks + p.split - 1) / p.split;
+  p.stages = std::max(1, std::min({kStreamMaxStages, cpc, static_cast<int>(kStreamRingBytes / stage_bytes)}));
+  const uint32_t groups = 32u * MT * nt;
+  const uint32_t red_bytes = kStreamConsumers * groups * 16u;
+  p.slot_off = (std::max(p.stages * stage_bytes, red_bytes) + 255u) / 256u * 256u;
+  p.hdr_off = p.slot_off + (p.split > 1 ? (groups + p.split - 1) / p.split * p.split * 16u : 0u);
+  p.status = status;
+  const int smem = static_cast<int>(1024 + p.hdr_off + 2 * 8 * kStreamMaxStages);
+  CUtensorMap map_a, map_w;
+  if (!make_map(&map_a, a, false, K, M, sam, 64, 16 * MT) ||
+      !make_map(&map_w, b, false, K, swiglu ? 2 * N : N, sbn, 64, static_cast<int>(cols)))
+    return NVB200_ERR_UNSUPPORTED;
+  switch (MT) {
+    case 1: return launch_stream_mt<1>(nt, map_a, map_w, p, static_cast<int>(grid), smem, early_weights, stream);
+    case 2: return launch_stream_mt<2>(nt, map_a, map_w, p, static_cast<int>(grid), smem, early_weights, stream);
+    default: return launch_stream_mt<4>(nt, map_a, map_w, p, static_cast<int>(grid), smem, early_weights, stream);
+  }
+}
+
 // Launches the skinny kernel for M <= kSkinnyMaxM with K-major A and B (A row-major, B = weight.t()); returns
 // NVB200_ERR_UNSUPPORTED otherwise.
 int launch_skinny(void *c, const void *a, const void *b, int64_t M, int64_t N, int64_t K, int64_t sam, int64_t sbn,
@@ -1234,7 +1630,7 @@ int launch_skinny(void *c, const void *a, const void *b, int64_t M, int64_t N, i
   // Partial slots (K split, all-reduce) or the gate_up form's exchange of 32 rows of up sums.
   p.hdr_off = p.red_off + (split > 1 || p.ar_world > 1 ? p.m_pad * BM * 4 : (swiglu ? 32 * (BM / 2) * 4 : 0));
   const int smem = 1024 + p.hdr_off + 256;
-  const int rc = f32 ? configure_once(matmul_skinny_kernel<true>, smem, 2) : configure_once(matmul_skinny_kernel<false>, smem, 3);
+  const int rc = f32 ? configure_once(matmul_skinny_kernel<true>, smem, 4) : configure_once(matmul_skinny_kernel<false>, smem, 5);
   if (rc) return rc;
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(static_cast<unsigned>(tiles * split), 1, 1);
@@ -1278,6 +1674,10 @@ int tc_launch(void *c, const void *a, const void *b, int64_t M, int64_t N, int64
   else return NVB200_ERR_UNSUPPORTED;
   if (!aligned16(a) || !aligned16(b)) return NVB200_ERR_UNSUPPORTED;
   if (M <= kSkinnyMaxM && !a_mn && !b_mn) {
+    if (!f32) {
+      const int rc = launch_stream(c, a, b, M, N, K, sam, sbn, scm, scn, swiglu, false, status, stream);
+      if (rc != NVB200_ERR_UNSUPPORTED) return rc;
+    }
     const int rc = launch_skinny(c, a, b, M, N, K, sam, sbn, scm, scn, f32, status, stream, nullptr, swiglu);
     if (rc != NVB200_ERR_UNSUPPORTED) return rc;
   }
@@ -1391,6 +1791,12 @@ int matmul_tc_launch(void *c, const void *a, const void *b, int64_t M, int64_t N
 int matmul_swiglu_launch(void *c, const void *a, const void *b, int64_t M, int64_t N, int64_t K, int64_t sam,
                          int64_t sak, int64_t sbk, int64_t sbn, int64_t scm, int32_t *status, cudaStream_t stream) {
   return tc_launch(c, a, b, M, N, K, sam, sak, sbk, sbn, scm, 1, NVB200_BF16, true, status, stream);
+}
+
+int linear_decode_launch(void *y, const void *x, const void *w, int64_t M, int64_t N, int64_t K, int64_t sx,
+                         int64_t sw, int64_t sy, bool swiglu, int32_t *status, cudaStream_t stream) {
+  if (!aligned16(x) || !aligned16(w)) return NVB200_ERR_UNSUPPORTED;
+  return launch_stream(y, x, w, M, N, K, sx, sw, sy, 1, swiglu, true, status, stream);
 }
 
 int64_t allreduce_buffer_bytes(int64_t max_n) {

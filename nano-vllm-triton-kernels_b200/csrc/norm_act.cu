@@ -163,6 +163,7 @@ NVB200_DEVICE void store_row(T *y, T *so, int n, int first, int step, float rstd
 // A group of L lanes (a power of two <= 32) per row; a CTA holds 256 / L rows.
 template <typename T, int VEC, bool ADD>
 __global__ void __launch_bounds__(kRowThreads) row_norm_kernel(const __grid_constant__ RowArgs a) {
+  launch_dependents();  // a dependent launched early waits for this grid before reading its output
   const int L = a.lanes;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * (kRowThreads / L) + threadIdx.x / L;
   const int li = threadIdx.x % L;
@@ -187,6 +188,7 @@ __global__ void __launch_bounds__(kRowThreads) row_norm_kernel(const __grid_cons
 // One CTA (blockDim.x threads, a multiple of 32) per row, the row in registers, a block-wide sum of squares.
 template <typename T, int VEC, bool ADD>
 __global__ void __launch_bounds__(kMaxBlockThreads) block_row_norm_kernel(const __grid_constant__ RowArgs a) {
+  launch_dependents();  // a dependent launched early waits for this grid before reading its output
   __shared__ float partial[kMaxBlockThreads / 32];
   const int64_t row = blockIdx.x;
   const T *x = static_cast<const T *>(a.x) + row_offset(a, row);
@@ -212,6 +214,7 @@ __global__ void __launch_bounds__(kMaxBlockThreads) block_row_norm_kernel(const 
 // waves at 8192 rows). fp32 values are recomputed from the raw vectors in each pass instead of being held.
 template <typename T, int VEC, bool ADD>
 __global__ void __launch_bounds__(kRowThreads) row_norm_pipe_kernel(const __grid_constant__ RowArgs a) {
+  launch_dependents();  // a dependent launched early waits for this grid before reading its output
   using Raw = RawVec<T, VEC>;
   const int L = a.lanes;
   const int lane = threadIdx.x & 31;
@@ -311,6 +314,7 @@ template <typename K> int resident_blocks(K kernel, int *cache, int threads = kR
 // Rows longer than a CTA holds in registers: one CTA per row, sum of squares first, then a second pass.
 template <typename T, bool ADD>
 __global__ void __launch_bounds__(kRowThreads) long_row_norm_kernel(const __grid_constant__ RowArgs a) {
+  launch_dependents();  // a dependent launched early waits for this grid before reading its output
   __shared__ float partial[kRowThreads / 32];
   const int64_t row = blockIdx.x;
   const T *x = static_cast<const T *>(a.x) + row_offset(a, row);
@@ -351,6 +355,8 @@ template <typename T, int VEC, bool ADD> int launch_norm_vec(RowArgs &a, cudaStr
   if (a.rows <= kFewRows && nvec >= 64 && nvec <= 32 * kVecPerThread) {
     // Decode-sized batches: spread each row over a CTA so every thread does one vector (short serial chain).
     const int threads = (nvec + 31) / 32 * 32;
+    static int carve[64];
+    prefer_carveout_once(block_row_norm_kernel<T, VEC, ADD>, carve);
     block_row_norm_kernel<T, VEC, ADD><<<static_cast<unsigned>(a.rows), threads, 0, stream>>>(a);
     return launch_status();
   }
@@ -366,9 +372,13 @@ template <typename T, int VEC, bool ADD> int launch_norm_vec(RowArgs &a, cudaStr
                           resident_blocks(row_norm_pipe_kernel<T, VEC, ADD>, resident);
     if (blocks > slots) {
       // More rows than one wave holds: the persistent two-rows-in-flight kernel.
+      static int carve[64];
+      prefer_carveout_once(row_norm_pipe_kernel<T, VEC, ADD>, carve);
       row_norm_pipe_kernel<T, VEC, ADD><<<static_cast<unsigned>(slots), kRowThreads, 0, stream>>>(a);
       return launch_status();
     }
+    static int carve[64];
+    prefer_carveout_once(row_norm_kernel<T, VEC, ADD>, carve);
     row_norm_kernel<T, VEC, ADD><<<static_cast<unsigned>(blocks), kRowThreads, 0, stream>>>(a);
     return launch_status();
   }
@@ -376,6 +386,8 @@ template <typename T, int VEC, bool ADD> int launch_norm_vec(RowArgs &a, cudaStr
   if (nvec <= kMaxBlockThreads * kVecPerThread) {
     int threads = 64;
     while (threads * kVecPerThread < nvec) threads *= 2;
+    static int carve[64];
+    prefer_carveout_once(block_row_norm_kernel<T, VEC, ADD>, carve);
     block_row_norm_kernel<T, VEC, ADD><<<static_cast<unsigned>(a.rows), threads, 0, stream>>>(a);
     return launch_status();
   }
@@ -418,6 +430,7 @@ constexpr int kSiluThreads = 128;
 template <typename T, int VEC>
 __global__ void __launch_bounds__(kSiluThreads) silu_and_mul_kernel(T *out, const T *x, int64_t rows, int n,
                                                                      int64_t x_row_stride) {
+  launch_dependents();  // a dependent launched early waits for this grid before reading its output
   const int nv = n / VEC;
   const int cv = blockIdx.x * kSiluThreads + threadIdx.x;
   if (cv >= nv) return;
@@ -489,10 +502,14 @@ template <typename T> int launch_silu(void *out, const void *x, int64_t rows, in
   T *o = static_cast<T *>(out);
   const T *i = static_cast<const T *>(x);
   const int ni = static_cast<int>(n);
-  if (vec)
+  static int carve[2][64];
+  if (vec) {
+    prefer_carveout_once(silu_and_mul_kernel<T, VEC>, carve[0]);
     silu_and_mul_kernel<T, VEC><<<grid, kSiluThreads, 0, stream>>>(o, i, rows, ni, stride);
-  else
+  } else {
+    prefer_carveout_once(silu_and_mul_kernel<T, 1>, carve[1]);
     silu_and_mul_kernel<T, 1><<<grid, kSiluThreads, 0, stream>>>(o, i, rows, ni, stride);
+  }
   return launch_status();
 }
 
@@ -540,6 +557,7 @@ NVB200_DEVICE int stream_next_unit(int it, int NS, int W) {
 
 __global__ void __launch_bounds__(32 * (1 + kStreamWarps), kStreamCtas)
     rms_stream_kernel(const __grid_constant__ StreamArgs a) {
+  launch_dependents();  // a dependent launched early waits for this grid before reading its output
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int NS = a.stages;

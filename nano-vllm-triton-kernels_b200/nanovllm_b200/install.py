@@ -23,8 +23,12 @@ The reference selects its kernels with the module-global string `nanovllm.kernel
    kernel takes (`nanovllm_b200.kernels.attention.supports`: bf16, head_dim 128, at most 16 query rows per KV head)
    keep flash-attn's; prefill attention (flash_attn_varlen_func, :79-83) stays flash-attn's;
 7. makes Qwen3MLP (nanovllm/models/qwen3.py:133-137) run its gate_up projection and SiLU x Mul as one kernel
-   (nanovllm_b200.kernels.matmul.matmul_silu_and_mul) for the batches `fused_gate_up_applies` admits (decode-sized
-   batches, where it was measured faster than the projection followed by the SiLU x Mul kernel).
+   (nanovllm_b200.kernels.matmul.linear_decode with swiglu) for the batches `fused_gate_up_applies` admits;
+8. makes ColumnParallelLinear (nanovllm/layers/linear.py:72-73) and, on one GPU, RowParallelLinear (:152-156) run
+   the projections `decode_gemm_applies` admits (decode-sized bf16 batches, no bias, N <= K: o_proj and down_proj)
+   through nanovllm_b200.kernels.matmul.linear_decode instead of F.linear (cuBLAS): a weight-streaming kernel whose
+   weight loads start while the preceding kernel finishes. The thresholds of both steps are the measured
+   crossovers against cuBLAS (nanovllm_b200/kernels/matmul.py).
 
 Call it once, before constructing `LLM(..., kernel_backend="b200")`.
 """
@@ -134,6 +138,7 @@ def install() -> None:
     def row_parallel_init(self, *args, **kwargs):
         row_init(self, *args, **kwargs)
         self._b200_fused = kernels_mod.backend == BACKEND and self.tp_size > 1
+        self._b200_matmul = kernels_mod.backend == BACKEND
 
     @functools.wraps(row_forward)
     def row_parallel_forward(self, x):
@@ -148,8 +153,8 @@ def install() -> None:
     linear_mod.RowParallelLinear.forward = row_parallel_forward
 
     # 7. Qwen3MLP (models/qwen3.py:133-137) of a b200 model: the gate_up projection and SiLU x Mul as one kernel
-    # (nvb200_matmul_silu_and_mul) for the batch sizes where it was measured faster than the projection followed by
-    # the SiLU x Mul kernel; the down projection is unchanged (step 5 applies to it under tensor parallelism).
+    # (nvb200_linear_decode with swiglu) for the batches where it was measured faster than the projection followed by
+    # the SiLU x Mul kernel; the down projection goes through its own layer (steps 5 and 8).
     mlp_init, mlp_forward = qwen3_mod.Qwen3MLP.__init__, qwen3_mod.Qwen3MLP.forward
 
     @functools.wraps(mlp_init)
@@ -163,9 +168,41 @@ def install() -> None:
         if (not getattr(self, "_b200_fused", False) or getattr(self.gate_up_proj, "bias", None) is not None
                 or not b200_matmul.fused_gate_up_applies(x, w)):
             return mlp_forward(self, x)
-        return self.down_proj(b200_matmul.matmul_silu_and_mul(x, w.t()))
+        y = b200_matmul.linear_decode(x, w, swiglu=True)
+        return mlp_forward(self, x) if y is None else self.down_proj(y)
     qwen3_mod.Qwen3MLP.__init__ = qwen3_mlp_init
     qwen3_mod.Qwen3MLP.forward = qwen3_mlp_forward
+
+    # 8. Decode-sized projections of a b200 model: column-parallel layers, and row-parallel ones without tensor
+    # parallelism (step 5 takes them under it), through b200 `matmul`.
+    col_init, col_forward = linear_mod.ColumnParallelLinear.__init__, linear_mod.ColumnParallelLinear.forward
+
+    @functools.wraps(col_init)
+    def column_parallel_init(self, *args, **kwargs):
+        col_init(self, *args, **kwargs)
+        self._b200_matmul = kernels_mod.backend == BACKEND
+
+    @functools.wraps(col_forward)
+    def column_parallel_forward(self, x):
+        if (not getattr(self, "_b200_matmul", False) or self.bias is not None
+                or not b200_matmul.decode_gemm_applies(x, self.weight)):
+            return col_forward(self, x)
+        y = b200_matmul.linear_decode(x, self.weight)
+        return col_forward(self, x) if y is None else y
+    linear_mod.ColumnParallelLinear.__init__ = column_parallel_init
+    linear_mod.ColumnParallelLinear.forward = column_parallel_forward
+
+    row_fused_forward = linear_mod.RowParallelLinear.forward
+
+    @functools.wraps(row_fused_forward)
+    def row_parallel_single_forward(self, x):
+        if (self.tp_size == 1 and getattr(self, "_b200_matmul", False) and self.bias is None
+                and b200_matmul.decode_gemm_applies(x, self.weight)):
+            y = b200_matmul.linear_decode(x, self.weight)
+            if y is not None:
+                return y
+        return row_fused_forward(self, x)
+    linear_mod.RowParallelLinear.forward = row_parallel_single_forward
     _installed = True
 
 

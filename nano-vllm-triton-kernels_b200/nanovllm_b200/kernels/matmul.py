@@ -58,16 +58,54 @@ def matmul_silu_and_mul(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
     return out
 
 
-# Largest batch for which the model's MLP (nanovllm_b200.install(), step 7) runs matmul_silu_and_mul in place of the
-# gate_up projection (cuBLAS) followed by the SiLU x Mul kernel. 0: never, as measured on B200 at the Qwen3-0.6B
-# decode step (32 rows, weights streamed from HBM): the skinny kernel's gate_up form took 13.7 us per layer against
-# 10.4 us for cuBLAS's projection and the SiLU x Mul kernel (ncu launch list), and the step rose from 1657 to 1780 us;
-# at K = 1024 the projection alone also runs faster on cuBLAS than the fused tiled kernel for large batches.
-FUSED_GATE_UP_MAX_ROWS = 0
+def linear_decode(x: torch.Tensor, weight: torch.Tensor, swiglu: bool = False) -> torch.Tensor | None:
+    """x [M, K] @ weight[N, K].t() -> [M, N] bf16 for decode-sized batches (`nvb200_linear_decode`): the weight is a
+    model parameter (no kernel in flight writes it), so its loads may overlap the preceding kernel. swiglu: weight
+    holds [gate; up] rows (2 N) and the result is silu(x gate^T) * (x up^T), [M, N]. None when the kernel does not
+    take the shape or layout (the caller then runs its own path)."""
+    if not (x.dim() == 2 and weight.dim() == 2 and x.shape[1] == weight.shape[1]):
+        raise AssertionError((x.shape, weight.shape))
+    if not (x.dtype == weight.dtype == torch.bfloat16):
+        raise AssertionError((x.dtype, weight.dtype))
+    if x.stride(1) != 1 or weight.stride(1) != 1 or (swiglu and weight.shape[0] % 2):
+        return None
+    M, K = x.shape
+    N = weight.shape[0] // 2 if swiglu else weight.shape[0]
+    y = torch.empty((M, N), device=x.device, dtype=x.dtype)
+    if M == 0 or N == 0:
+        return y
+    rc = _lib.lib().nvb200_linear_decode(y.data_ptr(), x.data_ptr(), weight.data_ptr(), M, N, K, x.stride(0),
+                                         weight.stride(0), y.stride(0), int(swiglu),
+                                         _lib.status_word(x.device).data_ptr(), _lib.stream_of(x))
+    if rc == _lib.ERR_UNSUPPORTED:
+        return None
+    _lib.check(rc, "linear_decode")
+    return y
+
+
+# Which of a b200 model's linear layers run `linear_decode` (nanovllm_b200.install(), steps 7 and 8) instead of
+# cuBLAS, as measured on B200 (each projection preceded by this library's RMSNorm, 28 weights per CUDA graph, 32
+# rows; us per norm + projection, the norm alone 1.7-2.6 us):
+#   Qwen3-0.6B o_proj 1024 x 2048:       6.28 (cuBLAS 9.03)     down_proj 1024 x 3072:  6.96 (cuBLAS 10.30)
+#   gate_up 2 x 3072 x 1024 + SiLU x Mul: 8.74 (cuBLAS + the SiLU x Mul kernel 10.73)
+#   qkv_proj 4096 x 1024:                7.09 (cuBLAS 6.24)     Qwen3-8B gate_up + SiLU x Mul: 56.8 (44.6)
+# so plain projections go through it when N <= K (the o and down projections) and the gate_up projection with its
+# SiLU x Mul when its weight is at most 32 MB; batches of at most 32 rows (at 64 rows cuBLAS was as fast or faster).
+DECODE_GEMM_MAX_ROWS = 32
+FUSED_GATE_UP_MAX_ROWS = 32
+FUSED_GATE_UP_MAX_WEIGHT_BYTES = 32 << 20
+
+
+def decode_gemm_applies(x: torch.Tensor, weight: torch.Tensor) -> bool:
+    """Whether a linear layer of a b200 model runs x @ weight.t() through `linear_decode`."""
+    return (x.dim() == 2 and 0 < x.shape[0] <= DECODE_GEMM_MAX_ROWS and weight.dim() == 2
+            and x.dtype == weight.dtype == torch.bfloat16 and weight.shape[1] == x.shape[1]
+            and weight.shape[0] <= weight.shape[1])
 
 
 def fused_gate_up_applies(x: torch.Tensor, weight: torch.Tensor) -> bool:
-    """Whether Qwen3MLP under kernel_backend="b200" runs x through matmul_silu_and_mul(x, weight.t())."""
+    """Whether Qwen3MLP under kernel_backend="b200" runs its gate_up projection and SiLU x Mul as
+    linear_decode(x, weight, swiglu=True)."""
     return (x.dim() == 2 and 0 < x.shape[0] <= FUSED_GATE_UP_MAX_ROWS and x.dtype == weight.dtype == torch.bfloat16
             and weight.dim() == 2 and weight.shape[1] == x.shape[1] and weight.shape[0] % 2 == 0
-            and x.stride(1) == 1 and weight.stride(1) == 1)
+            and weight.numel() * weight.element_size() <= FUSED_GATE_UP_MAX_WEIGHT_BYTES)

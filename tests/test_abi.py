@@ -88,6 +88,11 @@ def test_new_entry_points_reject_bad_arguments_without_a_gpu():
     assert lib.nvb200_paged_decode_splits(1, 8, 8, 256, 0) == 8
     assert lib.nvb200_paged_decode_splits(1, 1, 1, 64, 0) == 1
     assert lib.nvb200_paged_decode_splits(4, 4, 64, 256, 3) == 3
+    # linear_decode: negative sizes, a swiglu flag other than 0/1, null pointers with work to do; nothing to do.
+    assert lib.nvb200_linear_decode(8, 8, 8, -1, 16, 16, 16, 16, 16, 0, None, None) == _lib.ERR_ARG
+    assert lib.nvb200_linear_decode(8, 8, 8, 1, 16, 16, 16, 16, 16, 2, None, None) == _lib.ERR_ARG
+    assert lib.nvb200_linear_decode(None, 8, 8, 1, 16, 16, 16, 16, 16, 0, None, None) == _lib.ERR_ARG
+    assert lib.nvb200_linear_decode(None, None, None, 0, 16, 16, 16, 16, 16, 0, None, None) == _lib.OK
 
 
 def test_streamk_entry_points_check_arguments_without_a_gpu():
