@@ -36,6 +36,9 @@ import functools
 
 BACKEND = "b200"
 _installed = False
+# Depth of Qwen3Attention.__init__ calls of a b200 model in progress: step 3 runs them with the backend string set to
+# "triton_fused", so the layers built inside (qkv_proj, o_proj) ask this rather than the string.
+_attention_init_depth = 0
 
 
 def _by_backend(kernels_mod, ours, theirs):
@@ -44,6 +47,11 @@ def _by_backend(kernels_mod, ours, theirs):
         return (ours if kernels_mod.backend == BACKEND else theirs)(*args, **kwargs)
     fn.__b200__ = ours
     return fn
+
+
+def _building_b200(kernels_mod) -> bool:
+    """Whether a layer being constructed belongs to a kernel_backend="b200" model."""
+    return kernels_mod.backend == BACKEND or _attention_init_depth > 0
 
 
 def _model_runner(config, rank, event):
@@ -118,12 +126,15 @@ def install() -> None:
 
     @functools.wraps(attn_init)
     def __init__(self, *args, **kwargs):
+        global _attention_init_depth
         if kernels_mod.backend != BACKEND:
             return attn_init(self, *args, **kwargs)
         kernels_mod.backend = "triton_fused"
+        _attention_init_depth += 1
         try:
             attn_init(self, *args, **kwargs)
         finally:
+            _attention_init_depth -= 1
             kernels_mod.backend = BACKEND
     qwen3_mod.Qwen3Attention.__init__ = __init__
 
@@ -137,8 +148,8 @@ def install() -> None:
     @functools.wraps(row_init)
     def row_parallel_init(self, *args, **kwargs):
         row_init(self, *args, **kwargs)
-        self._b200_fused = kernels_mod.backend == BACKEND and self.tp_size > 1
-        self._b200_matmul = kernels_mod.backend == BACKEND
+        self._b200_fused = _building_b200(kernels_mod) and self.tp_size > 1
+        self._b200_matmul = _building_b200(kernels_mod)
 
     @functools.wraps(row_forward)
     def row_parallel_forward(self, x):
@@ -160,7 +171,7 @@ def install() -> None:
     @functools.wraps(mlp_init)
     def qwen3_mlp_init(self, *args, **kwargs):
         mlp_init(self, *args, **kwargs)
-        self._b200_fused = kernels_mod.backend == BACKEND
+        self._b200_fused = _building_b200(kernels_mod)
 
     @functools.wraps(mlp_forward)
     def qwen3_mlp_forward(self, x):
@@ -180,7 +191,7 @@ def install() -> None:
     @functools.wraps(col_init)
     def column_parallel_init(self, *args, **kwargs):
         col_init(self, *args, **kwargs)
-        self._b200_matmul = kernels_mod.backend == BACKEND
+        self._b200_matmul = _building_b200(kernels_mod)
 
     @functools.wraps(col_forward)
     def column_parallel_forward(self, x):

@@ -98,3 +98,31 @@ def test_qwen3_attention_is_fused_for_b200(ref):
         assert not b.fused_norm_rope
     finally:
         ref.backend = old
+
+
+def test_projections_of_a_b200_model_take_the_b200_routes(ref):
+    """Every projection of a b200 Qwen3 layer is marked for the b200 GEMM routes (steps 5, 7 and 8), including the
+    qkv and o projections that Qwen3Attention builds while its constructor runs with the backend string set to
+    "triton_fused"; the layers of other backends are not."""
+    import torch
+    import torch.distributed as dist
+    from nanovllm.models.qwen3 import Qwen3Attention, Qwen3MLP
+    if not dist.is_initialized():
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        os.environ.setdefault("MASTER_PORT", "29617")
+        dist.init_process_group("gloo", rank=0, world_size=1)
+    old = ref.backend
+    try:
+        for backend, expected in (("b200", True), ("compile", False)):
+            ref.backend = backend
+            with torch.device("meta"):
+                a = Qwen3Attention(1024, 16, 8, max_position=4096, head_dim=128, rope_theta=1e6)
+                m = Qwen3MLP(1024, 3072, "silu")
+            assert getattr(a.qkv_proj, "_b200_matmul", False) is expected
+            assert getattr(a.o_proj, "_b200_matmul", False) is expected
+            assert getattr(m.down_proj, "_b200_matmul", False) is expected
+            assert getattr(m, "_b200_fused", False) is expected
+            assert not getattr(a.o_proj, "_b200_fused", False)  # one rank: no all-reduce to fuse
+            assert ref.backend == backend
+    finally:
+        ref.backend = old
