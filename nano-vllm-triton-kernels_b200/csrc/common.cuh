@@ -326,10 +326,10 @@ int sm_count();
 // Returns NVB200_OK if the current device is sm_100 (B200/GB200), else NVB200_ERR_NO_DEVICE.
 int check_device();
 
-// Shared-memory carveout (percent of the unified L1/shared array) asked for the decode-step kernels that run next to
-// one another (norms, SiLU x Mul, the weight-streaming GEMM): one SM configuration for all of them, so that a CTA of
-// the GEMM can start on an SM where a norm CTA still runs and no SM is reconfigured between them (-1: the driver's
-// choice). Measured on B200 at the Qwen3-0.6B decode projections: 0.6-1.3 us less per norm + projection pair.
+// Shared-memory carveout (percent of the unified L1/shared array) asked for the weight-streaming GEMM (-1: the
+// driver's choice). Measured on B200 at the Qwen3-0.6B decode projections, each after an RMSNorm in a CUDA graph:
+// 0.6-1.3 us less per norm + projection pair with the norm kernels asking for it too, but those then lose L1 (Add +
+// RMSNorm at 8192 x 1024: 14.7 -> 18.7 us), so only the GEMM asks.
 #ifndef NVB200_CARVEOUT
 #define NVB200_CARVEOUT 100
 #endif
@@ -341,6 +341,52 @@ template <typename Kernel> void prefer_carveout_once(Kernel kernel, int (&done)[
   if (cudaGetDevice(&dev) != cudaSuccess || dev >= 64 || done[dev]) return;
   cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, NVB200_CARVEOUT);
   done[dev] = 1;
+}
+
+// Programmatic stream serialization for the decode-path kernels that launch through launch_ex, per kernel class: 1
+// lets their CTAs be scheduled while the preceding kernel finishes (when it lets its dependents start early; they
+// wait for it with grid_dependency_wait() before touching memory), 0 keeps plain stream order. Measured on B200, the
+// Qwen3-0.6B decode step (batch 32, context 1024, CUDA graph; the weight-streaming GEMM, which has its own switch,
+// launched so in every case): all plain 1548.7 us; the norms so 1481.6 us; the fused q/k op and decode attention
+// so 1645.5 us. Hence norms on, the others off.
+#ifndef NVB200_PDL
+#define NVB200_PDL 0
+#endif
+#ifndef NVB200_PDL_NORM
+#define NVB200_PDL_NORM 1
+#endif
+#ifndef NVB200_PDL_QKNR
+#define NVB200_PDL_QKNR NVB200_PDL
+#endif
+#ifndef NVB200_PDL_ATTN
+#define NVB200_PDL_ATTN NVB200_PDL
+#endif
+
+// Launches `kernel` with cudaLaunchKernelEx: a thread-block cluster of cluster_x CTAs (1: none) and, if pdl,
+// programmatic stream serialization. The kernel must call grid_dependency_wait() before its first global access.
+template <typename... KArgs, typename... Args>
+int launch_ex(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, int cluster_x,
+              bool pdl, Args &&...args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  if (cluster_x > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = cluster_x, attr[n].val.clusterDim.y = 1, attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  if (pdl) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...) == cudaSuccess ? NVB200_OK : NVB200_ERR_CUDA;
 }
 
 inline int launch_status() { return cudaGetLastError() == cudaSuccess ? NVB200_OK : NVB200_ERR_CUDA; }

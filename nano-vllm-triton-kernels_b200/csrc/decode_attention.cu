@@ -416,6 +416,7 @@ template <int R>
 __global__ void __launch_bounds__(kAttnThreads, cluster_min_blocks(R))
     paged_decode_kernel(const __grid_constant__ AttnParams p) {
   launch_dependents();  // a dependent launched early waits for this grid before reading its output
+  grid_dependency_wait();  // this grid may itself have been launched early
   extern __shared__ __align__(128) uint8_t smem[];
   const int h = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -669,6 +670,7 @@ template <int R>
 __global__ void __launch_bounds__(kAttnThreads, streamk_min_blocks(R))
     paged_decode_streamk_kernel(const __grid_constant__ AttnParams p, const __grid_constant__ StreamKParams sk) {
   launch_dependents();  // a dependent launched early waits for this grid before reading its output
+  grid_dependency_wait();  // this grid may itself have been launched early
   extern __shared__ __align__(128) uint8_t smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   float *q_s = reinterpret_cast<float *>(smem + kRingBytes);
@@ -964,13 +966,15 @@ template <int R> int launch_rows(const AttnParams &p, int batch, int hkv, cudaSt
   cfg.blockDim = dim3(kAttnThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = static_cast<unsigned>(p.splits);
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = NVB200_PDL_ATTN ? 2 : 1;
   return cudaLaunchKernelEx(&cfg, paged_decode_kernel<R>, p) == cudaSuccess ? NVB200_OK : NVB200_ERR_CUDA;
 }
 

@@ -1436,7 +1436,8 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
 #define NVB200_MM_STREAM 1
 #endif
 // 1: launch with programmatic stream serialization (the weight loads of the first stages overlap the preceding
-// kernel); 0: plain stream order.
+// kernel); 0: plain stream order. Measured on B200, the Qwen3-0.6B decode step (batch 32, context 1024): 1549 us
+// with it, 1595 us without.
 #ifndef NVB200_MM_STREAM_PDL
 #define NVB200_MM_STREAM_PDL 1
 #endif

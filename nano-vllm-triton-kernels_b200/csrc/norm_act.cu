@@ -164,6 +164,7 @@ NVB200_DEVICE void store_row(T *y, T *so, int n, int first, int step, float rstd
 template <typename T, int VEC, bool ADD>
 __global__ void __launch_bounds__(kRowThreads) row_norm_kernel(const __grid_constant__ RowArgs a) {
   launch_dependents();  // a dependent launched early waits for this grid before reading its output
+  grid_dependency_wait();  // this grid may itself have been launched early
   const int L = a.lanes;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * (kRowThreads / L) + threadIdx.x / L;
   const int li = threadIdx.x % L;
@@ -189,6 +190,7 @@ __global__ void __launch_bounds__(kRowThreads) row_norm_kernel(const __grid_cons
 template <typename T, int VEC, bool ADD>
 __global__ void __launch_bounds__(kMaxBlockThreads) block_row_norm_kernel(const __grid_constant__ RowArgs a) {
   launch_dependents();  // a dependent launched early waits for this grid before reading its output
+  grid_dependency_wait();  // this grid may itself have been launched early
   __shared__ float partial[kMaxBlockThreads / 32];
   const int64_t row = blockIdx.x;
   const T *x = static_cast<const T *>(a.x) + row_offset(a, row);
@@ -215,6 +217,7 @@ __global__ void __launch_bounds__(kMaxBlockThreads) block_row_norm_kernel(const 
 template <typename T, int VEC, bool ADD>
 __global__ void __launch_bounds__(kRowThreads) row_norm_pipe_kernel(const __grid_constant__ RowArgs a) {
   launch_dependents();  // a dependent launched early waits for this grid before reading its output
+  grid_dependency_wait();  // this grid may itself have been launched early
   using Raw = RawVec<T, VEC>;
   const int L = a.lanes;
   const int lane = threadIdx.x & 31;
@@ -315,6 +318,7 @@ template <typename K> int resident_blocks(K kernel, int *cache, int threads = kR
 template <typename T, bool ADD>
 __global__ void __launch_bounds__(kRowThreads) long_row_norm_kernel(const __grid_constant__ RowArgs a) {
   launch_dependents();  // a dependent launched early waits for this grid before reading its output
+  grid_dependency_wait();  // this grid may itself have been launched early
   __shared__ float partial[kRowThreads / 32];
   const int64_t row = blockIdx.x;
   const T *x = static_cast<const T *>(a.x) + row_offset(a, row);
@@ -355,10 +359,8 @@ template <typename T, int VEC, bool ADD> int launch_norm_vec(RowArgs &a, cudaStr
   if (a.rows <= kFewRows && nvec >= 64 && nvec <= 32 * kVecPerThread) {
     // Decode-sized batches: spread each row over a CTA so every thread does one vector (short serial chain).
     const int threads = (nvec + 31) / 32 * 32;
-    static int carve[64];
-    prefer_carveout_once(block_row_norm_kernel<T, VEC, ADD>, carve);
-    block_row_norm_kernel<T, VEC, ADD><<<static_cast<unsigned>(a.rows), threads, 0, stream>>>(a);
-    return launch_status();
+    return launch_ex(block_row_norm_kernel<T, VEC, ADD>, dim3(static_cast<unsigned>(a.rows)), dim3(threads), 0,
+                     stream, 1, NVB200_PDL_NORM, a);
   }
   if (nvec <= 32 * kVecPerThread) {
     int L = 1;
@@ -372,24 +374,18 @@ template <typename T, int VEC, bool ADD> int launch_norm_vec(RowArgs &a, cudaStr
                           resident_blocks(row_norm_pipe_kernel<T, VEC, ADD>, resident);
     if (blocks > slots) {
       // More rows than one wave holds: the persistent two-rows-in-flight kernel.
-      static int carve[64];
-      prefer_carveout_once(row_norm_pipe_kernel<T, VEC, ADD>, carve);
-      row_norm_pipe_kernel<T, VEC, ADD><<<static_cast<unsigned>(slots), kRowThreads, 0, stream>>>(a);
-      return launch_status();
+      return launch_ex(row_norm_pipe_kernel<T, VEC, ADD>, dim3(static_cast<unsigned>(slots)), dim3(kRowThreads), 0,
+                       stream, 1, NVB200_PDL_NORM, a);
     }
-    static int carve[64];
-    prefer_carveout_once(row_norm_kernel<T, VEC, ADD>, carve);
-    row_norm_kernel<T, VEC, ADD><<<static_cast<unsigned>(blocks), kRowThreads, 0, stream>>>(a);
-    return launch_status();
+    return launch_ex(row_norm_kernel<T, VEC, ADD>, dim3(static_cast<unsigned>(blocks)), dim3(kRowThreads), 0,
+                     stream, 1, NVB200_PDL_NORM, a);
   }
   if (a.rows > 0x7fffffffLL) return NVB200_ERR_UNSUPPORTED;
   if (nvec <= kMaxBlockThreads * kVecPerThread) {
     int threads = 64;
     while (threads * kVecPerThread < nvec) threads *= 2;
-    static int carve[64];
-    prefer_carveout_once(block_row_norm_kernel<T, VEC, ADD>, carve);
-    block_row_norm_kernel<T, VEC, ADD><<<static_cast<unsigned>(a.rows), threads, 0, stream>>>(a);
-    return launch_status();
+    return launch_ex(block_row_norm_kernel<T, VEC, ADD>, dim3(static_cast<unsigned>(a.rows)), dim3(threads), 0,
+                     stream, 1, NVB200_PDL_NORM, a);
   }
   long_row_norm_kernel<T, ADD><<<static_cast<unsigned>(a.rows), kRowThreads, 0, stream>>>(a);
   return launch_status();
@@ -431,6 +427,7 @@ template <typename T, int VEC>
 __global__ void __launch_bounds__(kSiluThreads) silu_and_mul_kernel(T *out, const T *x, int64_t rows, int n,
                                                                      int64_t x_row_stride) {
   launch_dependents();  // a dependent launched early waits for this grid before reading its output
+  grid_dependency_wait();  // this grid may itself have been launched early
   const int nv = n / VEC;
   const int cv = blockIdx.x * kSiluThreads + threadIdx.x;
   if (cv >= nv) return;
@@ -502,14 +499,10 @@ template <typename T> int launch_silu(void *out, const void *x, int64_t rows, in
   T *o = static_cast<T *>(out);
   const T *i = static_cast<const T *>(x);
   const int ni = static_cast<int>(n);
-  static int carve[2][64];
-  if (vec) {
-    prefer_carveout_once(silu_and_mul_kernel<T, VEC>, carve[0]);
+  if (vec)
     silu_and_mul_kernel<T, VEC><<<grid, kSiluThreads, 0, stream>>>(o, i, rows, ni, stride);
-  } else {
-    prefer_carveout_once(silu_and_mul_kernel<T, 1>, carve[1]);
+  else
     silu_and_mul_kernel<T, 1><<<grid, kSiluThreads, 0, stream>>>(o, i, rows, ni, stride);
-  }
   return launch_status();
 }
 
@@ -558,6 +551,7 @@ NVB200_DEVICE int stream_next_unit(int it, int NS, int W) {
 __global__ void __launch_bounds__(32 * (1 + kStreamWarps), kStreamCtas)
     rms_stream_kernel(const __grid_constant__ StreamArgs a) {
   launch_dependents();  // a dependent launched early waits for this grid before reading its output
+  grid_dependency_wait();  // this grid may itself have been launched early
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int NS = a.stages;

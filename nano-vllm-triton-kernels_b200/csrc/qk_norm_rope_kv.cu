@@ -146,6 +146,8 @@ NVB200_DEVICE int next_unit(int it, int NS, int W) {
 
 template <int D, int W, int CTAS>
 __global__ void __launch_bounds__(32 * (1 + W), CTAS) qknr_bulk_kernel(const __grid_constant__ QknrParams p) {
+  launch_dependents();     // a dependent launched early waits for this grid before reading its output
+  grid_dependency_wait();  // this grid may itself have been launched early
   constexpr int HALF = D / 2;
   constexpr int LPH = D / 16;    // lanes per head: each lane holds 8 + 8 elements
   constexpr int HPI = 32 / LPH;  // heads per warp step
@@ -357,6 +359,8 @@ constexpr int multi_stage_budget(int ctas) { return (228 * 1024) / ctas - 1024 -
 
 template <int D, int W, int CTAS>
 __global__ void __launch_bounds__(32 * (1 + W), CTAS) qknr_multi_kernel(const __grid_constant__ QknrParams p) {
+  launch_dependents();     // a dependent launched early waits for this grid before reading its output
+  grid_dependency_wait();  // this grid may itself have been launched early
   constexpr int HALF = D / 2;
   constexpr int LPH = D / 16;    // lanes per head: each lane holds 8 + 8 elements
   constexpr int HPI = 32 / LPH;  // heads per warp step
@@ -568,6 +572,8 @@ constexpr int64_t kDirectMaxBytes = NVB200_QKNR_DIRECT_MAX_BYTES;
 
 template <int D>
 __global__ void __launch_bounds__(32 * kDirectWarps) qknr_direct_kernel(const __grid_constant__ QknrParams p) {
+  launch_dependents();     // a dependent launched early waits for this grid before reading its output
+  grid_dependency_wait();  // this grid may itself have been launched early
   constexpr int HALF = D / 2;
   constexpr int LPH = D / 16;
   constexpr int HPI = 32 / LPH;
@@ -656,8 +662,7 @@ __global__ void __launch_bounds__(32 * kDirectWarps) qknr_direct_kernel(const __
 template <int D> int launch_direct(QknrParams &p, cudaStream_t stream) {
   constexpr int heads_per_cta = kDirectWarps * (32 / (D / 16));
   const dim3 grid(static_cast<unsigned>(p.num_tokens), (p.hq + p.hkv + heads_per_cta - 1) / heads_per_cta);
-  qknr_direct_kernel<D><<<grid, 32 * kDirectWarps, 0, stream>>>(p);
-  return launch_status();
+  return launch_ex(qknr_direct_kernel<D>, grid, dim3(32 * kDirectWarps), 0, stream, 1, NVB200_PDL_QKNR, p);
 }
 
 // ---------------------------------------------------------------------------------------------------------------
@@ -669,6 +674,8 @@ constexpr int kGenericMaxPairs = 8;  // D <= 512
 
 __global__ void __launch_bounds__(32 * kGenericWarps) qknr_generic_kernel(const __grid_constant__ QknrParams p,
                                                                           int D) {
+  launch_dependents();     // a dependent launched early waits for this grid before reading its output
+  grid_dependency_wait();  // this grid may itself have been launched early
   const int lane = threadIdx.x & 31;
   const int64_t t = blockIdx.x;
   const int h = blockIdx.y * kGenericWarps + (threadIdx.x >> 5);
@@ -765,8 +772,8 @@ int launch_bulk(QknrParams &p, int sms, cudaStream_t stream) {
   const int64_t grid = std::min<int64_t>(p.units, static_cast<int64_t>(sms) * CTAS);
   p.chunk = (p.units + grid - 1) / grid;
   const int64_t blocks = (p.units + p.chunk - 1) / p.chunk;
-  qknr_bulk_kernel<D, W, CTAS><<<static_cast<unsigned>(blocks), 32 * (1 + W), smem, stream>>>(p);
-  return launch_status();
+  return launch_ex(qknr_bulk_kernel<D, W, CTAS>, dim3(static_cast<unsigned>(blocks)), dim3(32 * (1 + W)), smem,
+                   stream, 1, NVB200_PDL_QKNR, p);
 }
 
 template <int D, int W, int CTAS, int MAX_STAGES>
@@ -789,8 +796,8 @@ int launch_multi(QknrParams &p, int sms, cudaStream_t stream) {
   const int64_t grid = std::min<int64_t>(p.units, static_cast<int64_t>(sms) * CTAS);
   p.chunk = (p.units + grid - 1) / grid;
   const int64_t blocks = (p.units + p.chunk - 1) / p.chunk;
-  qknr_multi_kernel<D, W, CTAS><<<static_cast<unsigned>(blocks), 32 * (1 + W), smem, stream>>>(p);
-  return launch_status();
+  return launch_ex(qknr_multi_kernel<D, W, CTAS>, dim3(static_cast<unsigned>(blocks)), dim3(32 * (1 + W)), smem,
+                   stream, 1, NVB200_PDL_QKNR, p);
 }
 
 template <int D> int launch_multi_shaped(QknrParams &p, int sms, cudaStream_t stream) {
