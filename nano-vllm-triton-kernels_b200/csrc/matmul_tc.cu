@@ -844,13 +844,36 @@ struct ArHeader {
   uint32_t completed;  // calls completed on this rank: this call's epoch is completed + 1
   uint32_t arrived;    // CTAs of the current call that are done
 };
-NVB200_DEVICE ArHeader *ar_header(const SkinnyParams &p, int owner) {
-  return reinterpret_cast<ArHeader *>(p.ar_base[owner]);
+NVB200_DEVICE ArHeader *ar_header_at(uint8_t *const *bases, int owner) {
+  return reinterpret_cast<ArHeader *>(bases[owner]);
 }
-NVB200_DEVICE uint64_t *ar_slot(const SkinnyParams &p, uint32_t epoch, int owner, int source) {
+NVB200_DEVICE uint64_t *ar_slot_at(uint8_t *const *bases, int64_t max_n, uint32_t epoch, int owner, int source) {
   const int64_t parity = epoch & 1;
-  return reinterpret_cast<uint64_t *>(p.ar_base[owner] + kArHeaderBytes) +
-         ((parity * kArMaxRanks + source) * kSkinnyMaxM) * p.ar_max_n;
+  return reinterpret_cast<uint64_t *>(bases[owner] + kArHeaderBytes) +
+         ((parity * kArMaxRanks + source) * kSkinnyMaxM) * max_n;
+}
+NVB200_DEVICE ArHeader *ar_header(const SkinnyParams &p, int owner) { return ar_header_at(p.ar_base, owner); }
+NVB200_DEVICE uint64_t *ar_slot(const SkinnyParams &p, uint32_t epoch, int owner, int source) {
+  return ar_slot_at(p.ar_base, p.ar_max_n, epoch, owner, source);
+}
+
+// Waits until the 8-byte exchange word at w carries `epoch` (bounded: after kWaitLimitNs the status bit is set and
+// *expired stops every later wait of the thread) and returns its fp32 value.
+NVB200_DEVICE float ar_take(const uint64_t *w, uint32_t epoch, bool *expired, uint64_t *start, int32_t *status) {
+  uint64_t a;
+  for (uint32_t spin = 1;; ++spin) {
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(a) : "l"(w) : "memory");
+    if ((a >> 32) == epoch || *expired) break;
+    if ((spin & 1023u) == 0) {
+      const uint64_t now = global_timer_ns();
+      if (*start == 0) *start = now;
+      else if (now - *start > kWaitLimitNs) {
+        set_status(status, NVB200_STATUS_WAIT_TIMEOUT);
+        *expired = true;
+      }
+    }
+  }
+  return __uint_as_float(static_cast<uint32_t>(a));
 }
 
 NVB200_DEVICE void store_c(const SkinnyParams &p, int m, int n, float v) {
@@ -1224,6 +1247,10 @@ struct StreamParams {
   uint32_t slot_off;  // the partials other CTAs of the cluster send (after the ring, which the sums reuse)
   uint32_t hdr_off;   // barriers
   int32_t *status;
+  // Fused all-reduce over ar_world GPUs (1: none): the exchange buffers of every rank, as for the skinny kernel.
+  int ar_world, ar_rank;
+  int64_t ar_max_n;
+  uint8_t *ar_base[kArMaxRanks];
 };
 
 // Address of the 16-byte chunk `ch` (0..7) of row `row` in a 128-byte-swizzled TMA tile at `tile` (rows of 128 bytes;
@@ -1412,22 +1439,98 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
   // Groups finished here: j = rank + S li (all of them when S == 1); for swiglu only the gate tiles (nt < NT / 2),
   // whose up partner j + 16 NT has the same owner (16 NT is a multiple of S).
   const int tiles_done = p.swiglu ? MT * (NT / 2) : MT * NT;
+  if (p.ar_world <= 1) {
+    for (int e = threadIdx.x; e < tiles_done * 32; e += kStreamThreads) {
+      const int ln = e & 31, t = e >> 5;
+      const int mt = p.swiglu ? t / (NT / 2) : t / NT, nt = p.swiglu ? t % (NT / 2) : t % NT;
+      const int j = (mt * NT + nt) * 32 + ln;
+      if (j % S != rank) continue;
+      const int row = mt * 16 + (ln >> 2), col = nt * 8 + 2 * (ln & 3);
+      const float4 v = group_sum(j);
+      if (!p.swiglu) {
+        store(row, n0 + col, pack_bf16x2(v.x, v.y));
+        store(row + 8, n0 + col, pack_bf16x2(v.z, v.w));
+      } else {
+        const float4 u = group_sum(j + 16 * NT);
+        const uint4 o = silu_mul8_bf16(make_uint4(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w), 0u, 0u),
+                                       make_uint4(pack_bf16x2(u.x, u.y), pack_bf16x2(u.z, u.w), 0u, 0u));
+        store(row, n0 + col, o.x);
+        store(row + 8, n0 + col, o.y);
+      }
+    }
+    return;
+  }
+
+  // -------------------------------------------------------------------- all-reduce over the GPUs (NVLink)
+  // The protocol of the skinny kernel's all-reduce (exchange buffers of epoch-tagged 8-byte words, two parities):
+  // 1. this GPU's sums of the CTA's groups go to every other rank's exchange buffer; 2. each group is summed over
+  // the ranks in rank order (the same bits on every GPU), the others' words taken once they carry this call's
+  // epoch; 3. the last CTA of the call advances this rank's epoch. Plain layout only (the host checks), N % 8 == 0
+  // so a group's column pair lies within N, and every CTA of the grid resident at once (the host checks).
+  const int W = p.ar_world, me = p.ar_rank;
+  uint32_t epoch;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];"
+               : "=r"(epoch)
+               : "l"(&ar_header_at(p.ar_base, me)->completed)
+               : "memory");
+  epoch += 1;
+  const uint64_t tag = static_cast<uint64_t>(epoch) << 32;
   for (int e = threadIdx.x; e < tiles_done * 32; e += kStreamThreads) {
-    const int ln = e & 31, t = e >> 5;
-    const int mt = p.swiglu ? t / (NT / 2) : t / NT, nt = p.swiglu ? t % (NT / 2) : t % NT;
+    const int ln = e & 31, t = e >> 5, mt = t / NT, nt = t % NT;
     const int j = (mt * NT + nt) * 32 + ln;
     if (j % S != rank) continue;
-    const int row = mt * 16 + (ln >> 2), col = nt * 8 + 2 * (ln & 3);
+    const int row = mt * 16 + (ln >> 2), n = n0 + nt * 8 + 2 * (ln & 3);
+    if (n >= p.N) continue;
     const float4 v = group_sum(j);
-    if (!p.swiglu) {
-      store(row, n0 + col, pack_bf16x2(v.x, v.y));
-      store(row + 8, n0 + col, pack_bf16x2(v.z, v.w));
-    } else {
-      const float4 u = group_sum(j + 16 * NT);
-      const uint4 o = silu_mul8_bf16(make_uint4(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w), 0u, 0u),
-                                     make_uint4(pack_bf16x2(u.x, u.y), pack_bf16x2(u.z, u.w), 0u, 0u));
-      store(row, n0 + col, o.x);
-      store(row + 8, n0 + col, o.y);
+    for (int dst = 0; dst < W; ++dst) {
+      if (dst == me) continue;
+      uint64_t *slot = ar_slot_at(p.ar_base, p.ar_max_n, epoch, dst, me) + n;
+      if (row < p.M)
+        asm volatile("st.relaxed.sys.global.v2.u64 [%0], {%1, %2};" ::"l"(slot + row * p.ar_max_n),
+                     "l"(tag | __float_as_uint(v.x)), "l"(tag | __float_as_uint(v.y))
+                     : "memory");
+      if (row + 8 < p.M)
+        asm volatile("st.relaxed.sys.global.v2.u64 [%0], {%1, %2};" ::"l"(slot + (row + 8) * p.ar_max_n),
+                     "l"(tag | __float_as_uint(v.z)), "l"(tag | __float_as_uint(v.w))
+                     : "memory");
+    }
+  }
+  bool expired = false;
+  uint64_t start = 0;
+  for (int e = threadIdx.x; e < tiles_done * 32; e += kStreamThreads) {
+    const int ln = e & 31, t = e >> 5, mt = t / NT, nt = t % NT;
+    const int j = (mt * NT + nt) * 32 + ln;
+    if (j % S != rank) continue;
+    const int row = mt * 16 + (ln >> 2), n = n0 + nt * 8 + 2 * (ln & 3);
+    if (n >= p.N) continue;
+    const float4 mine = group_sum(j);
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int src = 0; src < W; ++src) {
+      float x[4] = {mine.x, mine.y, mine.z, mine.w};
+      if (src != me) {
+        const uint64_t *w = ar_slot_at(p.ar_base, p.ar_max_n, epoch, me, src) + n;
+        if (row < p.M) {
+          x[0] = ar_take(w + row * p.ar_max_n, epoch, &expired, &start, p.status);
+          x[1] = ar_take(w + row * p.ar_max_n + 1, epoch, &expired, &start, p.status);
+        }
+        if (row + 8 < p.M) {
+          x[2] = ar_take(w + (row + 8) * p.ar_max_n, epoch, &expired, &start, p.status);
+          x[3] = ar_take(w + (row + 8) * p.ar_max_n + 1, epoch, &expired, &start, p.status);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[i] += x[i];
+    }
+    store(row, n, pack_bf16x2(acc[0], acc[1]));
+    store(row + 8, n, pack_bf16x2(acc[2], acc[3]));
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    ArHeader *h = ar_header_at(p.ar_base, me);
+    if (atomicAdd(&h->arrived, 1u) == gridDim.x - 1) {
+      h->arrived = 0;
+      __threadfence();
+      h->completed = epoch;
     }
   }
 }
@@ -1539,7 +1642,8 @@ StreamPlan stream_plan(int64_t M, int64_t N, int64_t K, bool swiglu, int sms) {
 // (scn == 1); returns NVB200_ERR_UNSUPPORTED otherwise. early_weights: the caller guarantees that no kernel in
 // flight writes B (model weights), so the launch may let the weight loads overlap the preceding kernel.
 int launch_stream(void *c, const void *a, const void *b, int64_t M, int64_t N, int64_t K, int64_t sam, int64_t sbn,
-                  int64_t scm, int64_t scn, bool swiglu, bool early_weights, int32_t *status, cudaStream_t stream) {
+                  int64_t scm, int64_t scn, bool swiglu, bool early_weights, int32_t *status, cudaStream_t stream,
+                  const nvb200_allreduce_group *ar = nullptr) {
   if (!NVB200_MM_STREAM || M <= 0 || M > 64 || N <= 0 || scn != 1 || K <= 0 || (sam * 2) % 16 != 0 ||
       (sbn * 2) % 16 != 0 || N > 0x3fffffffLL || K > 0x3fffffffLL)
     return NVB200_ERR_UNSUPPORTED;
@@ -1566,6 +1670,19 @@ int launch_stream(void *c, const void *a, const void *b, int64_t M, int64_t N, i
   p.slot_off = (std::max(p.stages * stage_bytes, red_bytes) + 255u) / 256u * 256u;
   p.hdr_off = p.slot_off + (p.split > 1 ? (groups + p.split - 1) / p.split * p.split * 16u : 0u);
   p.status = status;
+  p.ar_world = 1;
+  if (ar != nullptr) {
+    // Every CTA waits for its counterparts on the other GPUs, so the whole grid must be resident (one CTA per SM).
+    // (16-byte word pairs: the row pitch max_n must be even.)
+    if (swiglu || ar->world < 2 || ar->world > kArMaxRanks || ar->rank < 0 || ar->rank >= ar->world || N % 8 != 0 ||
+        N > ar->max_n || ar->max_n % 2 != 0 || M > kSkinnyMaxM || grid > std::min(sm_count(), kArMaxGrid))
+      return NVB200_ERR_UNSUPPORTED;
+    p.ar_world = ar->world, p.ar_rank = ar->rank, p.ar_max_n = ar->max_n;
+    for (int r = 0; r < ar->world; ++r) {
+      if (ar->buffers[r] == nullptr) return NVB200_ERR_ARG;
+      p.ar_base[r] = static_cast<uint8_t *>(ar->buffers[r]);
+    }
+  }
   const int smem = static_cast<int>(1024 + p.hdr_off + 2 * 8 * kStreamMaxStages);
   CUtensorMap map_a, map_w;
   if (!make_map(&map_a, a, false, K, M, sam, 64, 16 * MT) ||
@@ -1603,7 +1720,7 @@ int launch_skinny(void *c, const void *a, const void *b, int64_t M, int64_t N, i
   if (ar != nullptr) {
     // Every CTA waits for its peers' CTAs of the same slice, so all of them must be resident at once.
     if (ar->world < 2 || ar->world > kArMaxRanks || ar->rank < 0 || ar->rank >= ar->world || N % 4 != 0 ||
-        N > ar->max_n || static_cast<int64_t>(tiles) * split > std::min(sms, kArMaxGrid))
+        N > ar->max_n || ar->max_n % 2 != 0 || static_cast<int64_t>(tiles) * split > std::min(sms, kArMaxGrid))
       return NVB200_ERR_UNSUPPORTED;
     p.ar_world = ar->world, p.ar_rank = ar->rank, p.ar_max_n = ar->max_n;
     for (int r = 0; r < ar->world; ++r) {
@@ -1810,6 +1927,10 @@ int matmul_allreduce_launch(void *c, const void *a, const void *b, int64_t M, in
   if (K <= 0 || M > kSkinnyMaxM || N > 0x3fffffffLL || K > 0x7fffffffLL) return NVB200_ERR_UNSUPPORTED;
   if (sak != 1 || sbk != 1 || (sam * 2) % 16 != 0 || (sbn * 2) % 16 != 0 || !aligned16(a) || !aligned16(b))
     return NVB200_ERR_UNSUPPORTED;
+  // The weight-streaming kernel with the all-reduce epilogue (plain stream order: B is not promised to be a weight
+  // that no kernel in flight writes), else the skinny kernel's.
+  const int rc = launch_stream(c, a, b, M, N, K, sam, sbn, scm, 1, false, false, status, stream, g);
+  if (rc != NVB200_ERR_UNSUPPORTED) return rc;
   return launch_skinny(c, a, b, M, N, K, sam, sbn, scm, 1, false, status, stream, g);
 }
 
