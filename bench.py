@@ -55,7 +55,10 @@ def parse_args():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default="fused8b",
                     choices=["fused8b", "fused06b", "norm", "rmsnorm", "addrmsnorm", "silu", "matmul", "gateup",
-                             "rowpar", "attn", "storekv", "decode"])
+                             "rowpar", "attn", "storekv", "decode", "projections"])
+    ap.add_argument("--proj-model", default="qwen3-0.6b", choices=sorted(PROJECTIONS),
+                    help="--workload projections: which model's decode projections")
+    ap.add_argument("--proj-rows", type=int, default=32, help="--workload projections: rows (decode batch)")
     ap.add_argument("--decode-worker", default=None, help=argparse.SUPPRESS)
     ap.add_argument("--decode-backends", default="b200,compile,triton_fused")
     ap.add_argument("--decode-batch", type=int, default=32)
@@ -922,6 +925,94 @@ def run_decode(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+# Decode projections (`--workload projections`): each projection of a Qwen3 decode layer preceded by this library's
+# RMSNorm (as in the model, so that the projection kernel may start while the norm finishes), over enough distinct
+# weights that they come from HBM (at least 28, at least 2.4x the L2 in all), captured in one CUDA graph and
+# replayed; us per norm + projection, median of 5 x 10 replays. b200 runs the route install() takes for the layer
+# (nanovllm_b200.kernels.matmul: linear_decode where decode_gemm_applies / fused_gate_up_applies admit it, else
+# cuBLAS); cuBLAS is torch's F.linear (and the SiLU x Mul kernel for gate_up), what the reference's layers run.
+PROJECTIONS = {"qwen3-0.6b": {"qkv_proj": (4096, 1024, False), "o_proj": (1024, 2048, False),
+                              "gate_up_proj+silu": (3072, 1024, True), "down_proj": (1024, 3072, False)},
+               "qwen3-8b": {"qkv_proj": (6144, 4096, False), "o_proj": (4096, 4096, False),
+                            "gate_up_proj+silu": (12288, 4096, True), "down_proj": (4096, 12288, False)}}
+
+
+def run_projections(args) -> None:
+    import statistics
+    import nanovllm_b200.kernels.matmul as mm
+    from nanovllm_b200.kernels.rms_norm import rms_norm
+    from nanovllm_b200.kernels.swiglu import silu_and_mul
+    dev = torch.device("cuda", 0)
+    rows = args.proj_rows
+    res = {}
+
+    def timed(fn, calls):
+        fn()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            fn()
+        for _ in range(3):
+            graph.replay()
+        torch.cuda.synchronize()
+        out = []
+        for _ in range(5):
+            s_, e_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s_.record()
+            for _ in range(10):
+                graph.replay()
+            e_.record()
+            torch.cuda.synchronize()
+            out.append(s_.elapsed_time(e_) * 1e3 / (10 * calls))
+        del graph
+        return statistics.median(out)
+
+    g = torch.Generator(device=dev).manual_seed(17)
+    with torch.inference_mode(), ClockSampler(0) as clocks:
+        clocks.mark_start()
+        for name, (n, k, swiglu) in PROJECTIONS[args.proj_model].items():
+            w_rows = 2 * n if swiglu else n
+            count = max(28, -(-int(2.4 * 126e6) // (w_rows * k * 2)))
+            x = torch.randn(rows, k, device=dev, generator=g).to(torch.bfloat16)
+            nw = (1 + 0.1 * torch.randn(k, device=dev, generator=g)).to(torch.bfloat16)
+            ws = [torch.randn(w_rows, k, device=dev, generator=g).to(torch.bfloat16) for _ in range(count)]
+            routed = (mm.fused_gate_up_applies(x, ws[0]) if swiglu else mm.decode_gemm_applies(x, ws[0]))
+
+            def ours():
+                for w in ws:
+                    h = rms_norm(x, nw, 1e-6)
+                    y = mm.linear_decode(h, w, swiglu=swiglu) if routed else None
+                    if y is None:
+                        y = h @ w.t()
+                        if swiglu:
+                            silu_and_mul(y)
+
+            def cublas():
+                for w in ws:
+                    y = rms_norm(x, nw, 1e-6) @ w.t()
+                    if swiglu:
+                        silu_and_mul(y)
+
+            def norm_only():
+                for _ in ws:
+                    rms_norm(x, nw, 1e-6)
+            res[name] = {"shape": [rows, n, k], "weights": count, "routed_to_b200_kernel": routed,
+                         "b200_us": timed(ours, count), "cublas_us": timed(cublas, count),
+                         "norm_alone_us": timed(norm_only, count)}
+            del ws
+        clocks.mark_end()
+    b = sum(r["b200_us"] for r in res.values())
+    c = sum(r["cublas_us"] for r in res.values())
+    line = {"metric": f"decode projections: us per layer for RMSNorm + projection, {args.proj_model} shapes, "
+                      f"{rows} rows, CUDA graph", "value": b, "unit": "us", "n_gpus": 1, "steps": 50, "warmup": 4,
+            "ms_per_step": b / 1e3, "higher_is_better": False, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic (seeded weights and rows)",
+            "config": {"workload": "projections", "model": args.proj_model, "rows": rows,
+                       "l2": "weights rotate over >= 2.4x the L2"},
+            "cublas_us": c, "b200_vs_cublas": c / b, "projections": res, "clocks": clocks.summary()}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse_args()
     if args.decode_worker:
@@ -932,6 +1023,9 @@ def main():
         return
     if args.workload == "decode":
         run_decode(args)
+        return
+    if args.workload == "projections":
+        run_projections(args)
         return
     rank, world, local = setup_dist(args)
     if args.impl == "reference":

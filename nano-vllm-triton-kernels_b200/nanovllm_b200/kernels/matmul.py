@@ -84,14 +84,18 @@ def linear_decode(x: torch.Tensor, weight: torch.Tensor, swiglu: bool = False) -
 
 
 # Which of a b200 model's linear layers run `linear_decode` (nanovllm_b200.install(), steps 7 and 8) instead of
-# cuBLAS, as measured on B200 (each projection preceded by this library's RMSNorm, 28 weights per CUDA graph, 32
-# rows; us per norm + projection, the norm alone 1.7-2.6 us):
-#   Qwen3-0.6B o_proj 1024 x 2048:       6.28 (cuBLAS 9.03)     down_proj 1024 x 3072:  6.96 (cuBLAS 10.30)
-#   gate_up 2 x 3072 x 1024 + SiLU x Mul: 8.74 (cuBLAS + the SiLU x Mul kernel 10.73)
-#   qkv_proj 4096 x 1024:                7.09 (cuBLAS 6.24)     Qwen3-8B gate_up + SiLU x Mul: 56.8 (44.6)
-# so plain projections go through it when N <= K (the o and down projections) and the gate_up projection with its
-# SiLU x Mul when its weight is at most 32 MB; batches of at most 32 rows (at 64 rows cuBLAS was as fast or faster).
+# cuBLAS, as measured on B200 by `bench.py --workload projections` (each projection after this library's RMSNorm,
+# weights rotating over more than the L2, one CUDA graph; us per norm + projection):
+#   Qwen3-0.6B, 32 rows: o_proj 1024 x 2048      7.01 (cuBLAS  8.04)   down_proj 1024 x 3072    7.52 (cuBLAS  9.23)
+#                        gate_up + SiLU x Mul    7.43 (cuBLAS + the SiLU x Mul kernel 9.28)
+#                        qkv_proj 4096 x 1024    cuBLAS 6.15; the weight-streaming kernel measured slower at this shape
+#   Qwen3-0.6B, 1 row:   o_proj 5.38 (9.91), down_proj 6.01 (11.87), gate_up + SiLU x Mul 6.32 (8.67)
+#   Qwen3-8B, 32 rows:   o_proj 4096 x 4096 12.26 (11.73), down_proj 4096 x 12288 25.97 (25.23), gate_up 44.6 (42.6)
+# so plain projections go through it when N <= K and the weight is at most 16 MB (the o and down projections of the
+# small model), the gate_up projection with its SiLU x Mul when its weight is at most 32 MB; batches of at most 32
+# rows (at 64 rows cuBLAS was as fast or faster).
 DECODE_GEMM_MAX_ROWS = 32
+DECODE_GEMM_MAX_WEIGHT_BYTES = 16 << 20
 FUSED_GATE_UP_MAX_ROWS = 32
 FUSED_GATE_UP_MAX_WEIGHT_BYTES = 32 << 20
 
@@ -100,7 +104,8 @@ def decode_gemm_applies(x: torch.Tensor, weight: torch.Tensor) -> bool:
     """Whether a linear layer of a b200 model runs x @ weight.t() through `linear_decode`."""
     return (x.dim() == 2 and 0 < x.shape[0] <= DECODE_GEMM_MAX_ROWS and weight.dim() == 2
             and x.dtype == weight.dtype == torch.bfloat16 and weight.shape[1] == x.shape[1]
-            and weight.shape[0] <= weight.shape[1])
+            and weight.shape[0] <= weight.shape[1]
+            and weight.numel() * weight.element_size() <= DECODE_GEMM_MAX_WEIGHT_BYTES)
 
 
 def fused_gate_up_applies(x: torch.Tensor, weight: torch.Tensor) -> bool:
