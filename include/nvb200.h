@@ -172,6 +172,29 @@ NVB200_API int nvb200_linear_decode(void *y, const void *x, const void *weight, 
                                     int64_t sx, int64_t sw, int64_t sy, int swiglu, int32_t *status,
                                     nvb200_stream_t stream);
 
+/* The decode qkv projection with the fused q/k op as its epilogue: qkv = x[M, K] @ qkv_weight^T rounded to bf16
+ * ([Hq q heads | Hkv k heads | Hkv v heads] of 128 columns, QKVParallelLinear's layout), then exactly what
+ * nvb200_qk_norm_rope_kv does with q, k, v = the three parts of qkv: q heads RMSNorm + RoPE into q_out, k heads
+ * RMSNorm + RoPE into k_cache[slot], v heads into v_cache[slot] (slot -1 skipped; k_cache NULL: nothing stored).
+ * The qkv intermediate is never written. As for nvb200_linear_decode, qkv_weight is a model parameter that no kernel
+ * in flight writes (its loads may start while the preceding kernel finishes).
+ * Replaces: the qkv_proj F.linear (nanovllm/layers/linear.py:72-73 via models/qwen3.py:91-94) followed by
+ * qk_norm_rope_kv (nanovllm/kernels/qk_norm_rope_kv.py:92-125, called at layers/attention.py:71-72) in the decode
+ * branch of kernel_backend "triton_fused".
+ * qknr: the fused op's arguments with num_tokens = M; q, k, v and their strides are ignored; k_out must be NULL.
+ * Takes bf16, 1 <= M <= 32, head_dim 128, x and qkv_weight with unit last strides and 16-byte row pitches (x_row_stride,
+ * weight_row_stride in elements); NVB200_ERR_UNSUPPORTED otherwise (the caller runs the two steps). */
+typedef struct nvb200_linear_qkv_args {
+  const void *x;
+  int64_t x_row_stride;
+  const void *qkv_weight;
+  int64_t weight_row_stride;
+  int64_t K;
+  nvb200_qk_norm_rope_kv_args qknr;
+} nvb200_linear_qkv_args;
+
+NVB200_API int nvb200_linear_qkv_norm_rope_kv(const nvb200_linear_qkv_args *args, nvb200_stream_t stream);
+
 /* Row-parallel GEMM fused with its all-reduce over NVLink (decode-sized rows), for tensor parallelism: rank r
  * holds A_r [M, K_r] and B_r [K_r, N] (its K shard); every rank receives out[M, N] = sum over ranks of A_r @ B_r in
  * bf16, summed in fp32 in rank order (so every rank gets the same bits). One kernel per rank computes its partial

@@ -21,6 +21,8 @@ int matmul_swiglu_launch(void *c, const void *a, const void *b, int64_t M, int64
                          int64_t sak, int64_t sbk, int64_t sbn, int64_t scm, int32_t *status, cudaStream_t stream);
 int linear_decode_launch(void *y, const void *x, const void *w, int64_t M, int64_t N, int64_t K, int64_t sx,
                          int64_t sw, int64_t sy, bool swiglu, int32_t *status, cudaStream_t stream);
+int linear_qkv_launch(const void *x, int64_t sx, const void *w, int64_t sw, int64_t K,
+                      const nvb200_qk_norm_rope_kv_args &a, cudaStream_t stream);
 int64_t allreduce_buffer_bytes(int64_t max_n);
 int matmul_allreduce_launch(void *c, const void *a, const void *b, int64_t M, int64_t N, int64_t K, int64_t sam,
                             int64_t sak, int64_t sbk, int64_t sbn, int64_t scm, const nvb200_allreduce_group *g,
@@ -209,6 +211,23 @@ extern "C" int nvb200_linear_decode(void *y, const void *x, const void *weight, 
   if (int rc = check_device()) return rc;
   return linear_decode_launch(y, x, weight, M, N, K, sx, sw, sy, swiglu != 0, status,
                               reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int nvb200_linear_qkv_norm_rope_kv(const nvb200_linear_qkv_args *args, nvb200_stream_t stream) {
+  if (args == nullptr) return NVB200_ERR_ARG;
+  const nvb200_qk_norm_rope_kv_args &a = args->qknr;
+  if (a.num_tokens < 0 || a.num_q_heads <= 0 || a.num_kv_heads <= 0 || a.num_q_heads % a.num_kv_heads != 0 ||
+      a.head_dim <= 0 || args->K < 0 || a.num_positions <= 0 || a.cos_sin_stride < 0)
+    return NVB200_ERR_ARG;
+  if (a.k_cache != nullptr && (a.v_cache == nullptr || a.slot_mapping == nullptr || a.num_slots <= 0))
+    return NVB200_ERR_ARG;
+  if (a.num_tokens == 0) return NVB200_OK;
+  if (args->K == 0) return NVB200_ERR_UNSUPPORTED;
+  if (!args->x || !args->qkv_weight || !a.q_out || !a.positions || !a.q_weight || !a.k_weight || !a.cos_sin)
+    return NVB200_ERR_ARG;
+  if (int rc = check_device()) return rc;
+  return linear_qkv_launch(args->x, args->x_row_stride, args->qkv_weight, args->weight_row_stride, args->K, a,
+                           reinterpret_cast<cudaStream_t>(stream));
 }
 
 extern "C" int64_t nvb200_allreduce_buffer_bytes(int64_t max_n) {

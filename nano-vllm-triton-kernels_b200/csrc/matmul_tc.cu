@@ -22,6 +22,7 @@
 #include <cudaTypedefs.h>
 
 #include "common.cuh"
+#include "qknr_math.cuh"
 
 namespace nvb200 {
 namespace {
@@ -1251,6 +1252,21 @@ struct StreamParams {
   int ar_world, ar_rank;
   int64_t ar_max_n;
   uint8_t *ar_base[kArMaxRanks];
+  // epi = 1: the qkv projection with the fused q/k op as its epilogue. Slice t of 128 columns is head t of
+  // [Hq q heads | Hkv k heads | Hkv v heads]; q heads get RMSNorm (q_w) + RoPE into q_out [M, Hq, 128], k heads
+  // RMSNorm (k_w) + RoPE into k_cache[slot], v heads go to v_cache[slot] (slot -1: not stored; no cache: nothing).
+  int epi;
+  __nv_bfloat16 *q_out, *k_cache, *v_cache;
+  const int64_t *positions;
+  const int32_t *slots;
+  const float *cos_sin;
+  int64_t cs_stride, num_positions, num_slots;
+  const __nv_bfloat16 *q_w, *k_w;
+  int hq, hkv;
+  float eps;
+  uint32_t head_off;  // shared-memory offset of the [16 MT][128] bf16 staging tile of the slice's rows
+  uint32_t side_off;  // shared-memory offset of the epilogue's inputs: [16 MT] slots, [16 MT][128] fp32 cos | sin
+                      // rows, the 128 bf16 norm weights of the slice's head
 };
 
 // Address of the 16-byte chunk `ch` (0..7) of row `row` in a 128-byte-swizzled TMA tile at `tile` (rows of 128 bytes;
@@ -1259,13 +1275,22 @@ NVB200_DEVICE uint32_t sw128(uint32_t tile, int row, int ch) {
   return tile + row * 128 + ((ch ^ (row & 7)) << 4);
 }
 
+// 16-byte asynchronous global -> shared copy (cp.async), its commit and the wait for all of a thread's copies.
+NVB200_DEVICE void cp_async16(uint32_t dst, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+NVB200_DEVICE void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+NVB200_DEVICE void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 NVB200_DEVICE float ld_cluster_f32(uint32_t addr) {
   float v;
   asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
   return v;
 }
 
-template <int MT, int NT>
+// WN: the consumer warps split the slice's NT tiles into WN parts; warp w takes the WN k-steps w mod KW, + KW, ...
+// (KW = 8 / WN) of every chunk for the NT / WN tiles of part w / KW (WN = 1: one k-step, every tile).
+template <int MT, int NT, int WN = 1>
 __global__ void __launch_bounds__(kStreamThreads, 1)
     matmul_stream_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w,
                          const __grid_constant__ StreamParams p) {
@@ -1273,6 +1298,8 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   constexpr int NS = 8 * NT;
   constexpr int G = MT * NT * 32;  // fragment groups: (m tile, n tile, lane), four fp32 values each
+  constexpr int NTW = NT / WN, KW = kStreamConsumers / WN;
+  static_assert(NT % WN == 0 && kStreamConsumers % WN == 0, "tiles and warps must split evenly");
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int S = p.split, stages = p.stages;
   const int rank = static_cast<int>(blockIdx.x) % S, tile = static_cast<int>(blockIdx.x) / S;
@@ -1321,11 +1348,11 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
   }
   __syncthreads();
 
-  float acc[MT][NT][4];
+  float acc[MT][NTW][4];
 #pragma unroll
   for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) acc[mt][nt][0] = acc[mt][nt][1] = acc[mt][nt][2] = acc[mt][nt][3] = 0.f;
+    for (int nt = 0; nt < NTW; ++nt) acc[mt][nt][0] = acc[mt][nt][1] = acc[mt][nt][2] = acc[mt][nt][3] = 0.f;
 
   if (warp == kStreamConsumers) {
     // ------------------------------------------------------------------ producer (one lane): A, then the rest
@@ -1344,73 +1371,129 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
       }
     }
   } else {
-    // ------------------------------------------------------------------ consumers: k-step `warp` of every chunk
-    const int h = warp >> 2;            // which 64-element box of the chunk
-    const int ch0 = (warp & 3) * 2;     // first 16-byte chunk of the k-step in the box's 128-byte rows
-    const int arow = (lane & 7) + ((lane >> 3) & 1) * 8, ach = ch0 + (lane >> 4);
-    const int wrow = ((lane >> 4) << 3) + (lane & 7), wch = ch0 + ((lane >> 3) & 1);
+    // ------------------------------------------------------------------ consumers
+    if (p.epi == 1) {
+      // qkv epilogue inputs, fetched while the first chunks are on their way: for each row this CTA finishes, its
+      // slot and position (out-of-range values flagged as the fused op flags them), then asynchronous copies of its
+      // cos | sin row and of the head's norm weights into shared memory (waited for before the epilogue).
+      grid_dependency_wait();
+      const int head = static_cast<int>(blockIdx.x) / S;
+      const bool isq = head < p.hq, isv = head >= p.hq + p.hkv;
+      int32_t *slot_s = reinterpret_cast<int32_t *>(smem + p.side_off);
+      int32_t *pos_s = slot_s + 32;
+      const uint32_t cs_s = base + p.side_off + 64 * 4, w_s = cs_s + 16 * MT * 128 * 4;
+      const int own = p.M > rank ? (p.M - rank + S - 1) / S : 0;  // rows rank, rank + S, ...
+      const int t = threadIdx.x;                                 // 0..255 (the consumer warps)
+      if (t < own) {
+        const int m = rank + S * t;
+        int32_t slot = -1;
+        if (!isq && p.k_cache != nullptr) {
+          slot = __ldg(p.slots + m);
+          if (slot < -1 || slot >= p.num_slots) {
+            set_status(p.status, NVB200_STATUS_BAD_SLOT);
+            slot = -1;
+          }
+        }
+        int64_t pos = -1;
+        if (!isv && (isq || slot >= 0)) {
+          pos = __ldg(p.positions + m);
+          if (pos < 0 || pos >= p.num_positions) {
+            set_status(p.status, NVB200_STATUS_BAD_POSITION);
+            pos = 0;
+          }
+        }
+        slot_s[m] = slot;
+        pos_s[t] = static_cast<int32_t>(pos);
+      }
+      asm volatile("bar.sync 1, %0;" ::"n"(32 * kStreamConsumers) : "memory");  // the consumer warps only
+      for (int idx = t; idx < own * 32; idx += 32 * kStreamConsumers) {
+        const int u = idx >> 5, i = idx & 31;
+        const int32_t pos = pos_s[u];
+        if (pos >= 0) cp_async16(cs_s + ((rank + S * u) * 128 + 4 * i) * 4, p.cos_sin + pos * p.cs_stride + 4 * i);
+      }
+      if (!isv && t < 16) cp_async16(w_s + 16 * t, (isq ? p.q_w : p.k_w) + 8 * t);
+      cp_async_commit();
+    }
+    const int kw = warp % KW, npart = warp / KW;
+    const int arow = (lane & 7) + ((lane >> 3) & 1) * 8;
+    const int wrow = ((lane >> 4) << 3) + (lane & 7);
     for (int i = 0; i < nch; ++i) {
       const int st = i % stages;
       if (!mbar_wait_bounded(bar_full + 8 * st, (i / stages) & 1)) {
         if (lane == 0) set_status(p.status, NVB200_STATUS_WAIT_TIMEOUT);
         break;
       }
-      const uint32_t abox = base + st * stage_bytes + h * (p.a_bytes / 2);
-      const uint32_t wbox = base + st * stage_bytes + p.a_bytes + h * (p.w_bytes / 2);
-      uint32_t af[MT][4];
 #pragma unroll
-      for (int mt = 0; mt < MT; ++mt) ldsm_x4(sw128(abox, mt * 16 + arow, ach), af[mt]);
+      for (int ks = 0; ks < WN; ++ks) {
+        const int kstep = kw + KW * ks;      // 0..7: 16-element step of the chunk
+        const int h = kstep >> 2;            // which 64-element box of the chunk
+        const int ch0 = (kstep & 3) * 2;     // first 16-byte chunk of the k-step in the box's 128-byte rows
+        const int ach = ch0 + (lane >> 4), wch = ch0 + ((lane >> 3) & 1);
+        const uint32_t abox = base + st * stage_bytes + h * (p.a_bytes / 2);
+        // This warp's part of the slice starts NTW * 8 rows into the box (a multiple of 8 rows: same swizzle).
+        const uint32_t wbox = base + st * stage_bytes + p.a_bytes + h * (p.w_bytes / 2) + npart * NTW * 8 * 128;
+        uint32_t af[MT][4];
 #pragma unroll
-      for (int np = 0; np < NT / 2; ++np) {
-        uint32_t bw[4];
-        ldsm_x4(sw128(wbox, np * 16 + wrow, wch), bw);
+        for (int mt = 0; mt < MT; ++mt) ldsm_x4(sw128(abox, mt * 16 + arow, ach), af[mt]);
 #pragma unroll
-        for (int mt = 0; mt < MT; ++mt) {
-          mma_16816(acc[mt][2 * np], af[mt], bw[0], bw[1]);
-          mma_16816(acc[mt][2 * np + 1], af[mt], bw[2], bw[3]);
+        for (int np = 0; np < NTW / 2; ++np) {
+          uint32_t bw[4];
+          ldsm_x4(sw128(wbox, np * 16 + wrow, wch), bw);
+#pragma unroll
+          for (int mt = 0; mt < MT; ++mt) {
+            mma_16816(acc[mt][2 * np], af[mt], bw[0], bw[1]);
+            mma_16816(acc[mt][2 * np + 1], af[mt], bw[2], bw[3]);
+          }
         }
-      }
-      if constexpr (NT % 2 == 1) {
-        uint32_t bw[2];
-        ldsm_x2(sw128(wbox, (NT - 1) * 8 + (lane & 7), ch0 + ((lane >> 3) & 1)), bw);
+        if constexpr (NTW % 2 == 1) {
+          uint32_t bw[2];
+          ldsm_x2(sw128(wbox, (NTW - 1) * 8 + (lane & 7), ch0 + ((lane >> 3) & 1)), bw);
 #pragma unroll
-        for (int mt = 0; mt < MT; ++mt) mma_16816(acc[mt][NT - 1], af[mt], bw[0], bw[1]);
+          for (int mt = 0; mt < MT; ++mt) mma_16816(acc[mt][NTW - 1], af[mt], bw[0], bw[1]);
+        }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(bar_empty + 8 * st);  // this warp is done with the stage
     }
   }
 
+  if (p.epi == 1) cp_async_wait_all();  // the epilogue's inputs (a no-op for threads that copied nothing)
   // -------------------------------------------------------------------- sums
   // Every chunk was consumed, so no copy is in flight and the ring is free: the warps' shares go there in fragment
   // order (group j = (mt NT + nt) 32 + lane, a float4 per group and warp: conflict-free), each thread then sums the
   // eight shares of its groups. With a split, the sum of group j goes to the shared memory of the CTA that finishes
   // it (rank j % S, slot [this rank][j / S]); one cluster barrier later each CTA adds the S partials of its groups.
   __syncthreads();
-  float4 *red = reinterpret_cast<float4 *>(smem);  // [warp][G]
+  float4 *red = reinterpret_cast<float4 *>(smem);  // [k part][G]
   if (warp < kStreamConsumers) {
+    const int kw = warp % KW, npart = warp / KW;
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt)
-        red[warp * G + (mt * NT + nt) * 32 + lane] =
+      for (int nt = 0; nt < NTW; ++nt)
+        red[kw * G + (mt * NT + npart * NTW + nt) * 32 + lane] =
             make_float4(acc[mt][nt][0], acc[mt][nt][1], acc[mt][nt][2], acc[mt][nt][3]);
   }
   __syncthreads();
+  // Owner of group j and its slot there. Plain and gate_up forms: rank j mod S, slot j / S. The qkv epilogue keeps
+  // rows together: rank g mod S, g = (j mod 32) / 4 the group's row in its m tile (rows g and g + 8 share it, S | 8),
+  // slot (j / 32) (32 / S) + (g / S) 4 + j mod 4.
+  auto owner = [&](int j) { return p.epi ? ((j & 31) >> 2) % S : j % S; };
+  auto slot_of = [&](int j) { return p.epi ? (j >> 5) * (32 / S) + (((j & 31) >> 2) / S) * 4 + (j & 3) : j / S; };
   const int per_owner = (G + S - 1) / S;
   const uint32_t slots = base + p.slot_off;  // [S][per_owner] float4
   if (S > 1) asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
   for (int j = threadIdx.x; j < G; j += kStreamThreads) {
     float4 v = red[j];
 #pragma unroll
-    for (int w = 1; w < kStreamConsumers; ++w) {
+    for (int w = 1; w < KW; ++w) {
       const float4 x = red[w * G + j];
       v.x += x.x, v.y += x.y, v.z += x.z, v.w += x.w;
     }
     if (S == 1) {
       red[j] = v;  // this thread's element alone
     } else {
-      const uint32_t dst = map_to_cta(slots + (rank * per_owner + j / S) * 16, j % S);
+      const uint32_t dst = map_to_cta(slots + (rank * per_owner + slot_of(j)) * 16, owner(j));
       asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "f"(v.x), "f"(v.y), "f"(v.z),
                    "f"(v.w)
                    : "memory");
@@ -1422,7 +1505,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
   auto group_sum = [&](int j) {
     if (S == 1) return red[j];
     const float4 *sl = reinterpret_cast<const float4 *>(smem + p.slot_off);
-    const int li = j / S;
+    const int li = slot_of(j);
     float4 v = sl[li];
     for (int q = 1; q < S; ++q) {
       const float4 x = sl[q * per_owner + li];
@@ -1438,13 +1521,60 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
   };
   // Groups finished here: j = rank + S li (all of them when S == 1); for swiglu only the gate tiles (nt < NT / 2),
   // whose up partner j + 16 NT has the same owner (16 NT is a multiple of S).
+  if (p.epi == 1) {
+    // ------------------------------------------------------------------ qkv epilogue: the fused q/k op per row
+    // This CTA's rows (m mod S == rank) of the slice, rounded to bf16 as the projection's output, go to a staging
+    // tile; then 8 lanes per row run the fused op's per-head math on them (the direct kernel's lane layout and
+    // operations, so the same bits as qk_norm_rope_kv on that output).
+    __nv_bfloat16 *hs = reinterpret_cast<__nv_bfloat16 *>(smem + p.head_off);  // [16 MT][128]
+    for (int j = threadIdx.x; j < G; j += kStreamThreads) {
+      if (owner(j) != rank) continue;
+      const int ln = j & 31, t = j >> 5, mt = t / NT, nt = t % NT;
+      const int row = mt * 16 + (ln >> 2), col = nt * 8 + 2 * (ln & 3);
+      const float4 v = group_sum(j);
+      *reinterpret_cast<uint32_t *>(hs + row * 128 + col) = pack_bf16x2(v.x, v.y);
+      *reinterpret_cast<uint32_t *>(hs + (row + 8) * 128 + col) = pack_bf16x2(v.z, v.w);
+    }
+    __syncthreads();
+    const int head = tile;  // slice = head of the qkv output
+    const int32_t *slot_s = reinterpret_cast<const int32_t *>(smem + p.side_off);
+    const float *cs_s = reinterpret_cast<const float *>(smem + p.side_off + 64 * 4);
+    const __nv_bfloat16 *w_s = reinterpret_cast<const __nv_bfloat16 *>(smem + p.side_off + 64 * 4 + 16 * MT * 128 * 4);
+    const int nrows = p.M > rank ? (p.M - rank + S - 1) / S : 0;
+    const int j8 = lane & 7;
+    const unsigned gmask = 0xffu << (lane & 24);
+    for (int u = threadIdx.x >> 3; u < nrows; u += kStreamThreads / 8) {
+      const int m = rank + S * u;
+      const uint4 xa = *reinterpret_cast<const uint4 *>(hs + m * 128 + 8 * j8);
+      const uint4 xb = *reinterpret_cast<const uint4 *>(hs + m * 128 + 64 + 8 * j8);
+      const bool isq = head < p.hq, isv = head >= p.hq + p.hkv;
+      const int32_t slot = slot_s[m];
+      if (isv) {
+        if (slot >= 0) {
+          __nv_bfloat16 *o = p.v_cache + (static_cast<int64_t>(slot) * p.hkv + (head - p.hq - p.hkv)) * 128;
+          *reinterpret_cast<uint4 *>(o + 8 * j8) = xa;
+          *reinterpret_cast<uint4 *>(o + 64 + 8 * j8) = xb;
+        }
+        continue;
+      }
+      if (!isq && slot < 0) continue;  // a k head with nowhere to go
+      uint4 ya, yb;
+      head128_norm_rope(xa, xb, w_s, cs_s + m * 128, j8, p.eps, gmask, ya, yb);
+      __nv_bfloat16 *o = isq ? p.q_out + (static_cast<int64_t>(m) * p.hq + head) * 128
+                             : p.k_cache + (static_cast<int64_t>(slot) * p.hkv + (head - p.hq)) * 128;
+      *reinterpret_cast<uint4 *>(o + 8 * j8) = ya;
+      *reinterpret_cast<uint4 *>(o + 64 + 8 * j8) = yb;
+    }
+    return;
+  }
+
   const int tiles_done = p.swiglu ? MT * (NT / 2) : MT * NT;
   if (p.ar_world <= 1) {
     for (int e = threadIdx.x; e < tiles_done * 32; e += kStreamThreads) {
       const int ln = e & 31, t = e >> 5;
       const int mt = p.swiglu ? t / (NT / 2) : t / NT, nt = p.swiglu ? t % (NT / 2) : t % NT;
       const int j = (mt * NT + nt) * 32 + ln;
-      if (j % S != rank) continue;
+      if (owner(j) != rank) continue;
       const int row = mt * 16 + (ln >> 2), col = nt * 8 + 2 * (ln & 3);
       const float4 v = group_sum(j);
       if (!p.swiglu) {
@@ -1478,7 +1608,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
   for (int e = threadIdx.x; e < tiles_done * 32; e += kStreamThreads) {
     const int ln = e & 31, t = e >> 5, mt = t / NT, nt = t % NT;
     const int j = (mt * NT + nt) * 32 + ln;
-    if (j % S != rank) continue;
+    if (owner(j) != rank) continue;
     const int row = mt * 16 + (ln >> 2), n = n0 + nt * 8 + 2 * (ln & 3);
     if (n >= p.N) continue;
     const float4 v = group_sum(j);
@@ -1500,7 +1630,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
   for (int e = threadIdx.x; e < tiles_done * 32; e += kStreamThreads) {
     const int ln = e & 31, t = e >> 5, mt = t / NT, nt = t % NT;
     const int j = (mt * NT + nt) * 32 + ln;
-    if (j % S != rank) continue;
+    if (owner(j) != rank) continue;
     const int row = mt * 16 + (ln >> 2), n = n0 + nt * 8 + 2 * (ln & 3);
     if (n >= p.N) continue;
     const float4 mine = group_sum(j);
@@ -1545,20 +1675,20 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
 #define NVB200_MM_STREAM_PDL 1
 #endif
 
-template <int MT, int NT> int launch_stream_mt_nt(const CUtensorMap &map_a, const CUtensorMap &map_w,
-                                                  const StreamParams &p, int grid, int smem, bool early_weights,
-                                                  cudaStream_t stream) {
+template <int MT, int NT, int WN = 1>
+int launch_stream_mt_nt(const CUtensorMap &map_a, const CUtensorMap &map_w, const StreamParams &p, int grid, int smem,
+                        bool early_weights, cudaStream_t stream) {
   static int configured[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 64 && configured[dev] < smem) {
-    if (cudaFuncSetAttribute(matmul_stream_kernel<MT, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
-        cudaSuccess)
+  if (dev >= 64 || configured[dev] < smem) {
+    if (cudaFuncSetAttribute(matmul_stream_kernel<MT, NT, WN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             smem) != cudaSuccess)
       return NVB200_ERR_CUDA;
-    configured[dev] = smem;
+    if (dev < 64) configured[dev] = smem;
   }
   static int carve[64];
-  prefer_carveout_once(matmul_stream_kernel<MT, NT>, carve);
+  prefer_carveout_once(matmul_stream_kernel<MT, NT, WN>, carve);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kStreamThreads);
@@ -1578,8 +1708,9 @@ template <int MT, int NT> int launch_stream_mt_nt(const CUtensorMap &map_a, cons
   }
   cfg.attrs = attr;
   cfg.numAttrs = n;
-  return cudaLaunchKernelEx(&cfg, matmul_stream_kernel<MT, NT>, map_a, map_w, p) == cudaSuccess ? NVB200_OK
-                                                                                              : NVB200_ERR_CUDA;
+  return cudaLaunchKernelEx(&cfg, matmul_stream_kernel<MT, NT, WN>, map_a, map_w, p) == cudaSuccess
+             ? NVB200_OK
+             : NVB200_ERR_CUDA;
 }
 
 template <int MT> int launch_stream_mt(int nt, const CUtensorMap &map_a, const CUtensorMap &map_w,
@@ -1915,6 +2046,67 @@ int linear_decode_launch(void *y, const void *x, const void *w, int64_t M, int64
                          int64_t sw, int64_t sy, bool swiglu, int32_t *status, cudaStream_t stream) {
   if (!aligned16(x) || !aligned16(w)) return NVB200_ERR_UNSUPPORTED;
   return launch_stream(y, x, w, M, N, K, sx, sw, sy, 1, swiglu, true, status, stream);
+}
+
+// The decode qkv projection with the fused q/k op as its epilogue (StreamParams::epi = 1): slices of one 128-column
+// head (NT = 16, the consumer warps split into two 64-column parts), K split over a cluster so that the grid covers
+// about the SMs, weight loads overlapping the preceding kernel. M <= 32 rows, head_dim 128, x and W K-major with
+// 16-byte row pitches, no k_out; NVB200_ERR_UNSUPPORTED otherwise.
+int linear_qkv_launch(const void *x, int64_t sx, const void *w, int64_t sw, int64_t K,
+                      const nvb200_qk_norm_rope_kv_args &a, cudaStream_t stream) {
+  const int64_t M = a.num_tokens;
+  if (!NVB200_MM_STREAM || M < 1 || M > 32 || a.head_dim != 128 || a.k_out != nullptr || K <= 0 ||
+      K > 0x3fffffffLL || (sx * 2) % 16 != 0 || (sw * 2) % 16 != 0 || !aligned16(x) || !aligned16(w) ||
+      !aligned16(a.q_out) || a.cos_sin_stride % 4 != 0 || !aligned16(a.cos_sin) ||
+      reinterpret_cast<uintptr_t>(a.q_weight) % 16 != 0 || reinterpret_cast<uintptr_t>(a.k_weight) % 16 != 0)
+    return NVB200_ERR_UNSUPPORTED;
+  if (a.k_cache != nullptr && (!aligned16(a.k_cache) || !aligned16(a.v_cache))) return NVB200_ERR_UNSUPPORTED;
+  const int MT = M <= 16 ? 1 : 2;
+  constexpr int NT = 16, WN = 2;
+  const int heads = a.num_q_heads + 2 * a.num_kv_heads;
+  const int64_t chunks = (K + kStreamKc - 1) / kStreamKc;
+  const int sms = sm_count();
+  int split = 1;
+  while (split < 8 && split * 2 <= chunks && static_cast<int64_t>(heads) * split * 2 <= sms) split *= 2;
+#ifdef NVB200_QKV_SPLIT
+  split = std::min<int64_t>(NVB200_QKV_SPLIT, chunks);
+#endif
+  StreamParams p{};
+  p.M = static_cast<int>(M), p.N = heads * 128, p.K = static_cast<int>(K);
+  p.chunks = static_cast<int>(chunks);
+  p.split = split;
+  p.a_bytes = 2u * (16u * MT) * 128u;
+  p.w_bytes = 2u * (8u * NT) * 128u;
+  const uint32_t stage_bytes = p.a_bytes + p.w_bytes;
+  const int cpc = (p.chunks + split - 1) / split;
+  p.stages = std::max(1, std::min({kStreamMaxStages, cpc, static_cast<int>(kStreamRingBytes / stage_bytes)}));
+  const uint32_t groups = 32u * MT * NT;
+  const uint32_t red_bytes = (kStreamConsumers / WN) * groups * 16u;
+  p.slot_off = (std::max(p.stages * stage_bytes, red_bytes) + 255u) / 256u * 256u;
+  p.head_off = p.slot_off + (split > 1 ? groups * 16u : 0u);
+  p.side_off = p.head_off + 16u * MT * 128u * 2u;
+  p.hdr_off = p.side_off + 64u * 4u + 16u * MT * 128u * 4u + 128u * 2u;
+  p.status = a.status;
+  p.ar_world = 1;
+  p.epi = 1;
+  p.q_out = static_cast<__nv_bfloat16 *>(a.q_out);
+  p.k_cache = static_cast<__nv_bfloat16 *>(a.k_cache);
+  p.v_cache = static_cast<__nv_bfloat16 *>(a.v_cache);
+  p.positions = a.positions;
+  p.slots = a.slot_mapping;
+  p.cos_sin = a.cos_sin;
+  p.cs_stride = a.cos_sin_stride, p.num_positions = a.num_positions, p.num_slots = a.num_slots;
+  p.q_w = static_cast<const __nv_bfloat16 *>(a.q_weight);
+  p.k_w = static_cast<const __nv_bfloat16 *>(a.k_weight);
+  p.hq = a.num_q_heads, p.hkv = a.num_kv_heads;
+  p.eps = a.eps;
+  const int smem = static_cast<int>(1024 + p.hdr_off + 2 * 8 * kStreamMaxStages);
+  CUtensorMap map_a, map_w;
+  if (!make_map(&map_a, x, false, K, M, sx, 64, 16 * MT) || !make_map(&map_w, w, false, K, p.N, sw, 64, 8 * NT))
+    return NVB200_ERR_UNSUPPORTED;
+  const int grid = heads * split;
+  return MT == 1 ? launch_stream_mt_nt<1, NT, WN>(map_a, map_w, p, grid, smem, true, stream)
+                 : launch_stream_mt_nt<2, NT, WN>(map_a, map_w, p, grid, smem, true, stream);
 }
 
 int64_t allreduce_buffer_bytes(int64_t max_n) {

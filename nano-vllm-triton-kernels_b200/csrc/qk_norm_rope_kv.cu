@@ -23,6 +23,7 @@
 #include <algorithm>
 
 #include "common.cuh"
+#include "qknr_math.cuh"
 
 namespace nvb200 {
 namespace {
@@ -94,33 +95,6 @@ struct QknrParams {
   float eps;
   int32_t *status;
 };
-
-// ---------------------------------------------------------------------------------------------------------------
-// Per-head math of the bulk kernel. x1/x2: the 8 + 8 elements this lane holds of the two halves (fp32 values of
-// bf16 inputs). rstd: 1/rms of the head. w1/w2: the matching weights as bf16x2 words. c/s: cos/sin of the lane's
-// 8 RoPE pairs. y1/y2: the rotated outputs in fp32 (rounded to bf16 by the caller's pack).
-
-NVB200_DEVICE void norm_rope8(const float (&x1)[8], const float (&x2)[8], float rstd, const uint32_t (&w1)[4],
-                              const uint32_t (&w2)[4], const float (&c)[8], const float (&s)[8], float (&y1)[8],
-                              float (&y2)[8]) {
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    // torch: x.mul_(rsqrt(var + eps)) in fp32, .to(bf16), .mul_(weight) in bf16 (exact product, one rounding).
-    const uint32_t n1 = bf16x2_mul(pack_bf16x2(__fmul_rn(x1[2 * i], rstd), __fmul_rn(x1[2 * i + 1], rstd)), w1[i]);
-    const uint32_t n2 = bf16x2_mul(pack_bf16x2(__fmul_rn(x2[2 * i], rstd), __fmul_rn(x2[2 * i + 1], rstd)), w2[i]);
-    const float a0 = bf16_lo(n1), a1 = bf16_hi(n1), b0 = bf16_lo(n2), b1 = bf16_hi(n2);
-    // apply_rotary_emb: y1 = x1*cos - x2*sin, y2 = x2*cos + x1*sin, each product rounded separately.
-    y1[2 * i] = __fsub_rn(__fmul_rn(a0, c[2 * i]), __fmul_rn(b0, s[2 * i]));
-    y1[2 * i + 1] = __fsub_rn(__fmul_rn(a1, c[2 * i + 1]), __fmul_rn(b1, s[2 * i + 1]));
-    y2[2 * i] = __fadd_rn(__fmul_rn(b0, c[2 * i]), __fmul_rn(a0, s[2 * i]));
-    y2[2 * i + 1] = __fadd_rn(__fmul_rn(b1, c[2 * i + 1]), __fmul_rn(a1, s[2 * i + 1]));
-  }
-}
-
-NVB200_DEVICE void load_w8(const __nv_bfloat16 *p, uint32_t (&w)[4]) {
-  const uint4 v = __ldg(reinterpret_cast<const uint4 *>(p));
-  w[0] = v.x, w[1] = v.y, w[2] = v.z, w[3] = v.w;
-}
 
 // Token of work unit `unit` and the head group `s` it covers; splits == 1 (large batches) needs no division, and
 // otherwise the units fit 31 bits (checked on the host), so the division is a cheap 32-bit one.

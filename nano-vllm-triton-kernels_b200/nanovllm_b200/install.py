@@ -29,6 +29,9 @@ The reference selects its kernels with the module-global string `nanovllm.kernel
    through nanovllm_b200.kernels.matmul.linear_decode instead of F.linear (cuBLAS): a weight-streaming kernel whose
    weight loads start while the preceding kernel finishes. The thresholds of both steps are the measured
    crossovers against cuBLAS (nanovllm_b200/kernels/matmul.py).
+9. makes the decode steps of Qwen3Attention (nanovllm/models/qwen3.py:77-84) run the qkv projection with the fused
+   q/k op as its epilogue (nanovllm_b200.kernels.qk_norm_rope_kv.linear_qkv_norm_rope_kv: one kernel, the qkv
+   intermediate never written) and then the decode attention (step 6), for the batches that kernel takes.
 
 Call it once, before constructing `LLM(..., kernel_backend="b200")`.
 """
@@ -136,7 +139,34 @@ def install() -> None:
         finally:
             _attention_init_depth -= 1
             kernels_mod.backend = BACKEND
+        self._b200_qkv = self.fused_norm_rope
     qwen3_mod.Qwen3Attention.__init__ = __init__
+
+    # 9. Decode steps of a b200 Qwen3Attention: the qkv projection with the fused q/k op as its epilogue (one kernel,
+    # nvb200_linear_qkv_norm_rope_kv), then the decode attention on the cache it wrote; other calls (prefill, more
+    # rows than the kernel takes) run the forward above.
+    attn_forward = qwen3_mod.Qwen3Attention.forward
+    import nanovllm.utils.context as context_mod
+
+    @functools.wraps(attn_forward)
+    def qwen3_attention_forward(self, positions, hidden_states):
+        ctx = context_mod.get_context()
+        if (getattr(self, "_b200_qkv", False) and not ctx.is_prefill and hidden_states.dim() == 2
+                and getattr(self.qkv_proj, "bias", None) is None and self.attn.k_cache.numel() > 0):
+            attn = self.attn
+            q_norm, k_norm, rotary = attn.norm_rope
+            q = b200_fused.linear_qkv_norm_rope_kv(
+                hidden_states, self.qkv_proj.weight, self.num_heads, self.num_kv_heads, positions, q_norm.weight,
+                k_norm.weight, q_norm.eps, rotary.cos_sin_cache, attn.k_cache, attn.v_cache, ctx.slot_mapping)
+            if q is not None:
+                num_seqs = ctx.context_lens.size(0)
+                o = attention_mod.flash_attn_with_kvcache(
+                    q.reshape(num_seqs, -1, attn.num_heads, attn.head_dim), attn.k_cache, attn.v_cache,
+                    cache_seqlens=ctx.context_lens, block_table=ctx.block_tables, softmax_scale=attn.scale,
+                    causal=True)
+                return self.post_attn(o.view(-1, attn.num_heads, attn.head_dim))
+        return attn_forward(self, positions, hidden_states)
+    qwen3_mod.Qwen3Attention.forward = qwen3_attention_forward
 
     # 4. Spawned tensor-parallel workers register the backend before building their ModelRunner.
     engine_mod.ModelRunner = _model_runner

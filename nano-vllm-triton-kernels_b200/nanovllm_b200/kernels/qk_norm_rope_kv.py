@@ -104,3 +104,56 @@ def kernel_plan(q, k, v, positions, q_weight, k_weight, eps, cos_sin_cache, k_ca
     _lib.check(_lib.lib().nvb200_qk_norm_rope_kv_plan(ctypes.byref(a), ctypes.byref(kernel), ctypes.byref(tpu)),
                "qk_norm_rope_kv_plan")
     return _lib.QKNR_KERNELS[kernel.value], tpu.value
+
+
+def linear_qkv_norm_rope_kv(x: torch.Tensor, qkv_weight: torch.Tensor, num_q_heads: int, num_kv_heads: int,
+                            positions: torch.Tensor, q_weight: torch.Tensor, k_weight: torch.Tensor, eps: float,
+                            cos_sin_cache: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                            slot_mapping: torch.Tensor | None) -> torch.Tensor | None:
+    """The decode qkv projection with this op as its epilogue (`nvb200_linear_qkv_norm_rope_kv`): the same result as
+    qkv = x @ qkv_weight.t() (bf16) followed by qk_norm_rope_kv(q, k, v, ..., write_k=False) on its q | k | v parts,
+    without writing qkv. qkv_weight: [(Hq + 2 Hkv) * 128, K] in nn.Linear layout, a model parameter (its loads may
+    start while the preceding kernel finishes). Returns q_out [M, Hq, 128], or None when the kernel does not take the
+    call (more than 32 rows, head_dim != 128, layouts), in which case the caller runs the two steps."""
+    M, K = x.shape
+    D = 128
+    _require(x.dtype == qkv_weight.dtype == torch.bfloat16 and qkv_weight.shape == ((num_q_heads + 2 * num_kv_heads) * D, K),
+             "x and qkv_weight must be bf16, qkv_weight [(Hq + 2 Hkv) * 128, K]")
+    if (q_weight.shape != (D,) or x.stride(1) != 1 or qkv_weight.stride(1) != 1 or M > 32
+            or num_q_heads % num_kv_heads or cos_sin_cache.shape[-1] != D):
+        return None
+    _require(positions.shape == (M,) and positions.dtype == torch.int64, "positions must be int64 [M]")
+    _require(cos_sin_cache.dtype == torch.float32 and cos_sin_cache.stride(-1) == 1
+             and cos_sin_cache.numel() == cos_sin_cache.shape[0] * D, "cos_sin_cache must be fp32 [max_pos, (1,) 128]")
+    _require(q_weight.dtype == k_weight.dtype == torch.bfloat16 and k_weight.shape == (D,)
+             and q_weight.is_contiguous() and k_weight.is_contiguous(), "q/k weights must be contiguous bf16 [128]")
+    store = k_cache.numel() > 0
+    if store:
+        _require(k_cache.is_contiguous() and v_cache.is_contiguous() and k_cache.shape[-2:] == (num_kv_heads, D)
+                 and v_cache.shape == k_cache.shape and k_cache.dtype == v_cache.dtype == torch.bfloat16,
+                 "k_cache, v_cache must be contiguous bf16 [..., Hkv, 128]")
+        _require(slot_mapping is not None and slot_mapping.shape == (M,) and slot_mapping.dtype == torch.int32,
+                 "slot_mapping must be int32 [M]")
+    q_out = torch.empty(M, num_q_heads, D, dtype=x.dtype, device=x.device)
+    if M == 0:
+        return q_out
+    a = _lib.LinearQkvArgs()
+    a.x, a.x_row_stride = x.data_ptr(), x.stride(0)
+    a.qkv_weight, a.weight_row_stride, a.K = qkv_weight.data_ptr(), qkv_weight.stride(0), K
+    g = a.qknr
+    g.q_out, g.k_out = q_out.data_ptr(), None
+    g.positions = positions.data_ptr()
+    g.slot_mapping = slot_mapping.data_ptr() if store else None
+    g.q_weight, g.k_weight = q_weight.data_ptr(), k_weight.data_ptr()
+    g.cos_sin, g.cos_sin_stride, g.num_positions = (cos_sin_cache.data_ptr(), cos_sin_cache.stride(0),
+                                                    cos_sin_cache.shape[0])
+    if store:
+        g.k_cache, g.v_cache, g.num_slots = k_cache.data_ptr(), v_cache.data_ptr(), k_cache.numel() // (num_kv_heads * D)
+    g.num_tokens, g.num_q_heads, g.num_kv_heads, g.head_dim = M, num_q_heads, num_kv_heads, D
+    g.eps = eps
+    g.status = _lib.status_word(x.device).data_ptr()
+    rc = _lib.lib().nvb200_linear_qkv_norm_rope_kv(ctypes.byref(a), _lib.stream_of(x))
+    if rc == _lib.ERR_UNSUPPORTED:
+        return None
+    _lib.check(rc, "linear_qkv_norm_rope_kv")
+    return q_out

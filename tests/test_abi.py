@@ -49,7 +49,8 @@ def test_no_gpu_means_error_not_crash():
 @pytest.mark.skipif(shutil.which("gcc") is None, reason="gcc not available")
 @pytest.mark.parametrize("ctype,cname", [(_lib.QkNormRopeKvArgs, "nvb200_qk_norm_rope_kv_args"),
                                          (_lib.PagedDecodeArgs, "nvb200_paged_decode_args"),
-                                         (_lib.AllreduceGroup, "nvb200_allreduce_group")])
+                                         (_lib.AllreduceGroup, "nvb200_allreduce_group"),
+                                         (_lib.LinearQkvArgs, "nvb200_linear_qkv_args")])
 def test_struct_layout_matches_header(tmp_path, ctype, cname):
     fields = [f[0] for f in ctype._fields_]
     src = tmp_path / "layout.c"
@@ -93,6 +94,16 @@ def test_new_entry_points_reject_bad_arguments_without_a_gpu():
     assert lib.nvb200_linear_decode(8, 8, 8, 1, 16, 16, 16, 16, 16, 2, None, None) == _lib.ERR_ARG
     assert lib.nvb200_linear_decode(None, 8, 8, 1, 16, 16, 16, 16, 16, 0, None, None) == _lib.ERR_ARG
     assert lib.nvb200_linear_decode(None, None, None, 0, 16, 16, 16, 16, 16, 0, None, None) == _lib.OK
+    # linear_qkv_norm_rope_kv: a null args pointer, Hq not a multiple of Hkv, a cache without slots; no tokens.
+    assert lib.nvb200_linear_qkv_norm_rope_kv(None, None) == _lib.ERR_ARG
+    la = _lib.LinearQkvArgs()
+    la.K, la.qknr.num_tokens, la.qknr.num_q_heads, la.qknr.num_kv_heads, la.qknr.head_dim = 1024, 4, 12, 8, 128
+    la.qknr.num_positions = 4096
+    assert lib.nvb200_linear_qkv_norm_rope_kv(ctypes.byref(la), None) == _lib.ERR_ARG
+    la.qknr.num_q_heads, la.qknr.k_cache = 16, 8
+    assert lib.nvb200_linear_qkv_norm_rope_kv(ctypes.byref(la), None) == _lib.ERR_ARG
+    la.qknr.k_cache, la.qknr.num_tokens = None, 0
+    assert lib.nvb200_linear_qkv_norm_rope_kv(ctypes.byref(la), None) == _lib.OK
 
 
 def test_streamk_entry_points_check_arguments_without_a_gpu():

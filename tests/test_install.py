@@ -119,6 +119,7 @@ def test_projections_of_a_b200_model_take_the_b200_routes(ref):
                 a = Qwen3Attention(1024, 16, 8, max_position=4096, head_dim=128, rope_theta=1e6)
                 m = Qwen3MLP(1024, 3072, "silu")
             assert getattr(a.qkv_proj, "_b200_matmul", False) is expected
+            assert getattr(a, "_b200_qkv", False) is expected  # step 9: qkv projection + fused q/k epilogue
             assert getattr(a.o_proj, "_b200_matmul", False) is expected
             assert getattr(m.down_proj, "_b200_matmul", False) is expected
             assert getattr(m, "_b200_fused", False) is expected

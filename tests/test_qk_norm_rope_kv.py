@@ -381,3 +381,52 @@ def test_rank_qkv_layout_multi_token_kernel(cuda, world, tokens, store, write_k)
     else:
         assert torch.equal(cache, x["cache"])
     assert _lib.status(cuda) == 0
+
+
+# The decode qkv projection with this op as its epilogue (nvb200_linear_qkv_norm_rope_kv): against qkv = the fp64
+# product rounded to bf16, then this op. The projection accumulates in fp32, so a few qkv elements round one bf16
+# step away from the fp64 product's rounding, and the norm and rotation carry that on: within the bf16 tolerance, and
+# bitwise on almost every element; cache rows outside the batch's slots (and slot -1 rows) untouched.
+LINEAR_QKV = [(hq, hkv, M, K) for (hq, hkv) in SHAPES.values() for M, K in ((1, 1024), (7, 1024), (32, 1024))] + \
+             [(32, 8, 32, 4096), (16, 8, 16, 2048), (4, 2, 32, 4096)]
+
+
+@pytest.mark.parametrize("hq,hkv,M,K", LINEAR_QKV)
+def test_linear_qkv_epilogue(cuda, hq, hkv, M, K):
+    from nanovllm_b200.kernels.qk_norm_rope_kv import linear_qkv_norm_rope_kv
+    x = make_inputs(cuda, M, True, hq=hq, hkv=hkv, seed_extra=K)
+    g = torch.Generator(device=cuda).manual_seed(M * 31 + K + hq)
+    a = (torch.randn(M, K, device=cuda, generator=g) / K ** 0.5).to(torch.bfloat16)
+    w = torch.randn((hq + 2 * hkv) * D, K, device=cuda, generator=g).to(torch.bfloat16)
+    qkv = om.matmul(a, w.t()).to(torch.bfloat16)
+    q, k, v = qkv.split([hq * D, hkv * D, hkv * D], dim=-1)
+    cache_ref = x["cache"].clone()
+    q_ref, _ = qk_norm_rope_kv(q.reshape(M, hq, D), k.reshape(M, hkv, D), v.reshape(M, hkv, D), x["positions"],
+                               x["q_w"], x["k_w"], EPS, table(cuda), cache_ref[0], cache_ref[1], x["slots"],
+                               write_k=False)
+    cache = x["cache"].clone()
+    _lib.status(cuda, clear=True)
+    q_out = linear_qkv_norm_rope_kv(a, w, hq, hkv, x["positions"], x["q_w"], x["k_w"], EPS, table(cuda), cache[0],
+                                    cache[1], x["slots"])
+    assert q_out is not None and q_out.shape == (M, hq, D)
+    assert _lib.status(cuda, clear=True) == 0
+    for got, ref in ((q_out, q_ref), (cache[0], cache_ref[0]), (cache[1], cache_ref[1])):
+        torch.testing.assert_close(cpu(got).float(), cpu(ref).float(), rtol=1.6e-2, atol=1e-2)
+        assert (om.bf16_ulp_diff(cpu(got), cpu(ref)) == 0).float().mean() > 0.97
+    # rows of the cache that no kept slot names are exactly as they were
+    kept = x["slots"][x["slots"] >= 0].long()
+    untouched = torch.ones(cache[0].numel() // (hkv * D), dtype=torch.bool, device=cuda)
+    untouched[kept] = False
+    for c, before in ((cache[0], x["cache"][0]), (cache[1], x["cache"][1])):
+        assert torch.equal(c.view(-1, hkv, D)[untouched], before.view(-1, hkv, D)[untouched])
+
+
+def test_linear_qkv_declines_what_it_does_not_take(cuda):
+    from nanovllm_b200.kernels.qk_norm_rope_kv import linear_qkv_norm_rope_kv
+    x = make_inputs(cuda, 33, True)
+    a = torch.randn(33, 1024, device=cuda).to(torch.bfloat16)
+    w = torch.randn(32 * D, 1024, device=cuda).to(torch.bfloat16)
+    cache = x["cache"].clone()
+    assert linear_qkv_norm_rope_kv(a, w, 16, 8, x["positions"], x["q_w"], x["k_w"], EPS, table(cuda), cache[0],
+                                   cache[1], x["slots"]) is None  # more than 32 rows
+    assert torch.equal(cache, x["cache"])
