@@ -1222,10 +1222,13 @@ __global__ void __launch_bounds__(kSkinnyThreads)
 //     (griddepcontrol.launch_dependents, as this library's norm, SiLU x Mul and decode-attention kernels do), the
 //     weight stream overlaps it;
 //   * TMA moves 128-element K chunks (two 64-element boxes per operand, 128-byte swizzle) through a ring; 8 consumer
-//     warps each take one 16-element k-step of every chunk on warp-level bf16 MMAs (the slice is 8-64 rows wide, below
-//     the 64/128-row tiles of tcgen05.mma) and one pass through shared memory sums the 8 warps' shares.
-// The gate_up form takes NS / 2 gate rows and the matching NS / 2 up rows and finishes with the SiLU x Mul routine of
-// the two-step form.
+//     warps each take one 16-element k-step of every chunk on warp-level bf16 MMAs (the slice is 32-128 rows wide,
+//     below the 64/128-row tiles of tcgen05.mma at 1-32 activation rows) and one pass through shared memory sums the
+//     warps' shares.
+// Epilogues: bf16 stores; the gate_up form (NS / 2 gate rows and the matching NS / 2 up rows, finished with the SiLU x
+// Mul routine of the two-step form); the row-parallel form (the sums exchanged with the other GPUs over NVLink, as
+// the skinny kernel's all-reduce does); the qkv form (each slice one head, finished with the fused q/k op's per-head
+// math and stored to q_out and the KV cache).
 
 constexpr int kStreamKc = 128;  // K elements per stage: two 64-element (128-byte) TMA boxes per operand
 constexpr int kStreamConsumers = 8;
@@ -1265,8 +1268,8 @@ struct StreamParams {
   int hq, hkv;
   float eps;
   uint32_t head_off;  // shared-memory offset of the [16 MT][128] bf16 staging tile of the slice's rows
-  uint32_t side_off;  // shared-memory offset of the epilogue's inputs: [16 MT] slots, [16 MT][128] fp32 cos | sin
-                      // rows, the 128 bf16 norm weights of the slice's head
+  uint32_t side_off;  // shared-memory offset of the epilogue's inputs: 32 slots and 32 positions (int32), the rows'
+                      // cos | sin ([16 MT][128] fp32), the 128 bf16 norm weights of the slice's head
 };
 
 // Address of the 16-byte chunk `ch` (0..7) of row `row` in a 128-byte-swizzled TMA tile at `tile` (rows of 128 bytes;
@@ -1281,12 +1284,6 @@ NVB200_DEVICE void cp_async16(uint32_t dst, const void *src) {
 }
 NVB200_DEVICE void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 NVB200_DEVICE void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
-
-NVB200_DEVICE float ld_cluster_f32(uint32_t addr) {
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
-  return v;
-}
 
 // WN: the consumer warps split the slice's NT tiles into WN parts; warp w takes the WN k-steps w mod KW, + KW, ...
 // (KW = 8 / WN) of every chunk for the NT / WN tiles of part w / KW (WN = 1: one k-step, every tile).
