@@ -2063,8 +2063,10 @@ int linear_qkv_launch(const void *x, int64_t sx, const void *w, int64_t sw, int6
   const int heads = a.num_q_heads + 2 * a.num_kv_heads;
   const int64_t chunks = (K + kStreamKc - 1) / kStreamKc;
   const int sms = sm_count();
+  // K split: the largest power of two up to 4 that keeps heads x split within the SMs (clusters of 8 CTAs measured
+  // slower than 4 in every sweep of the weight-streaming kernel).
   int split = 1;
-  while (split < 8 && split * 2 <= chunks && static_cast<int64_t>(heads) * split * 2 <= sms) split *= 2;
+  while (split < 4 && split * 2 <= chunks && static_cast<int64_t>(heads) * split * 2 <= sms) split *= 2;
 #ifdef NVB200_QKV_SPLIT
   split = std::min<int64_t>(NVB200_QKV_SPLIT, chunks);
 #endif

@@ -29,9 +29,11 @@ The reference selects its kernels with the module-global string `nanovllm.kernel
    through nanovllm_b200.kernels.matmul.linear_decode instead of F.linear (cuBLAS): a weight-streaming kernel whose
    weight loads start while the preceding kernel finishes. The thresholds of both steps are the measured
    crossovers against cuBLAS (nanovllm_b200/kernels/matmul.py).
-9. makes the decode steps of Qwen3Attention (nanovllm/models/qwen3.py:77-84) run the qkv projection with the fused
-   q/k op as its epilogue (nanovllm_b200.kernels.qk_norm_rope_kv.linear_qkv_norm_rope_kv: one kernel, the qkv
-   intermediate never written) and then the decode attention (step 6), for the batches that kernel takes.
+9. makes the decode steps of Qwen3Attention (nanovllm/models/qwen3.py:77-84) on one GPU run the qkv projection with
+   the fused q/k op as its epilogue (nanovllm_b200.kernels.qk_norm_rope_kv.linear_qkv_norm_rope_kv: one kernel, the
+   qkv intermediate never written) and then the decode attention (step 6), for the batches that kernel takes. (Under
+   tensor parallelism each rank's few heads leave the kernel with too little work per CTA: the TP 2 step measured
+   slower with it, 1628 us against 1469 us without it on another box.)
 
 Call it once, before constructing `LLM(..., kernel_backend="b200")`.
 """
@@ -152,7 +154,8 @@ def install() -> None:
     def qwen3_attention_forward(self, positions, hidden_states):
         ctx = context_mod.get_context()
         if (getattr(self, "_b200_qkv", False) and not ctx.is_prefill and hidden_states.dim() == 2
-                and getattr(self.qkv_proj, "bias", None) is None and self.attn.k_cache.numel() > 0):
+                and self.qkv_proj.tp_size == 1 and getattr(self.qkv_proj, "bias", None) is None
+                and self.attn.k_cache.numel() > 0):
             attn = self.attn
             q_norm, k_norm, rotary = attn.norm_rope
             q = b200_fused.linear_qkv_norm_rope_kv(
