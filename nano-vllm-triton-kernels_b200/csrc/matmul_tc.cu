@@ -2119,9 +2119,13 @@ int matmul_allreduce_launch(void *c, const void *a, const void *b, int64_t M, in
   if (sak != 1 || sbk != 1 || (sam * 2) % 16 != 0 || (sbn * 2) % 16 != 0 || !aligned16(a) || !aligned16(b))
     return NVB200_ERR_UNSUPPORTED;
   // The weight-streaming kernel with the all-reduce epilogue (plain stream order: B is not promised to be a weight
-  // that no kernel in flight writes), else the skinny kernel's.
-  const int rc = launch_stream(c, a, b, M, N, K, sam, sbn, scm, 1, false, false, status, stream, g);
-  if (rc != NVB200_ERR_UNSUPPORTED) return rc;
+  // that no kernel in flight writes) for shards of at most 16 MB of B, else the skinny kernel's. Measured on two
+  // B200s: the Qwen3-0.6B decode step at TP 2 (o_proj / down_proj shards of 2-3 MB) 1608 -> 1469 us with the former;
+  // the Qwen3-8B down_proj shard (50 MB, bench.py --workload rowpar) 26.5 us with the skinny kernel, 31.3 with it.
+  if (N * K * 2 <= (16LL << 20)) {
+    const int rc = launch_stream(c, a, b, M, N, K, sam, sbn, scm, 1, false, false, status, stream, g);
+    if (rc != NVB200_ERR_UNSUPPORTED) return rc;
+  }
   return launch_skinny(c, a, b, M, N, K, sam, sbn, scm, 1, false, status, stream, g);
 }
 

@@ -20,8 +20,8 @@ pytestmark = pytest.mark.gpu
 
 WORLD = 2
 # (M, N, K total): decode o_proj / down_proj of Qwen3-0.6B and -8B shards, M = 1 and odd M, ragged K shards. N a
-# multiple of 8 runs the weight-streaming kernel's all-reduce (K split over clusters of 1, 2 and 4 CTAs among these
-# shapes); N = 1004 the skinny kernel's.
+# multiple of 8 with shards of at most 16 MB runs the weight-streaming kernel's all-reduce (K split over clusters of 1,
+# 2 and 4 CTAs among these shapes); N = 1004 and the 8B down_proj shard (50 MB) the skinny kernel's.
 SHAPES = [(32, 1024, 2048), (32, 1024, 6144), (1, 4096, 1024), (7, 1000, 512), (64, 2048, 1024), (32, 4096, 24576),
           (5, 1004, 512)]
 
