@@ -129,7 +129,9 @@ def check_oracle_full_size(ref_root: str) -> None:
 
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("NANOVLLM_REFERENCE", "/root/reference"))
+    # The reference checkout: $NANOVLLM_REFERENCE, else a checkout named `reference` beside this repository.
+    ap.add_argument("--reference",
+                    default=os.environ.get("NANOVLLM_REFERENCE", os.path.join(os.path.dirname(ROOT), "reference")))
     args = ap.parse_args()
     check_oracle_full_size(args.reference)
     data = generate(args.reference)
