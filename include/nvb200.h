@@ -172,6 +172,12 @@ NVB200_API int nvb200_linear_decode(void *y, const void *x, const void *weight, 
                                     int64_t sx, int64_t sw, int64_t sy, int swiglu, int32_t *status,
                                     nvb200_stream_t stream);
 
+/* The launch shape nvb200_linear_decode picks for an M x N x K call on the current device (148 SMs when no GPU
+ * answers), without launching: *tiles = 8-column tiles per CTA (the CTA's weight rows / 8; with swiglu half of them
+ * gate rows), *split = CTAs of a thread-block cluster that split K. NVB200_ERR_UNSUPPORTED for shapes the kernel does
+ * not take. Host-only, for tests and tools. Replaces: nothing in the reference. */
+NVB200_API int nvb200_linear_decode_plan(int64_t M, int64_t N, int64_t K, int swiglu, int32_t *tiles, int32_t *split);
+
 /* The decode qkv projection with the fused q/k op as its epilogue: qkv = x[M, K] @ qkv_weight^T rounded to bf16
  * ([Hq q heads | Hkv k heads | Hkv v heads] of 128 columns, QKVParallelLinear's layout), then exactly what
  * nvb200_qk_norm_rope_kv does with q, k, v = the three parts of qkv: q heads RMSNorm + RoPE into q_out, k heads

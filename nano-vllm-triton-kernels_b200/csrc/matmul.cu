@@ -21,6 +21,7 @@ int matmul_swiglu_launch(void *c, const void *a, const void *b, int64_t M, int64
                          int64_t sak, int64_t sbk, int64_t sbn, int64_t scm, int32_t *status, cudaStream_t stream);
 int linear_decode_launch(void *y, const void *x, const void *w, int64_t M, int64_t N, int64_t K, int64_t sx,
                          int64_t sw, int64_t sy, bool swiglu, int32_t *status, cudaStream_t stream);
+int linear_decode_plan(int64_t M, int64_t N, int64_t K, bool swiglu, int32_t *nt, int32_t *split);
 int linear_qkv_launch(const void *x, int64_t sx, const void *w, int64_t sw, int64_t K,
                       const nvb200_qk_norm_rope_kv_args &a, cudaStream_t stream);
 int64_t allreduce_buffer_bytes(int64_t max_n);
@@ -211,6 +212,12 @@ extern "C" int nvb200_linear_decode(void *y, const void *x, const void *weight, 
   if (int rc = check_device()) return rc;
   return linear_decode_launch(y, x, weight, M, N, K, sx, sw, sy, swiglu != 0, status,
                               reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int nvb200_linear_decode_plan(int64_t M, int64_t N, int64_t K, int swiglu, int32_t *tiles,
+                                         int32_t *split) {
+  if (M < 0 || N < 0 || K < 0 || (swiglu != 0 && swiglu != 1)) return NVB200_ERR_ARG;
+  return linear_decode_plan(M, N, K, swiglu != 0, tiles, split);
 }
 
 extern "C" int nvb200_linear_qkv_norm_rope_kv(const nvb200_linear_qkv_args *args, nvb200_stream_t stream) {

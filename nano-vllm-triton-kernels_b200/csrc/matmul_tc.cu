@@ -2039,6 +2039,15 @@ int matmul_swiglu_launch(void *c, const void *a, const void *b, int64_t M, int64
   return tc_launch(c, a, b, M, N, K, sam, sak, sbk, sbn, scm, 1, NVB200_BF16, true, status, stream);
 }
 
+int linear_decode_plan(int64_t M, int64_t N, int64_t K, bool swiglu, int32_t *nt, int32_t *split) {
+  if (M <= 0 || M > 64 || N <= 0 || K <= 0 || N > 0x3fffffffLL || K > 0x3fffffffLL) return NVB200_ERR_UNSUPPORTED;
+  const StreamPlan plan = stream_plan(M, N, K, swiglu, sm_count());
+  if (plan.nt == 0) return NVB200_ERR_UNSUPPORTED;
+  if (nt) *nt = plan.nt;
+  if (split) *split = plan.split;
+  return NVB200_OK;
+}
+
 int linear_decode_launch(void *y, const void *x, const void *w, int64_t M, int64_t N, int64_t K, int64_t sx,
                          int64_t sw, int64_t sy, bool swiglu, int32_t *status, cudaStream_t stream) {
   if (!aligned16(x) || !aligned16(w)) return NVB200_ERR_UNSUPPORTED;

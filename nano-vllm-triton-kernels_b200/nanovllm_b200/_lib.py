@@ -24,7 +24,7 @@ QKNR_KERNELS = {0: "none", 1: "generic", 2: "direct", 3: "multi", 4: "bulk"}
 EXPORTS = ("nvb200_status_string", "nvb200_qk_norm_rope_kv", "nvb200_qk_norm_rope_kv_plan", "nvb200_rms_norm",
            "nvb200_fused_add_rms_norm",
            "nvb200_silu_and_mul", "nvb200_matmul_workspace_size", "nvb200_matmul", "nvb200_matmul_silu_and_mul",
-           "nvb200_linear_decode", "nvb200_linear_qkv_norm_rope_kv",
+           "nvb200_linear_decode", "nvb200_linear_decode_plan", "nvb200_linear_qkv_norm_rope_kv",
            "nvb200_allreduce_buffer_bytes", "nvb200_allreduce_buffer_create", "nvb200_allreduce_buffer_open",
            "nvb200_allreduce_buffer_close", "nvb200_matmul_allreduce", "nvb200_store_kvcache",
            "nvb200_paged_decode_attention", "nvb200_paged_decode_splits", "nvb200_paged_decode_workspace_size",
@@ -112,6 +112,8 @@ def _declare(lib):
     lib.nvb200_matmul_allreduce.restype = ctypes.c_int
     lib.nvb200_linear_decode.argtypes = [_vp, _vp, _vp] + [_i64] * 6 + [ctypes.c_int, _vp, _vp]
     lib.nvb200_linear_decode.restype = ctypes.c_int
+    lib.nvb200_linear_decode_plan.argtypes = [_i64, _i64, _i64, ctypes.c_int, _vp, _vp]
+    lib.nvb200_linear_decode_plan.restype = ctypes.c_int
     lib.nvb200_linear_qkv_norm_rope_kv.argtypes = [ctypes.POINTER(LinearQkvArgs), _vp]
     lib.nvb200_linear_qkv_norm_rope_kv.restype = ctypes.c_int
     lib.nvb200_store_kvcache.argtypes = [_vp, _i64, _vp, _i64, _vp, _vp, _vp, ctypes.c_int, _i64, _i64, _i64,

@@ -122,3 +122,25 @@ def test_streamk_entry_points_check_arguments_without_a_gpu():
     if not torch.cuda.is_available():
         a.num_q_heads = 16
         assert lib.nvb200_paged_decode_workspace_size(ctypes.byref(a)) == -1
+
+
+# The weight-streaming kernel's launch shape (tiles of 8 weight rows per CTA x CTAs splitting K), as calibrated by a
+# sweep of every pair on B200 (148 SMs; this machine's library answers with 148 when no GPU is present).
+PLANS = [((32, 1024, 2048, 0), (4, 4)),   # Qwen3-0.6B o_proj
+         ((32, 1024, 3072, 0), (4, 4)),   # down_proj
+         ((32, 3072, 1024, 1), (6, 1)),   # gate_up with SiLU x Mul
+         ((32, 4096, 1024, 0), (4, 1)),   # qkv_proj
+         ((32, 4096, 4096, 0), (7, 2)),   # Qwen3-8B o_proj
+         ((32, 4096, 12288, 0), (7, 2)),  # Qwen3-8B down_proj
+         ((1, 1024, 2048, 0), (4, 4)), ((64, 1024, 3072, 0), (4, 4))]
+
+
+@pytest.mark.skipif(__import__("torch").cuda.is_available(), reason="the SM count of this machine's GPU differs")
+@pytest.mark.parametrize("shape,expected", PLANS)
+def test_decode_projection_plan(shape, expected):
+    lib = _lib.lib()
+    tiles, split = ctypes.c_int32(0), ctypes.c_int32(0)
+    assert lib.nvb200_linear_decode_plan(*shape, ctypes.byref(tiles), ctypes.byref(split)) == _lib.OK
+    assert (tiles.value, split.value) == expected
+    assert lib.nvb200_linear_decode_plan(65, 1024, 1024, 0, None, None) == _lib.ERR_UNSUPPORTED
+    assert lib.nvb200_linear_decode_plan(1, 1024, 1024, 2, None, None) == _lib.ERR_ARG
