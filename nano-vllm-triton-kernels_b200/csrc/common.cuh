@@ -326,23 +326,6 @@ int sm_count();
 // Returns NVB200_OK if the current device is sm_100 (B200/GB200), else NVB200_ERR_NO_DEVICE.
 int check_device();
 
-// Shared-memory carveout (percent of the unified L1/shared array) asked for the weight-streaming GEMM (-1: the
-// driver's choice). Measured on B200 at the Qwen3-0.6B decode projections, each after an RMSNorm in a CUDA graph:
-// 0.6-1.3 us less per norm + projection pair with the norm kernels asking for it too, but those then lose L1 (Add +
-// RMSNorm at 8192 x 1024: 14.7 -> 18.7 us), so only the GEMM asks.
-#ifndef NVB200_CARVEOUT
-#define NVB200_CARVEOUT 100
-#endif
-
-// Sets `kernel`'s preferred carveout to NVB200_CARVEOUT once per device; `done` is the call site's own record.
-template <typename Kernel> void prefer_carveout_once(Kernel kernel, int (&done)[64]) {
-  if (NVB200_CARVEOUT < 0) return;
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev >= 64 || done[dev]) return;
-  cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, NVB200_CARVEOUT);
-  done[dev] = 1;
-}
-
 // Programmatic stream serialization for the decode-path kernels that launch through launch_ex, per kernel class: 1
 // lets their CTAs be scheduled while the preceding kernel finishes (when it lets its dependents start early; they
 // wait for it with grid_dependency_wait() before touching memory), 0 keeps plain stream order. Measured on B200, the

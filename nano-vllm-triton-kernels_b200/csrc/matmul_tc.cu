@@ -1684,8 +1684,6 @@ int launch_stream_mt_nt(const CUtensorMap &map_a, const CUtensorMap &map_w, cons
       return NVB200_ERR_CUDA;
     if (dev < 64) configured[dev] = smem;
   }
-  static int carve[64];
-  prefer_carveout_once(matmul_stream_kernel<MT, NT, WN>, carve);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kStreamThreads);
